@@ -1,0 +1,396 @@
+"""Benchmark of the B200 kernel chain (libkvasir_b200) on BASELINE workloads.
+
+Default (the contract line): BASELINE config 5 -- sequence-sharded long-context
+greedy decode of a random-init Llama-3.2-1B (16 layers, bf16): 256 independent
+sequences with a 16384-token KV cache each, split evenly over the ranks (one
+process per GPU; `torchrun --nproc-per-node N bench.py --gpus N`).  A step is
+one decode step (one new token for every sequence) of the whole model: cuBLAS
+projections + the kvb kernels + greedy argmax, replayed as one CUDA graph.
+
+  value     whole-job tokens/s with ids, weights and KV resident in HBM,
+            CUDA-event timed over K steps, max over ranks;
+  e2e       the same through kvb_decoder_step_host (pinned host ids in,
+            H2D, step, D2H, sync) every step;
+  roofline  the dominant kernel, split-KV decode attention (kvb_attention_decode,
+            decode + combine passes), timed alone on the same stream with
+            CUDA events: algorithmic K+V+Q+O bytes per call / mean duration,
+            against the measured HBM copy bandwidth;
+  cpu_baseline  the CPU oracle's decode step (the reference's f64 CPU-reference
+            kernels composed, oracle/) on a bounded sample of sequences,
+            rank 0 at N = 1 only.
+
+`--impl reference` times only that CPU path (the reference arm).
+`--workload cfg1|cfg2|cfg3|cfg4` print per-kernel lines for the other
+BASELINE configs instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode-step tokens/s & attention HBM GB/s (% of peak) at 1/2/4/8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.dev), "-lms", "100"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4)
+                          if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+# ----------------------------------------------------------------------------- dist
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world):
+    if world <= 1:
+        return None
+    import datetime
+    import torch.distributed as dist
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    return dist
+
+
+def max_over_ranks(x: float, dist, torch) -> float:
+    if dist is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist, torch):
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ----------------------------------------------------------------------------- CPU baseline
+class CpuDecodeSample:
+    """The oracle's decode step (the reference's f64 CPU-reference kernels,
+    composed; oracle/) for n_seq sequences at a given context, with weights and
+    KV generated once on the host."""
+
+    def __init__(self, cfg, context: int, max_steps: int, threads: int, n_seq: int = 1):
+        from oracle import oracle as O
+        self.O = O
+        O.set_threads(threads)
+        h, i, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_layers
+        fill = lambda n, s, seed, mean=0.0: O.fill_normal(n, mean, s, seed)
+        self.W = dict(embed=fill(cfg.vocab_size * h, 0.02, 1), final_norm=fill(h, 0.02, 2, 1.0),
+                      attn_norm=[fill(h, 0.02, 10 + l, 1.0) for l in range(L)],
+                      mlp_norm=[fill(h, 0.02, 30 + l, 1.0) for l in range(L)],
+                      w_qkv=[fill(cfg.qkv_dim * h, 0.02, 50 + l) for l in range(L)],
+                      w_o=[fill(h * cfg.q_dim, 0.02, 70 + l) for l in range(L)],
+                      w_gu=[fill(2 * i * h, 0.02, 90 + l) for l in range(L)],
+                      w_down=[fill(h * i, 0.02, 110 + l) for l in range(L)])
+        max_seq = context + max_steps + 1
+        kv = n_seq * L * cfg.num_kv_heads * max_seq * cfg.head_dim
+        self.kc = fill(kv, 1.0, 200)
+        self.vc = fill(kv, 1.0, 201)
+        self.cos, self.sin = O.cos_sin_table(cfg.head_dim, max_seq, **O.LLAMA3_ROPE)
+        self.dims = dict(hidden=h, inter=i, n_layers=L, n_q=cfg.num_heads, n_kv=cfg.num_kv_heads,
+                         head_dim=cfg.head_dim, vocab=cfg.vocab_size, max_seq=max_seq,
+                         eps=cfg.rms_norm_eps)
+        self.ids = np.arange(n_seq, dtype=np.int32) * 7 + 11
+        self.pos = np.full(n_seq, context, np.int32)
+        self.n_seq = n_seq
+        self.steps_left = max_steps
+
+    def step(self) -> float:
+        """One decode step; returns its wall time in seconds."""
+        assert self.steps_left > 0
+        t0 = time.perf_counter()
+        _, self.ids = self.O.decode_step(self.dims, self.W, self.cos, self.sin, self.kc, self.vc,
+                                         self.ids, self.pos)
+        dt = time.perf_counter() - t0
+        self.pos += 1
+        self.steps_left -= 1
+        return dt
+
+
+def cpu_decode_sample(cfg, context: int, min_seconds: float, max_steps: int, threads: int,
+                      n_seq: int = 1):
+    """(tokens/s, steps, seconds) of the CPU oracle decode step, stepping until
+    min_seconds of CPU work or max_steps."""
+    s = CpuDecodeSample(cfg, context, max_steps, threads, n_seq)
+    steps, total = 0, 0.0
+    while steps < max_steps:
+        total += s.step()
+        steps += 1
+        if total >= min_seconds:
+            break
+    s.O.set_threads(1)
+    return n_seq * steps / total, steps, total
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+# ----------------------------------------------------------------------------- main workload
+def run_decode(args):
+    import torch
+    from kvasir_b200 import Gpu
+    from kvasir_b200.config import LlamaConfig
+    from kvasir_b200.decoder import Decoder
+    from kvasir_b200.shard import shard_sequences
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = init_dist(world)
+    peaks, peak_kind = load_peaks()
+    cfg = LlamaConfig.llama_3_2_1b()
+    n_total, ctx = args.seqs, args.context
+    first, n_local = shard_sequences(n_total, world, rank)
+    K, W = args.steps, args.warmup
+    max_seq = ctx + W + 2 * K + 2
+    dec = Decoder(cfg, n_local, max_seq, device=f"cuda:{local}", seed=0)
+    dec.fill_kv_normal(seed=1000 + rank)
+    dec.set_lengths(ctx)
+    rng = np.random.default_rng(7)
+    ids0 = rng.integers(0, cfg.vocab_size, n_total).astype(np.int32)[first:first + n_local]
+    dec.ids_in.copy_(torch.from_numpy(ids0).cuda())
+    stream = torch.cuda.current_stream()
+
+    for _ in range(W):
+        dec.step()
+    own, lib = dec.launches_per_step()
+
+    # ---- device-resident throughput
+    barrier(dist, torch)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(K):
+            dec.step()
+        ev1.record(stream)
+        ev1.synchronize()
+    barrier(dist, torch)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / K, dist, torch)
+    value = n_total / (ms / 1e3)
+
+    # ---- end to end through the host-facing step (pinned ids in / out)
+    h_in = torch.from_numpy(dec.ids_out.cpu().numpy()).pin_memory()
+    h_out = torch.empty(n_local, dtype=torch.int32).pin_memory()
+    barrier(dist, torch)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K):
+        dec.step_host(h_in, h_out, stream)
+        h_in.copy_(h_out)
+    e1.record(stream)
+    e1.synchronize()
+    barrier(dist, torch)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K, dist, torch)
+
+    # ---- dominant kernel alone: decode attention over layer 0's cache
+    g = Gpu(local)
+    hd, nkv, nq = cfg.head_dim, cfg.num_kv_heads, cfg.num_heads
+    per = nkv * max_seq * hd
+    lens_host = np.full(n_local, ctx + 1, np.int32)
+    lens = torch.from_numpy(lens_host).cuda()
+    q = torch.randn(n_local, cfg.qkv_dim, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(n_local, cfg.q_dim, dtype=torch.bfloat16, device="cuda")
+    wsb = g.attention_decode_workspace_bytes(n_local, max_seq, nq, nkv, hd)
+    ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
+    kc0, vc0 = dec.kc[0].reshape(-1), dec.vc[0].reshape(-1)
+
+    def attn():
+        g.attention_decode(q, cfg.qkv_dim, kc0, vc0, per, lens, max_seq, nq, nkv, hd, max_seq,
+                           out, cfg.q_dim, workspace=ws)
+
+    for _ in range(3):
+        attn()
+    reps = max(10, min(200, K))
+    a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a0.record(stream)
+    for _ in range(reps):
+        attn()
+    a1.record(stream)
+    a1.synchronize()
+    attn_ms = a0.elapsed_time(a1) / reps
+    alg_bytes = int(lens_host.sum()) * nkv * hd * 2 * 2 + n_local * nq * hd * 2 * 2
+    achieved = alg_bytes / (attn_ms / 1e3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "attn_decode_traffic.json")
+    if os.path.exists(tp):
+        with open(tp) as f:
+            tr = json.load(f)
+        traffic = int(tr["dram_bytes_per_alg_byte"] * alg_bytes)
+    clocks = clk.summary()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        tps, steps, dt = cpu_decode_sample(cfg, ctx, args.cpu_seconds, 64, threads)
+        cpu = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"oracle decode step of 1 sequence at context {ctx}, all 16 layers, "
+                         f"{steps} steps in {dt:.1f} s on {threads} threads ({cpu_model()})"}
+    if dist is not None:
+        dist.barrier()
+    dec.close()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+            "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init weights N(0,0.02), KV N(0,1), uniform random ids",
+            "config": {"workload": "cfg5: sequence-sharded long-context decode, Llama-3.2-1B "
+                                   "(16 layers, random init), 256 sequences x 16384-token KV",
+                       "n_seq_total": n_total, "context": ctx, "n_seq_per_gpu": n_local,
+                       "parallelism": f"independent sequences over {world} GPU(s)",
+                       "l2": "inputs larger than L2 (KV %.1f GB per GPU, weights 2.47 GB)" %
+                             (2 * cfg.num_layers * n_local * per * 2 / 1e9)},
+            "e2e": {"value": n_total / (e2e_ms / 1e3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * n_total, "d2h_bytes_per_step": 4 * n_total},
+            "gpu_launches": K * own,
+            "launches_per_step": {"own": own, "cublas": lib},
+            "roofline": {"bound": "hbm", "achieved": achieved,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
+                         "kernel": "kvb_attention_decode (split-KV decode + combine), layer 0",
+                         "alg_bytes_per_launch": alg_bytes, "ms_per_launch": attn_ms,
+                         "peak_source": f"{peak_kind} hbm_gbs"},
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    from kvasir_b200.config import LlamaConfig
+    cfg = LlamaConfig.llama_3_2_1b()
+    threads = os.cpu_count() or 1
+    steps = max(1, min(args.steps, 5))
+    sample = CpuDecodeSample(cfg, args.context, steps + 1, threads)
+    sample.step()  # warm-up
+    per_step = [sample.step() for _ in range(steps)]
+    sec = statistics.mean(per_step)
+    v = 1.0 / sec
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": 1, "ms_per_step": sec * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic: seeded N(0,0.02) weights, N(0,1) KV",
+            "config": {"workload": "cfg5: sequence-sharded long-context decode, Llama-3.2-1B "
+                                   "(16 layers, random init), 256 sequences x 16384-token KV",
+                       "context": args.context},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
+                             "sample": f"oracle decode step of 1 sequence per timed step at "
+                                       f"context {args.context} ({cpu_model()})"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=60)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="kernel", choices=["kernel", "reference"])
+    ap.add_argument("--workload", default="cfg5", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+    ap.add_argument("--seqs", type=int, default=256, help="total sequences (cfg5)")
+    ap.add_argument("--context", type=int, default=16384, help="KV tokens per sequence (cfg5)")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.workload == "cfg5":
+        return run_decode(args)
+    from kvasir_b200 import bench_suite
+    bench_suite.run(args.workload, args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,255 @@
+/*
+ * kvasir_b200.h -- C ABI of libkvasir_b200.so, the sm_100a (B200) kernel
+ * chain that replaces the launch wrappers of kvasir's engine/src/gpu.
+ *
+ * Conventions (mirroring the reference's `impl Gpu` methods in
+ * engine/src/gpu/kernels.rs:58-372 and engine/src/gpu/gemm.rs:63-115):
+ *   - every buffer is a device pointer plus its length in ELEMENTS, exactly
+ *     the (ptr, len) pair a cudarc CudaView carries;
+ *   - every entry point validates every dimension and length before it
+ *     launches anything and returns KVB_ERR_SHAPE with a message (read with
+ *     kvb_last_error) instead of launching (reference ensure_shape!,
+ *     engine/src/error.rs:23-30); dimensions must fit in int32
+ *     (reference i32_of, kernels.rs:48-50);
+ *   - launches are asynchronous on the caller's stream; no entry point
+ *     synchronises, allocates device memory or frees it (reference
+ *     DESIGN.md:30-33).  Kernels that need scratch take a caller-provided
+ *     workspace sized by the matching *_workspace_bytes function;
+ *   - 16-bit element arrays carry a dtype tag: KVB_BF16 (primary) or KVB_F16
+ *     (the reference's own element type).
+ */
+#ifndef KVASIR_B200_H
+#define KVASIR_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* kvb_stream_t;
+
+enum kvb_status {
+    KVB_OK = 0,
+    KVB_ERR_SHAPE = 1,       /* a size or length check failed; nothing launched */
+    KVB_ERR_CUDA = 2,        /* a CUDA runtime / driver / cuBLAS call failed */
+    KVB_ERR_UNSUPPORTED = 3, /* valid request this build does not implement */
+    KVB_ERR_DEVICE = 4       /* a kernel reported a device-side error (kvb_device_error) */
+};
+
+enum kvb_dtype { KVB_BF16 = 0, KVB_F16 = 1 };
+
+/* Message describing the last non-OK status returned on this host thread. */
+const char* kvb_last_error(void);
+const char* kvb_version(void);
+
+/* Reads and clears the device-side error word of the current device
+ * (bit 1: a bounded wait timed out; 2: a sequence length out of range;
+ * 4: a position outside the cache or RoPE table).  Synchronises the device. */
+int kvb_device_error(uint32_t* code);
+
+/* ---------------------------------------------------------------------------
+ * Kernels with a reference counterpart (one entry per `Gpu` method).
+ * ------------------------------------------------------------------------- */
+
+/* Replaces Gpu::embedding_gather (engine/src/gpu/kernels.rs:59-88;
+ * kernel engine/kernels/embedding.cu:3-10).  out[t,:] = table[ids[t],:];
+ * ids outside [0, table_len/hidden) produce a zero row. */
+int kvb_embedding_gather(kvb_stream_t stream, const int32_t* ids, size_t t, const void* table,
+                         size_t table_len, void* out, size_t out_len, size_t hidden, int dtype);
+
+/* Replaces Gpu::rmsnorm (kernels.rs:90-121; engine/kernels/rmsnorm.cu:3-17).
+ * out = x * rsqrt(mean(x^2) + eps) * w, f32 accumulation, one rounding. */
+int kvb_rmsnorm(kvb_stream_t stream, const void* x, size_t x_len, const void* w, size_t w_len,
+                void* out, size_t out_len, size_t rows, size_t hidden, float eps, int dtype);
+
+/* Replaces Gpu::rope_inplace (kernels.rs:124-169; engine/kernels/rope.cu:3-19).
+ * rotate_half RoPE on the n_q + n_kv leading heads of each qkv row, token t at
+ * position pos0 + t; cos/sin are f32 [max_pos, head_dim/2]. */
+int kvb_rope_inplace(kvb_stream_t stream, void* qkv, size_t qkv_len, const float* cos_t,
+                     size_t cos_len, const float* sin_t, size_t sin_len, size_t t, size_t pos0,
+                     size_t n_q, size_t n_kv, size_t head_dim, int dtype);
+
+/* Replaces Gpu::silu_mul (kernels.rs:171-194; engine/kernels/silu_mul.cu:3-12).
+ * out[t,i] = silu(gu[t,i]) * gu[t,inter+i]. */
+int kvb_silu_mul(kvb_stream_t stream, const void* gu, size_t gu_len, void* out, size_t out_len,
+                 size_t t, size_t inter, int dtype);
+
+/* Replaces Gpu::add_inplace (kernels.rs:196-209; engine/kernels/elementwise.cu:4-9). */
+int kvb_add_inplace(kvb_stream_t stream, void* x, size_t x_len, const void* y, size_t y_len,
+                    int dtype);
+
+/* Replaces Gpu::bf16_to_f16 (kernels.rs:211-235; engine/kernels/elementwise.cu:11-20).
+ * Adds to *bad the number of values with !(|v| <= 65504). */
+int kvb_bf16_to_f16(kvb_stream_t stream, const void* src, size_t src_len, void* dst,
+                    size_t dst_len, uint32_t* bad, size_t bad_len);
+
+/* Replaces Gpu::kv_append (kernels.rs:238-291; engine/kernels/elementwise.cu:22-34).
+ * Copies the k and v slices of T qkv rows to kc/vc[h, pos0+t, :] of the
+ * contiguous per-layer cache [n_kv, max_seq, head_dim]. */
+int kvb_kv_append(kvb_stream_t stream, const void* qkv, size_t qkv_len, void* kc, size_t kc_len,
+                  void* vc, size_t vc_len, size_t t, size_t pos0, size_t n_q, size_t n_kv,
+                  size_t head_dim, size_t max_seq, int dtype);
+
+/* Replaces Gpu::attention (kernels.rs:294-371; engine/kernels/attention.cu:5-57).
+ * Causal GQA attention of T query rows (read from the qkv buffer) against the
+ * contiguous cache, scale 1/sqrt(head_dim).  T == 1 runs the split-KV decode
+ * kernel, T > 1 the tcgen05 prefill kernel (head_dim 64) or, for other head
+ * sizes, a general kernel.  workspace may be NULL (no KV split); a workspace
+ * of kvb_attention_workspace_bytes(...) bytes lets long contexts split across
+ * CTAs.  Unlike the reference there is no 48 KiB / ~11.9k-key limit. */
+int kvb_attention(kvb_stream_t stream, const void* qkv, size_t qkv_len, const void* kc,
+                  size_t kc_len, const void* vc, size_t vc_len, void* out, size_t out_len,
+                  size_t t, size_t pos0, size_t n_q, size_t n_kv, size_t head_dim, size_t max_seq,
+                  void* workspace, size_t workspace_len, int dtype);
+size_t kvb_attention_workspace_bytes(size_t t, size_t pos0, size_t n_q, size_t n_kv,
+                                     size_t head_dim);
+
+/* Replaces gemm::linear_f16 / gemm::linear_f32 (engine/src/gpu/gemm.rs:17-115):
+ * y[t,out] = x[t,in] * w[out,in]^T through cublasGemmEx, f32 accumulate; y is
+ * 16-bit (y_f32 = 0) or f32 (y_f32 = 1).  The handle owns a cuBLAS handle. */
+typedef struct kvb_blas_s* kvb_blas_t;
+int kvb_blas_create(kvb_blas_t* out);
+int kvb_blas_destroy(kvb_blas_t blas);
+int kvb_linear(kvb_blas_t blas, kvb_stream_t stream, const void* x, size_t x_len, const void* w,
+               size_t w_len, void* y, size_t y_len, size_t t, size_t in_dim, size_t out_dim,
+               int dtype, int y_f32);
+/* Hands cuBLAS a caller-owned device workspace (cublasSetWorkspace) so that
+ * GEMMs recorded into a CUDA graph never allocate. */
+int kvb_blas_set_workspace(kvb_blas_t blas, void* workspace, size_t workspace_len);
+
+/* Host-side RoPE table (engine/src/model/rope.rs:3-39): f64 inverse
+ * frequencies with optional llama3 scaling, f32 cos/sin [max_pos, head_dim/2]
+ * written to HOST arrays cos_t/sin_t of max_pos*head_dim/2 floats. */
+int kvb_rope_table(size_t head_dim, double theta, int llama3_scaling, double factor,
+                   double low_freq_factor, double high_freq_factor, double orig_max_pos,
+                   size_t max_pos, float* cos_t, float* sin_t);
+
+/* ---------------------------------------------------------------------------
+ * Fused and batched kernels (no single reference counterpart; each equals a
+ * composition of the entries above, bit for bit).
+ * ------------------------------------------------------------------------- */
+
+/* kvb_rope_inplace followed by kvb_kv_append, in one pass over qkv
+ * (kernels.rs:124-169 + :238-291): q and k heads rotated in place, rotated k
+ * and raw v written to the cache. */
+int kvb_rope_kv_append(kvb_stream_t stream, void* qkv, size_t qkv_len, const float* cos_t,
+                       const float* sin_t, size_t table_len, void* kc, void* vc, size_t cache_len,
+                       size_t t, size_t pos0, size_t n_q, size_t n_kv, size_t head_dim,
+                       size_t max_seq, int dtype);
+
+/* Batched decode form: row b of qkv belongs to sequence b at position pos[b]
+ * (device int32 array).  Sequence b's cache starts at kc/vc + b*seq_stride
+ * elements and is laid out [n_kv, max_seq, head_dim]. */
+int kvb_rope_kv_append_batched(kvb_stream_t stream, void* qkv, size_t n_seq, const int32_t* pos,
+                               const float* cos_t, const float* sin_t, size_t table_len,
+                               void* kc, void* vc, size_t seq_stride, size_t cache_len,
+                               size_t n_q, size_t n_kv, size_t head_dim, size_t max_seq,
+                               int dtype);
+
+/* kvb_add_inplace(x, y) followed by kvb_rmsnorm(x, w, out): the residual
+ * stream x is updated in place and its normalised copy written to out. */
+int kvb_add_rmsnorm(kvb_stream_t stream, void* x, const void* y, const void* w, void* out,
+                    size_t rows, size_t hidden, float eps, int dtype);
+
+/* Batched single-query decode attention, one query row per sequence:
+ * q row b at q + b*q_row_stride (head h at h*head_dim), sequence b attends
+ * keys [0, lens[b]) of its cache (kc/vc + b*seq_stride, laid out
+ * [n_kv, max_seq, head_dim]); out row b at out + b*out_row_stride.  lens is a
+ * device int32 array with 0 <= lens[b] <= max_len <= max_seq (lens[b] == 0
+ * gives a zero row).  Split-KV over CTAs with a combine pass when the
+ * workspace (kvb_attention_decode_workspace_bytes) allows. */
+int kvb_attention_decode(kvb_stream_t stream, const void* q, size_t q_row_stride, const void* kc,
+                         const void* vc, size_t seq_stride, size_t cache_len,
+                         const int32_t* lens, size_t n_seq, size_t max_len, size_t n_q,
+                         size_t n_kv, size_t head_dim, size_t max_seq, float scale, void* out,
+                         size_t out_row_stride, void* workspace, size_t workspace_len,
+                         int dtype);
+size_t kvb_attention_decode_workspace_bytes(size_t n_seq, size_t max_len, size_t n_q,
+                                            size_t n_kv, size_t head_dim);
+
+/* Causal prefill attention for n_seq sequences of t tokens each (uniform
+ * length, positions pos0 .. pos0+t-1): qkv rows [n_seq*t, (n_q+2n_kv)*hd],
+ * caches [n_seq][n_kv][max_seq][hd] already holding keys [0, pos0+t); out
+ * [n_seq*t, n_q*hd].  tcgen05/TMEM kernel for head_dim 64. */
+int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, const void* kc, const void* vc,
+                          void* out, size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
+                          size_t head_dim, size_t max_seq, int dtype);
+
+/* Greedy sampling: ids[r] = first index of the maximum of logits[r, 0:vocab)
+ * (NaN never wins).  If advance is non-NULL, advance[r] += 1 for every r and,
+ * if advance2 is non-NULL, advance2[r] += 1 (position / length counters of
+ * the decode loop). */
+int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
+                   int32_t* ids, int32_t* advance, int32_t* advance2);
+
+/* ---------------------------------------------------------------------------
+ * Decode-step driver: the reference's planned Llama forward pass
+ * (reference DESIGN.md:36-74, engine/src/model/weights.rs:13-27 for the
+ * weight layout) for n_seq independent sequences, one token each, captured
+ * in a CUDA graph on first use.  Weights, KV cache and workspace are
+ * caller-owned device buffers; the driver allocates nothing on the device
+ * after kvb_decoder_create (which creates its cuBLAS handle).
+ * ------------------------------------------------------------------------- */
+typedef struct {
+    int32_t hidden, inter, n_layers, n_q, n_kv, head_dim, vocab;
+    int32_t max_seq;  /* KV capacity per sequence */
+    int32_t n_seq;    /* sequences decoded per step */
+    float eps;
+    int32_t dtype;
+} kvb_decoder_config;
+
+typedef struct {
+    const void* embed;      /* [vocab, hidden]; tied LM head */
+    const void* final_norm; /* [hidden] */
+    const void* const* attn_norm; /* host array of n_layers device pointers, [hidden] each */
+    const void* const* w_qkv;     /* [q_dim + 2 kv_dim, hidden] */
+    const void* const* w_o;       /* [hidden, q_dim] */
+    const void* const* mlp_norm;  /* [hidden] */
+    const void* const* w_gu;      /* [2 inter, hidden] */
+    const void* const* w_down;    /* [hidden, inter] */
+} kvb_decoder_weights;
+
+typedef struct kvb_decoder_s* kvb_decoder_t;
+
+/* Bytes of device workspace the driver needs (activations, logits, split-KV
+ * partials, position counters). */
+size_t kvb_decoder_workspace_bytes(const kvb_decoder_config* cfg);
+/* kc/vc: [n_layers][n_seq][n_kv][max_seq][head_dim] each; cos/sin: f32
+ * [max_seq, head_dim/2] device tables. */
+int kvb_decoder_create(kvb_decoder_t* out, const kvb_decoder_config* cfg,
+                       const kvb_decoder_weights* w, void* kc, void* vc, const float* cos_t,
+                       const float* sin_t, void* workspace, size_t workspace_len);
+int kvb_decoder_destroy(kvb_decoder_t dec);
+/* Sets the per-sequence cache fill (tokens already in the cache) from a host
+ * array; the next step writes position cur_len[b]. */
+int kvb_decoder_set_lengths(kvb_decoder_t dec, kvb_stream_t stream, const int32_t* cur_len_host);
+/* Device pointers of the step's input ids and output ids ([n_seq] int32 each).
+ * The step reads ids_in and writes the greedy ids to ids_out; each step also
+ * copies ids_out to ids_in so consecutive steps continue generation. */
+int32_t* kvb_decoder_ids_in(kvb_decoder_t dec);
+int32_t* kvb_decoder_ids_out(kvb_decoder_t dec);
+const float* kvb_decoder_logits(kvb_decoder_t dec);
+/* One decode step on the device (graph replay after the first call). */
+int kvb_decoder_step(kvb_decoder_t dec, kvb_stream_t stream);
+/* One decode step from host to host: copies ids_host_in (pinned or pageable)
+ * to the device, runs the step, copies the greedy ids back to ids_host_out
+ * and synchronises the stream. */
+int kvb_decoder_step_host(kvb_decoder_t dec, kvb_stream_t stream, const int32_t* ids_host_in,
+                          int32_t* ids_host_out);
+/* Number of kernels (own + cuBLAS) one step launches. */
+int kvb_decoder_launches_per_step(kvb_decoder_t dec, int* own, int* library);
+
+/* ---------------------------------------------------------------------------
+ * Self test of the bounded-wait machinery: launches one CTA that waits on an
+ * mbarrier nobody completes, with a time limit of limit_ms; returns
+ * KVB_ERR_DEVICE once the kernel has given up (the device stays usable).
+ * ------------------------------------------------------------------------- */
+int kvb_selftest_wait_timeout(kvb_stream_t stream, uint32_t limit_ms);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KVASIR_B200_H */

@@ -1,0 +1,296 @@
+// attn_decode.cuh -- split-KV GQA decode attention for head_dim 64.
+//
+// Work unit: one CTA per (key chunk, kv head, sequence).  The group of
+// n_q/n_kv query heads that share a kv head is handled by the same CTA, so
+// every K/V byte crosses HBM once (the reference kernel,
+// engine/kernels/attention.cu:5-57, re-reads K/V once per query head and reads
+// keys with a head_dim stride across threads).
+//
+// Data path per warp, per 64-key tile:
+//   TMA (cp.async.bulk.tensor, 128-byte swizzle, no multicast) brings the K
+//   and V tiles (8 KB each) into shared memory and completes an mbarrier;
+//   S = Q K^T runs on the tensor cores as m16n8k16 MMAs with the group's
+//   query heads as the 16 rows (padded), K fragments via ldmatrix;
+//   an online softmax in f32 (exp2, running max / sum) turns S into P;
+//   O += P V with P re-used from registers and V fragments via ldmatrix.trans.
+// The four warps of a CTA take interleaved tiles of the chunk, merge their
+// (max, sum, O) states through shared memory, and either write the final
+// rows (single-chunk sequences) or an unnormalised partial that
+// attn_combine_kernel folds across chunks.  The kernel is HBM-bound: per key
+// it reads 256 bytes (K+V) and does 4*64*2*2 = 1024 useful flops.
+#pragma once
+
+#include "kvb_ptx.cuh"
+
+namespace kvb {
+
+constexpr int kDecTileKeys = 64;
+constexpr int kDecWarps = 4;
+constexpr int kDecTileBytes = kDecTileKeys * 64 * 2;  // one K (or V) tile
+constexpr int kDecSmemBytes = kDecWarps * 2 * kDecTileBytes + 1024;  // + alignment slack
+
+struct DecodeArgs {
+    const uint16_t* q;
+    long long q_row_stride;
+    const int32_t* lens;     // per-sequence key count (device) or nullptr
+    int len_const;           // key count when lens == nullptr
+    int max_len;
+    int n_kv, group, max_seq;
+    long long seq_rows;      // rows (of 64 elements) between sequences in the cache
+    float scale_log2;        // softmax scale * log2(e)
+    uint16_t* out;
+    long long out_row_stride;
+    float* ws;               // split-KV partials, or nullptr when chunks == 1
+    int chunk_keys;          // keys per CTA (multiple of 256)
+    int max_chunks;
+};
+
+__device__ __forceinline__ int decode_len(const DecodeArgs& a, int b) {
+    int len = a.lens ? a.lens[b] : a.len_const;
+    if (len < 0 || len > a.max_len) {
+        if (threadIdx.x == 0) raise_dev_error(kDevErrBadLength);
+        len = len < 0 ? 0 : a.max_len;
+    }
+    return len;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                             const __grid_constant__ CUtensorMap vmap,
+                                                             DecodeArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t bars[kDecWarps];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int G = a.group;
+
+    const int len = decode_len(a, b);
+    const int n_chunks = (len + a.chunk_keys - 1) / a.chunk_keys;
+    T* outb = reinterpret_cast<T*>(a.out) + (size_t)b * a.out_row_stride + (size_t)kvh * G * 64;
+    if (len == 0) {  // no keys: defined as a zero output row
+        if (chunk == 0)
+            for (int i = threadIdx.x; i < G * 64; i += blockDim.x) outb[i] = Elem<T>::from_f(0.f);
+        return;
+    }
+    if (chunk >= n_chunks) return;
+    const int key_begin = chunk * a.chunk_keys;
+    const int key_end = min(len, key_begin + a.chunk_keys);
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDecWarps; ++i) mbar_init(&bars[i], 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    uint8_t* ktile = smem + warp * 2 * kDecTileBytes;
+    uint8_t* vtile = ktile + kDecTileBytes;
+    const uint32_t kb = smem_u32(ktile), vb = smem_u32(vtile);
+    const int row_base = (int)((long long)b * a.seq_rows + (long long)kvh * a.max_seq);
+
+    // Q fragments (A operand, rows = the group's heads, padded to 16).
+    uint32_t qa[4][4];
+    {
+        const T* qb = reinterpret_cast<const T*>(a.q) + (size_t)b * a.q_row_stride +
+                      (size_t)kvh * G * 64;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+            const int d0 = 16 * s + 2 * c;
+            qa[s][0] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * 64 + d0) : 0u;
+            qa[s][1] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * 64 + d0) : 0u;
+            qa[s][2] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * 64 + d0 + 8) : 0u;
+            qa[s][3] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * 64 + d0 + 8) : 0u;
+        }
+    }
+
+    float o[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    uint32_t phase = 0;
+    bool ok = true;
+
+    for (int kt0 = key_begin + warp * kDecTileKeys; kt0 < key_end && ok;
+         kt0 += kDecWarps * kDecTileKeys) {
+        const int nk = min(kDecTileKeys, key_end - kt0);
+        if (lane == 0) {
+            mbar_expect_tx(&bars[warp], 2 * kDecTileBytes);
+            tma_load_2d(ktile, &kmap, &bars[warp], 0, row_base + kt0);
+            tma_load_2d(vtile, &vmap, &bars[warp], 0, row_base + kt0);
+        }
+        ok = mbar_wait(&bars[warp], phase);
+        phase ^= 1;
+        if (!ok) break;
+        if (nk < kDecTileKeys) {  // rows past the sequence end: zero V so that 0 * garbage stays 0
+            uint4* vz = reinterpret_cast<uint4*>(vtile);
+            for (int i = nk * 8 + lane; i < kDecTileKeys * 8; i += 32) vz[i] = make_uint4(0, 0, 0, 0);
+            __syncwarp();
+        }
+
+        // ---- S = Q K^T : 16 x 64 per warp
+        float s[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+            const int r = 8 * j + (lane & 7);
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int ch = 4 * hf + (lane >> 3);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4(kb + r * 128 + ((ch ^ (lane & 7)) << 4), b0, b1, b2, b3);
+                mma_16816<T>(s[j], qa[2 * hf], b0, b1);
+                mma_16816<T>(s[j], qa[2 * hf + 1], b2, b3);
+            }
+        }
+        // ---- online softmax (log2 domain); rows g (e = 0,1) and g + 8 (e = 2,3)
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int key = 8 * j + 2 * c + (e & 1);
+                s[j][e] = key < nk ? s[j][e] * a.scale_log2 : -INFINITY;
+            }
+            mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+            mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+        const float al0 = exp2f(m0 - mn0), al1 = exp2f(m1 - mn1);
+        float sum0 = 0.f, sum1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            s[j][0] = exp2f(s[j][0] - mn0);
+            s[j][1] = exp2f(s[j][1] - mn0);
+            s[j][2] = exp2f(s[j][2] - mn1);
+            s[j][3] = exp2f(s[j][3] - mn1);
+            sum0 += s[j][0] + s[j][1];
+            sum1 += s[j][2] + s[j][3];
+        }
+        sum0 += __shfl_xor_sync(0xffffffffu, sum0, 1);
+        sum0 += __shfl_xor_sync(0xffffffffu, sum0, 2);
+        sum1 += __shfl_xor_sync(0xffffffffu, sum1, 1);
+        sum1 += __shfl_xor_sync(0xffffffffu, sum1, 2);
+        l0 = l0 * al0 + sum0;
+        l1 = l1 * al1 + sum1;
+        m0 = mn0;
+        m1 = mn1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            o[j][0] *= al0;
+            o[j][1] *= al0;
+            o[j][2] *= al1;
+            o[j][3] *= al1;
+        }
+        // ---- O += P V : P from registers, V^T fragments via ldmatrix.trans
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+            uint32_t pa[4];
+            pa[0] = Elem<T>::pack(s[2 * kk][0], s[2 * kk][1]);
+            pa[1] = Elem<T>::pack(s[2 * kk][2], s[2 * kk][3]);
+            pa[2] = Elem<T>::pack(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+            pa[3] = Elem<T>::pack(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+            const int key = 16 * kk + (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+            for (int jp = 0; jp < 4; ++jp) {
+                const int ch = 2 * jp + (lane >> 4);
+                uint32_t b0, b1, b2, b3;
+                ldsm_x4_t(vb + key * 128 + ((ch ^ (lane & 7)) << 4), b0, b1, b2, b3);
+                mma_16816<T>(o[2 * jp], pa, b0, b1);
+                mma_16816<T>(o[2 * jp + 1], pa, b2, b3);
+            }
+        }
+        __syncwarp();
+        fence_async_smem();  // generic-proxy reads of this buffer precede the next TMA write
+    }
+    if (!ok) {
+        // A copy did not complete in time (the error word is set): wait once
+        // more, bounded, so that no copy lands in shared memory after the CTA
+        // exits, and contribute an empty state to the merge.
+        mbar_wait(&bars[warp], phase ^ 1);
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    }
+
+    // ---- merge the four warps' states through shared memory (own K tile area)
+    float* wo = reinterpret_cast<float*>(ktile);  // [16 rows][64] O, then m[16], l[16]
+    float* wm = wo + 16 * 64;
+    float* wl = wm + 16;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int d = 8 * j + 2 * c;
+        wo[g * 64 + d] = o[j][0];
+        wo[g * 64 + d + 1] = o[j][1];
+        wo[(g + 8) * 64 + d] = o[j][2];
+        wo[(g + 8) * 64 + d + 1] = o[j][3];
+    }
+    if (c == 0) {
+        wm[g] = m0;
+        wl[g] = l0;
+        wm[g + 8] = m1;
+        wl[g + 8] = l1;
+    }
+    __syncthreads();
+    float* wsb = nullptr;
+    if (n_chunks > 1)
+        wsb = a.ws + (((size_t)b * a.n_kv + kvh) * a.max_chunks + chunk) * (size_t)G * 66;
+    for (int i = threadIdx.x; i < G * 64; i += blockDim.x) {
+        const int r = i >> 6, d = i & 63;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDecWarps; ++w)
+            M = fmaxf(M, reinterpret_cast<const float*>(smem + w * 2 * kDecTileBytes)[16 * 64 + r]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDecWarps; ++w) {
+            const float* base = reinterpret_cast<const float*>(smem + w * 2 * kDecTileBytes);
+            const float mw = base[16 * 64 + r];
+            const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+            L += base[16 * 64 + 16 + r] * f;
+            O += base[r * 64 + d] * f;
+        }
+        if (n_chunks == 1) {
+            outb[i] = Elem<T>::from_f(L > 0.f ? O / L : 0.f);
+        } else {
+            wsb[i] = O;
+            if (d == 0) {
+                wsb[G * 64 + r] = M;
+                wsb[G * 65 + r] = L;
+            }
+        }
+    }
+}
+
+// Folds the per-chunk partials of every (sequence, kv head) with more than one chunk.
+template <typename T>
+__global__ void __launch_bounds__(256) attn_combine_kernel(DecodeArgs a) {
+    const int kvh = blockIdx.x, b = blockIdx.y;
+    const int G = a.group;
+    const int len = decode_len(a, b);
+    const int n_chunks = (len + a.chunk_keys - 1) / a.chunk_keys;
+    if (n_chunks <= 1) return;
+    const float* base = a.ws + ((size_t)b * a.n_kv + kvh) * a.max_chunks * (size_t)G * 66;
+    T* outb = reinterpret_cast<T*>(a.out) + (size_t)b * a.out_row_stride + (size_t)kvh * G * 64;
+    for (int i = threadIdx.x; i < G * 64; i += blockDim.x) {
+        const int r = i >> 6;
+        float M = -INFINITY;
+        for (int ch = 0; ch < n_chunks; ++ch) M = fmaxf(M, base[(size_t)ch * G * 66 + G * 64 + r]);
+        float L = 0.f, O = 0.f;
+        for (int ch = 0; ch < n_chunks; ++ch) {
+            const float* p = base + (size_t)ch * G * 66;
+            const float f = exp2f(p[G * 64 + r] - M);
+            L += p[G * 65 + r] * f;
+            O += p[i] * f;
+        }
+        outb[i] = Elem<T>::from_f(O / L);
+    }
+}
+
+}  // namespace kvb

@@ -1,0 +1,825 @@
+// kvb_api.cu -- the kernels of libkvasir_b200 and their C-ABI launchers.
+//
+// Each kvb_* entry point validates its arguments exactly where the matching
+// reference wrapper does (engine/src/gpu/kernels.rs, ensure_shape!), then picks
+// the fast path (16-byte vectors, TMA, tensor cores) when shapes and
+// alignment allow it, else a general kernel -- always on the GPU.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "attn_decode.cuh"
+#include "attn_generic.cuh"
+#include "attn_prefill.cuh"
+#include "elementwise.cuh"
+#include "kvb_host.h"
+#include "norm.cuh"
+#include "rope.cuh"
+
+namespace kvb {
+
+// ---------------------------------------------------------------- host helpers
+static thread_local std::string t_err;
+
+int fail(int status, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_err = buf;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(KVB_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int num_sms() {
+    static int cache[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 148;
+    if (!cache[dev]) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+int encode_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, int dtype) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return fail(KVB_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+    cuuint64_t d[5], st[4];
+    cuuint32_t bx[5], es[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        bx[i] = box[i];
+        es[i] = 1;
+        if (i + 1 < rank) st[i] = strides_bytes[i];
+    }
+    const CUresult r = fn(map,
+                          dtype == KVB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                          (cuuint32_t)rank, const_cast<void*>(base), d, st, bx, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(KVB_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return KVB_OK;
+}
+
+// Grid size for grid-stride loops: enough CTAs to fill every SM several times.
+static unsigned grid_for(size_t work, int block) {
+    size_t g = (work + block - 1) / block;
+    const size_t cap = (size_t)num_sms() * 16;
+    if (g > cap) g = cap;
+    return g ? (unsigned)g : 1u;
+}
+
+template <typename F>
+static void set_max_smem(F* kernel, int bytes) {
+    // Idempotent; called before the first launch of each instantiation.
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+// ---------------------------------------------------------------- rope / kv append launcher
+static int launch_rope(kvb_stream_t stream, const RopeArgs& a, int rows, int dtype, bool vec) {
+    if (rows == 0) return KVB_OK;
+    if (vec) {
+        if (dtype == KVB_BF16)
+            rope_append_vec_kernel<__nv_bfloat16><<<rows, 256, 0, stream>>>(a);
+        else
+            rope_append_vec_kernel<__half><<<rows, 256, 0, stream>>>(a);
+    } else {
+        if (dtype == KVB_BF16)
+            rope_append_scalar_kernel<__nv_bfloat16><<<rows, 256, 0, stream>>>(a);
+        else
+            rope_append_scalar_kernel<__half><<<rows, 256, 0, stream>>>(a);
+    }
+    KVB_CHECK_LAUNCH("rope/kv_append launch");
+    return KVB_OK;
+}
+
+// ---------------------------------------------------------------- decode attention launcher
+// Keys per CTA: aim for ~8 waves of 3 resident CTAs per SM over the worst-case
+// work (every sequence at max_len), at least one 64-key tile per warp.
+static int decode_chunk_keys(size_t n_seq, size_t n_kv, size_t max_len) {
+    const size_t tiles = (max_len + 63) / 64;
+    const size_t target = (size_t)num_sms() * 3 * 8;
+    size_t per_cta = (n_seq * n_kv * tiles + target - 1) / target;
+    if (per_cta < 4) per_cta = 4;
+    per_cta = (per_cta + 3) / 4 * 4;
+    if (per_cta > tiles) per_cta = (tiles + 3) / 4 * 4;
+    return (int)(per_cta * 64);
+}
+
+static size_t decode_ws_bytes(size_t n_seq, size_t max_len, size_t n_q, size_t n_kv) {
+    if (max_len == 0 || n_kv == 0) return 0;
+    const size_t ck = (size_t)decode_chunk_keys(n_seq, n_kv, max_len);
+    const size_t chunks = (max_len + ck - 1) / ck;
+    if (chunks <= 1) return 0;
+    const size_t group = n_q / n_kv;
+    return n_seq * n_kv * chunks * group * 66 * sizeof(float);
+}
+
+struct DecodeLaunch {
+    const void* q;
+    size_t q_row_stride;
+    const void* kc;
+    const void* vc;
+    size_t seq_stride;  // elements
+    size_t total_rows;  // rows of 64 elements covered by the caches
+    const int32_t* lens;
+    int len_const;
+    size_t n_seq, max_len, n_q, n_kv, max_seq;
+    float scale;
+    void* out;
+    size_t out_row_stride;
+    void* ws;
+    size_t ws_len;
+    int dtype;
+};
+
+static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
+    CUtensorMap kmap, vmap;
+    const uint64_t dims[2] = {64, L.total_rows};
+    const uint64_t strides[1] = {128};
+    const uint32_t box[2] = {64, 64};
+    int st = encode_tmap(&kmap, L.kc, 2, dims, strides, box, L.dtype);
+    if (st) return st;
+    st = encode_tmap(&vmap, L.vc, 2, dims, strides, box, L.dtype);
+    if (st) return st;
+
+    DecodeArgs a;
+    a.q = static_cast<const uint16_t*>(L.q);
+    a.q_row_stride = (long long)L.q_row_stride;
+    a.lens = L.lens;
+    a.len_const = L.len_const;
+    a.max_len = (int)L.max_len;
+    a.n_kv = (int)L.n_kv;
+    a.group = (int)(L.n_q / L.n_kv);
+    a.max_seq = (int)L.max_seq;
+    a.seq_rows = (long long)(L.seq_stride / 64);
+    a.scale_log2 = L.scale * 1.4426950408889634f;
+    a.out = static_cast<uint16_t*>(L.out);
+    a.out_row_stride = (long long)L.out_row_stride;
+    int ck = decode_chunk_keys(L.n_seq, L.n_kv, L.max_len);
+    const size_t need = decode_ws_bytes(L.n_seq, L.max_len, L.n_q, L.n_kv);
+    if (need == 0 || L.ws == nullptr || L.ws_len < need || !aligned(L.ws, 16)) {
+        ck = (int)(((L.max_len + 255) / 256) * 256);  // one chunk: no workspace
+        if (ck == 0) ck = 256;
+        a.ws = nullptr;
+    } else {
+        a.ws = static_cast<float*>(L.ws);
+    }
+    a.chunk_keys = ck;
+    a.max_chunks = (int)((L.max_len + ck - 1) / ck);
+    if (a.max_chunks < 1) a.max_chunks = 1;
+
+    dim3 grid(a.max_chunks, (unsigned)L.n_kv, (unsigned)L.n_seq);
+    if (L.dtype == KVB_BF16) {
+        set_max_smem(attn_decode_kernel<__nv_bfloat16>, kDecSmemBytes);
+        attn_decode_kernel<__nv_bfloat16><<<grid, 128, kDecSmemBytes, stream>>>(kmap, vmap, a);
+    } else {
+        set_max_smem(attn_decode_kernel<__half>, kDecSmemBytes);
+        attn_decode_kernel<__half><<<grid, 128, kDecSmemBytes, stream>>>(kmap, vmap, a);
+    }
+    KVB_CHECK_LAUNCH("attention decode launch");
+    if (a.max_chunks > 1) {
+        dim3 g2((unsigned)L.n_kv, (unsigned)L.n_seq);
+        if (L.dtype == KVB_BF16)
+            attn_combine_kernel<__nv_bfloat16><<<g2, 256, 0, stream>>>(a);
+        else
+            attn_combine_kernel<__half><<<g2, 256, 0, stream>>>(a);
+        KVB_CHECK_LAUNCH("attention combine launch");
+    }
+    return KVB_OK;
+}
+
+static int launch_generic_attn(kvb_stream_t stream, const GenericAttnArgs& a, size_t rows,
+                               int dtype) {
+    if (rows == 0) return KVB_OK;
+    dim3 grid((unsigned)((a.n_q + 3) / 4), (unsigned)rows);
+    if (dtype == KVB_BF16)
+        attn_generic_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(a);
+    else
+        attn_generic_kernel<__half><<<grid, 128, 0, stream>>>(a);
+    KVB_CHECK_LAUNCH("attention (general kernel) launch");
+    return KVB_OK;
+}
+
+static int launch_prefill(kvb_stream_t stream, const void* qkv, const void* kc, const void* vc,
+                          void* out, size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
+                          size_t max_seq, int dtype) {
+    const size_t stride = (n_q + 2 * n_kv) * 64;
+    CUtensorMap qmap, kmap, vmap;
+    {
+        const uint64_t dims[3] = {stride, t, n_seq};
+        const uint64_t strides[2] = {stride * 2, t * stride * 2};
+        const uint32_t box[3] = {64, (uint32_t)kPfRows, 1};
+        int st = encode_tmap(&qmap, qkv, 3, dims, strides, box, dtype);
+        if (st) return st;
+    }
+    {
+        const uint64_t dims[3] = {64, pos0 + t, n_seq * n_kv};
+        const uint64_t strides[2] = {128, max_seq * 128};
+        const uint32_t box[3] = {64, (uint32_t)kPfKeys, 1};
+        int st = encode_tmap(&kmap, kc, 3, dims, strides, box, dtype);
+        if (st) return st;
+        st = encode_tmap(&vmap, vc, 3, dims, strides, box, dtype);
+        if (st) return st;
+    }
+    PrefillArgs a;
+    a.t = (int)t;
+    a.pos0 = (int)pos0;
+    a.n_q = (int)n_q;
+    a.n_kv = (int)n_kv;
+    a.group = (int)(n_q / n_kv);
+    a.n_qtiles = (int)((t + kPfRows - 1) / kPfRows);
+    a.scale_log2 = (1.0f / sqrtf(64.0f)) * 1.4426950408889634f;
+    a.out = static_cast<uint16_t*>(out);
+    a.out_row_stride = (long long)(n_q * 64);
+    dim3 grid((unsigned)n_q, (unsigned)n_seq, (unsigned)a.n_qtiles);
+    if (dtype == KVB_BF16) {
+        set_max_smem(attn_prefill_kernel<__nv_bfloat16>, kPfSmemBytes);
+        attn_prefill_kernel<__nv_bfloat16><<<grid, 128, kPfSmemBytes, stream>>>(qmap, kmap, vmap, a);
+    } else {
+        set_max_smem(attn_prefill_kernel<__half>, kPfSmemBytes);
+        attn_prefill_kernel<__half><<<grid, 128, kPfSmemBytes, stream>>>(qmap, kmap, vmap, a);
+    }
+    KVB_CHECK_LAUNCH("attention prefill launch");
+    return KVB_OK;
+}
+
+// ---------------------------------------------------------------- norm launcher
+template <bool kAdd>
+static int launch_rmsnorm(kvb_stream_t stream, void* x, const void* y, const void* w, void* out,
+                          size_t rows, size_t hidden, float eps, int dtype) {
+    if (rows == 0) return KVB_OK;
+    const size_t chunks = hidden / 8;
+    const bool vec = hidden % 8 == 0 && aligned(x, 16) && aligned(w, 16) && aligned(out, 16) &&
+                     (!kAdd || aligned(y, 16)) && chunks <= 32 * 16;
+    if (vec) {
+        const unsigned grid = (unsigned)((rows + 3) / 4);
+        const float ih = 1.0f / (float)hidden;
+        const int nv = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : chunks <= 256 ? 8 : 16;
+#define KVB_NORM_CASE(NV)                                                                          \
+    case NV:                                                                                       \
+        if (dtype == KVB_BF16)                                                                     \
+            rmsnorm_warp_kernel<__nv_bfloat16, NV, kAdd><<<grid, 128, 0, stream>>>(               \
+                (uint4*)x, (const uint4*)y, (const uint4*)w, (uint4*)out, (int)rows, (int)chunks, ih, \
+                eps);                                                                              \
+        else                                                                                       \
+            rmsnorm_warp_kernel<__half, NV, kAdd><<<grid, 128, 0, stream>>>(                      \
+                (uint4*)x, (const uint4*)y, (const uint4*)w, (uint4*)out, (int)rows, (int)chunks, ih, \
+                eps);                                                                              \
+        break;
+        switch (nv) {
+            KVB_NORM_CASE(1)
+            KVB_NORM_CASE(2)
+            KVB_NORM_CASE(4)
+            KVB_NORM_CASE(8)
+            KVB_NORM_CASE(16)
+        }
+#undef KVB_NORM_CASE
+    } else {
+        if (dtype == KVB_BF16)
+            rmsnorm_generic_kernel<__nv_bfloat16, kAdd><<<(unsigned)rows, 256, 0, stream>>>(
+                (__nv_bfloat16*)x, (const __nv_bfloat16*)y, (const __nv_bfloat16*)w,
+                (__nv_bfloat16*)out, (int)hidden, eps);
+        else
+            rmsnorm_generic_kernel<__half, kAdd><<<(unsigned)rows, 256, 0, stream>>>(
+                (__half*)x, (const __half*)y, (const __half*)w, (__half*)out, (int)hidden, eps);
+    }
+    KVB_CHECK_LAUNCH("rmsnorm launch");
+    return KVB_OK;
+}
+
+// ---------------------------------------------------------------- self test
+__global__ void selftest_wait_kernel(uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        // Nothing ever arrives on this barrier: the bounded wait must give up.
+        mbar_wait(&bar, 0, limit_ns, kDevErrSelfTest);
+        mbar_inval(&bar);
+    }
+}
+
+}  // namespace kvb
+
+using namespace kvb;
+
+// =====================================================================================
+extern "C" {
+
+const char* kvb_last_error(void) { return t_err.c_str(); }
+const char* kvb_version(void) { return "kvasir_b200 0.1 (sm_100a)"; }
+
+int kvb_device_error(uint32_t* code) {
+    KVB_CHECK(code != nullptr, "kvb_device_error: null output pointer");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "kvb_device_error: synchronize");
+    uint32_t v = 0, zero = 0;
+    e = cudaMemcpyFromSymbol(&v, g_dev_error, sizeof v);
+    if (e != cudaSuccess) return cuda_fail(e, "kvb_device_error: read");
+    e = cudaMemcpyToSymbol(g_dev_error, &zero, sizeof zero);
+    if (e != cudaSuccess) return cuda_fail(e, "kvb_device_error: clear");
+    *code = v;
+    return KVB_OK;
+}
+
+// ------------------------------------------------------------------ embedding gather
+int kvb_embedding_gather(kvb_stream_t stream, const int32_t* ids, size_t t, const void* table,
+                         size_t table_len, void* out, size_t out_len, size_t hidden, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(hidden > 0, "embedding: hidden must be > 0");
+    KVB_CHECK(out_len == t * hidden, "embedding: out has %zu elems, want %zux%zu", out_len, t, hidden);
+    KVB_CHECK(table_len % hidden == 0, "embedding: table len %zu not a multiple of hidden %zu",
+              table_len, hidden);
+    KVB_CHECK(fits_i32(hidden), "hidden=%zu does not fit in i32", hidden);
+    KVB_CHECK(fits_i32(t), "t=%zu does not fit in i32", t);
+    const size_t vocab = table_len / hidden;
+    KVB_CHECK(fits_i32(vocab), "vocab=%zu does not fit in i32", vocab);
+    if (t == 0) return KVB_OK;
+    if (hidden % 8 == 0 && aligned(table, 16) && aligned(out, 16)) {
+        embedding_gather_vec_kernel<<<(unsigned)((t + 3) / 4), 128, 0, stream>>>(
+            ids, (const uint4*)table, (uint4*)out, (int)t, (int)(hidden / 8), (int)vocab);
+    } else {
+        embedding_gather_scalar_kernel<<<(unsigned)t, 256, 0, stream>>>(
+            ids, (const uint16_t*)table, (uint16_t*)out, (int)hidden, (int)vocab);
+    }
+    KVB_CHECK_LAUNCH("embedding launch");
+    return KVB_OK;
+}
+
+// ------------------------------------------------------------------ rmsnorm
+int kvb_rmsnorm(kvb_stream_t stream, const void* x, size_t x_len, const void* w, size_t w_len,
+                void* out, size_t out_len, size_t rows, size_t hidden, float eps, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(x_len == rows * hidden, "rmsnorm: x has %zu elems, want %zux%zu", x_len, rows, hidden);
+    KVB_CHECK(out_len == rows * hidden, "rmsnorm: out has %zu elems, want %zux%zu", out_len, rows,
+              hidden);
+    KVB_CHECK(w_len == hidden, "rmsnorm: w has %zu elems, want %zu", w_len, hidden);
+    KVB_CHECK(fits_i32(hidden), "hidden=%zu does not fit in i32", hidden);
+    KVB_CHECK(fits_i32(rows), "rows=%zu does not fit in i32", rows);
+    KVB_CHECK(hidden > 0 || rows == 0, "rmsnorm: hidden must be > 0");
+    return launch_rmsnorm<false>(stream, const_cast<void*>(x), nullptr, w, out, rows, hidden, eps,
+                                 dtype);
+}
+
+int kvb_add_rmsnorm(kvb_stream_t stream, void* x, const void* y, const void* w, void* out,
+                    size_t rows, size_t hidden, float eps, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(fits_i32(hidden) && fits_i32(rows), "add_rmsnorm: rows/hidden do not fit in i32");
+    KVB_CHECK(hidden > 0 || rows == 0, "add_rmsnorm: hidden must be > 0");
+    KVB_CHECK(x != out, "add_rmsnorm: out must not alias the residual x");
+    return launch_rmsnorm<true>(stream, x, y, w, out, rows, hidden, eps, dtype);
+}
+
+// ------------------------------------------------------------------ rope / kv append
+static RopeArgs rope_args(void* qkv, size_t n_q, size_t n_kv, size_t hd) {
+    RopeArgs a;
+    memset(&a, 0, sizeof a);
+    a.qkv = static_cast<uint16_t*>(qkv);
+    a.n_q = (int)n_q;
+    a.n_kv = (int)n_kv;
+    a.hd = (int)hd;
+    a.row_stride = (int)((n_q + 2 * n_kv) * hd);
+    return a;
+}
+
+int kvb_rope_inplace(kvb_stream_t stream, void* qkv, size_t qkv_len, const float* cos_t,
+                     size_t cos_len, const float* sin_t, size_t sin_len, size_t t, size_t pos0,
+                     size_t n_q, size_t n_kv, size_t head_dim, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    KVB_CHECK(head_dim > 0 && head_dim % 2 == 0, "rope: odd head_dim %zu", head_dim);
+    KVB_CHECK(qkv_len == t * stride, "rope: qkv has %zu elems, want %zux%zu", qkv_len, t, stride);
+    KVB_CHECK(cos_len == sin_len && cos_len % (head_dim / 2) == 0, "rope: bad cos/sin table sizes");
+    const size_t max_pos = cos_len / (head_dim / 2);
+    KVB_CHECK(pos0 + t <= max_pos, "rope: positions up to %zu exceed table of %zu", pos0 + t, max_pos);
+    KVB_CHECK(fits_i32(pos0) && fits_i32(n_q) && fits_i32(n_kv) && fits_i32(head_dim) &&
+                  fits_i32(stride) && fits_i32(t) && fits_i32(max_pos),
+              "rope: a dimension does not fit in i32");
+    if (t == 0) return KVB_OK;
+    RopeArgs a = rope_args(qkv, n_q, n_kv, head_dim);
+    a.rows_per_seq = (int)t;
+    a.pos0 = (int)pos0;
+    a.cos_t = cos_t;
+    a.sin_t = sin_t;
+    a.max_pos = (int)max_pos;
+    a.max_seq = (int)max_pos;
+    a.do_rope = 1;
+    const bool vec = head_dim % 16 == 0 && aligned(qkv, 16) && aligned(cos_t, 16) && aligned(sin_t, 16);
+    return launch_rope(stream, a, (int)t, dtype, vec);
+}
+
+int kvb_kv_append(kvb_stream_t stream, const void* qkv, size_t qkv_len, void* kc, size_t kc_len,
+                  void* vc, size_t vc_len, size_t t, size_t pos0, size_t n_q, size_t n_kv,
+                  size_t head_dim, size_t max_seq, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    KVB_CHECK(qkv_len == t * stride, "kv_append: qkv has %zu elems, want %zux%zu", qkv_len, t, stride);
+    KVB_CHECK(kc_len == n_kv * max_seq * head_dim && vc_len == kc_len, "kv_append: bad cache sizes");
+    KVB_CHECK(pos0 + t <= max_seq, "kv_append: positions up to %zu exceed max_seq %zu", pos0 + t,
+              max_seq);
+    KVB_CHECK(fits_i32(pos0) && fits_i32(n_kv) && fits_i32(head_dim) && fits_i32(max_seq) &&
+                  fits_i32(n_q * head_dim) && fits_i32(stride) && fits_i32(t),
+              "kv_append: a dimension does not fit in i32");
+    if (t == 0) return KVB_OK;
+    RopeArgs a = rope_args(const_cast<void*>(qkv), n_q, n_kv, head_dim);
+    a.rows_per_seq = (int)t;
+    a.pos0 = (int)pos0;
+    a.kc = static_cast<uint16_t*>(kc);
+    a.vc = static_cast<uint16_t*>(vc);
+    a.seq_stride = 0;
+    a.max_seq = (int)max_seq;
+    a.do_append = 1;
+    const bool vec = head_dim % 16 == 0 && aligned(qkv, 16) && aligned(kc, 16) && aligned(vc, 16);
+    return launch_rope(stream, a, (int)t, dtype, vec);
+}
+
+int kvb_rope_kv_append(kvb_stream_t stream, void* qkv, size_t qkv_len, const float* cos_t,
+                       const float* sin_t, size_t table_len, void* kc, void* vc, size_t cache_len,
+                       size_t t, size_t pos0, size_t n_q, size_t n_kv, size_t head_dim,
+                       size_t max_seq, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    KVB_CHECK(head_dim > 0 && head_dim % 2 == 0, "rope: odd head_dim %zu", head_dim);
+    KVB_CHECK(qkv_len == t * stride, "rope_kv_append: qkv has %zu elems, want %zux%zu", qkv_len, t,
+              stride);
+    KVB_CHECK(table_len % (head_dim / 2) == 0, "rope: bad cos/sin table sizes");
+    const size_t max_pos = table_len / (head_dim / 2);
+    KVB_CHECK(pos0 + t <= max_pos, "rope: positions up to %zu exceed table of %zu", pos0 + t, max_pos);
+    KVB_CHECK(cache_len == n_kv * max_seq * head_dim, "kv_append: bad cache sizes");
+    KVB_CHECK(pos0 + t <= max_seq, "kv_append: positions up to %zu exceed max_seq %zu", pos0 + t,
+              max_seq);
+    KVB_CHECK(fits_i32(pos0) && fits_i32(stride) && fits_i32(t) && fits_i32(max_seq) &&
+                  fits_i32(max_pos),
+              "rope_kv_append: a dimension does not fit in i32");
+    if (t == 0) return KVB_OK;
+    RopeArgs a = rope_args(qkv, n_q, n_kv, head_dim);
+    a.rows_per_seq = (int)t;
+    a.pos0 = (int)pos0;
+    a.cos_t = cos_t;
+    a.sin_t = sin_t;
+    a.max_pos = (int)max_pos;
+    a.kc = static_cast<uint16_t*>(kc);
+    a.vc = static_cast<uint16_t*>(vc);
+    a.max_seq = (int)max_seq;
+    a.do_rope = 1;
+    a.do_append = 1;
+    const bool vec = head_dim % 16 == 0 && aligned(qkv, 16) && aligned(cos_t, 16) &&
+                     aligned(sin_t, 16) && aligned(kc, 16) && aligned(vc, 16);
+    return launch_rope(stream, a, (int)t, dtype, vec);
+}
+
+int kvb_rope_kv_append_batched(kvb_stream_t stream, void* qkv, size_t n_seq, const int32_t* pos,
+                               const float* cos_t, const float* sin_t, size_t table_len,
+                               void* kc, void* vc, size_t seq_stride, size_t cache_len,
+                               size_t n_q, size_t n_kv, size_t head_dim, size_t max_seq,
+                               int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    const size_t per_seq = n_kv * max_seq * head_dim;
+    KVB_CHECK(head_dim > 0 && head_dim % 2 == 0, "rope: odd head_dim %zu", head_dim);
+    KVB_CHECK(pos != nullptr, "rope_kv_append_batched: null position array");
+    KVB_CHECK(table_len % (head_dim / 2) == 0, "rope: bad cos/sin table sizes");
+    KVB_CHECK(seq_stride >= per_seq, "rope_kv_append_batched: seq_stride %zu < cache of %zu",
+              seq_stride, per_seq);
+    KVB_CHECK(n_seq == 0 || cache_len >= (n_seq - 1) * seq_stride + per_seq,
+              "rope_kv_append_batched: cache of %zu elems is too small", cache_len);
+    KVB_CHECK(fits_i32(n_seq) && fits_i32(stride) && fits_i32(max_seq) &&
+                  fits_i32(table_len / (head_dim / 2)),
+              "rope_kv_append_batched: a dimension does not fit in i32");
+    if (n_seq == 0) return KVB_OK;
+    RopeArgs a = rope_args(qkv, n_q, n_kv, head_dim);
+    a.rows_per_seq = 1;
+    a.pos_arr = pos;
+    a.cos_t = cos_t;
+    a.sin_t = sin_t;
+    a.max_pos = (int)(table_len / (head_dim / 2));
+    a.kc = static_cast<uint16_t*>(kc);
+    a.vc = static_cast<uint16_t*>(vc);
+    a.seq_stride = (long long)seq_stride;
+    a.max_seq = (int)max_seq;
+    a.do_rope = 1;
+    a.do_append = 1;
+    const bool vec = head_dim % 16 == 0 && seq_stride % 8 == 0 && aligned(qkv, 16) &&
+                     aligned(cos_t, 16) && aligned(sin_t, 16) && aligned(kc, 16) && aligned(vc, 16);
+    return launch_rope(stream, a, (int)n_seq, dtype, vec);
+}
+
+// ------------------------------------------------------------------ silu_mul
+int kvb_silu_mul(kvb_stream_t stream, const void* gu, size_t gu_len, void* out, size_t out_len,
+                 size_t t, size_t inter, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(gu_len == t * 2 * inter, "silu_mul: gu has %zu elems, want %zux%zu", gu_len, t,
+              2 * inter);
+    KVB_CHECK(out_len == t * inter, "silu_mul: out has %zu elems, want %zux%zu", out_len, t, inter);
+    KVB_CHECK(fits_i32(inter) && fits_i32(t), "silu_mul: a dimension does not fit in i32");
+    if (t == 0 || inter == 0) return KVB_OK;
+    const unsigned gy = (unsigned)(t < 65535 ? t : 65535);
+    if (inter % 8 == 0 && aligned(gu, 16) && aligned(out, 16)) {
+        const int chunks = (int)(inter / 8);
+        dim3 grid((unsigned)((chunks + 255) / 256), gy);
+        if (dtype == KVB_BF16)
+            silu_mul_vec_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>((const uint4*)gu, (uint4*)out,
+                                                                       chunks, (int)t);
+        else
+            silu_mul_vec_kernel<__half><<<grid, 256, 0, stream>>>((const uint4*)gu, (uint4*)out, chunks,
+                                                                (int)t);
+    } else {
+        dim3 grid((unsigned)((inter + 255) / 256 < 64 ? (inter + 255) / 256 : 64), gy);
+        if (dtype == KVB_BF16)
+            silu_mul_scalar_kernel<__nv_bfloat16><<<grid, 256, 0, stream>>>(
+                (const __nv_bfloat16*)gu, (__nv_bfloat16*)out, (int)inter, (int)t);
+        else
+            silu_mul_scalar_kernel<__half><<<grid, 256, 0, stream>>>((const __half*)gu, (__half*)out,
+                                                                   (int)inter, (int)t);
+    }
+    KVB_CHECK_LAUNCH("silu_mul launch");
+    return KVB_OK;
+}
+
+// ------------------------------------------------------------------ add_inplace
+int kvb_add_inplace(kvb_stream_t stream, void* x, size_t x_len, const void* y, size_t y_len,
+                    int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(x_len == y_len, "add: lengths differ (%zu vs %zu)", x_len, y_len);
+    if (x_len == 0) return KVB_OK;
+    if (x_len % 8 == 0 && aligned(x, 16) && aligned(y, 16)) {
+        const size_t nvec = x_len / 8;
+        if (dtype == KVB_BF16)
+            add_vec_kernel<__nv_bfloat16><<<grid_for(nvec, 256), 256, 0, stream>>>((uint4*)x,
+                                                                                  (const uint4*)y, nvec);
+        else
+            add_vec_kernel<__half><<<grid_for(nvec, 256), 256, 0, stream>>>((uint4*)x, (const uint4*)y,
+                                                                           nvec);
+    } else {
+        if (dtype == KVB_BF16)
+            add_scalar_kernel<__nv_bfloat16><<<grid_for(x_len, 256), 256, 0, stream>>>(
+                (__nv_bfloat16*)x, (const __nv_bfloat16*)y, x_len);
+        else
+            add_scalar_kernel<__half><<<grid_for(x_len, 256), 256, 0, stream>>>(
+                (__half*)x, (const __half*)y, x_len);
+    }
+    KVB_CHECK_LAUNCH("add launch");
+    return KVB_OK;
+}
+
+// ------------------------------------------------------------------ bf16 -> f16
+int kvb_bf16_to_f16(kvb_stream_t stream, const void* src, size_t src_len, void* dst,
+                    size_t dst_len, uint32_t* bad, size_t bad_len) {
+    KVB_CHECK(src_len == dst_len, "bf16_to_f16: lengths differ (%zu vs %zu)", src_len, dst_len);
+    KVB_CHECK(bad_len == 1, "bf16_to_f16: bad counter must hold exactly one u32");
+    if (src_len == 0) return KVB_OK;
+    bf16_to_f16_kernel<<<grid_for(src_len, 256), 256, 0, stream>>>((const __nv_bfloat16*)src,
+                                                                   (__half*)dst, src_len, bad);
+    KVB_CHECK_LAUNCH("bf16_to_f16 launch");
+    return KVB_OK;
+}
+
+// ------------------------------------------------------------------ attention
+size_t kvb_attention_workspace_bytes(size_t t, size_t pos0, size_t n_q, size_t n_kv,
+                                     size_t head_dim) {
+    if (t != 1 || head_dim != 64 || n_kv == 0) return 0;
+    return decode_ws_bytes(1, pos0 + 1, n_q, n_kv);
+}
+
+int kvb_attention(kvb_stream_t stream, const void* qkv, size_t qkv_len, const void* kc,
+                  size_t kc_len, const void* vc, size_t vc_len, void* out, size_t out_len,
+                  size_t t, size_t pos0, size_t n_q, size_t n_kv, size_t head_dim, size_t max_seq,
+                  void* workspace, size_t workspace_len, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    KVB_CHECK(n_kv > 0 && n_q % n_kv == 0, "attention: n_q %zu not a multiple of n_kv %zu", n_q, n_kv);
+    KVB_CHECK(head_dim > 0 && 128 % head_dim == 0, "attention: head_dim %zu must divide 128",
+              head_dim);
+    KVB_CHECK(qkv_len == t * stride, "attention: qkv has %zu elems, want %zux%zu", qkv_len, t, stride);
+    KVB_CHECK(kc_len == n_kv * max_seq * head_dim && vc_len == kc_len, "attention: bad cache sizes");
+    KVB_CHECK(out_len == t * n_q * head_dim, "attention: out has %zu elems, want %zux%zu", out_len, t,
+              n_q * head_dim);
+    KVB_CHECK(pos0 + t <= max_seq, "attention: kv length %zu exceeds max_seq %zu", pos0 + t, max_seq);
+    KVB_CHECK(fits_i32(pos0) && fits_i32(n_q) && fits_i32(n_kv) && fits_i32(head_dim) &&
+                  fits_i32(max_seq) && fits_i32(stride) && fits_i32(t),
+              "attention: a dimension does not fit in i32");
+    if (t == 0) return KVB_OK;
+    const size_t group = n_q / n_kv;
+    const float scale = 1.0f / sqrtf((float)head_dim);
+    const bool fast = head_dim == 64 && aligned(qkv, 16) && aligned(kc, 16) && aligned(vc, 16) &&
+                      aligned(out, 16) && fits_i32(n_kv * max_seq);
+    if (fast && t == 1 && group <= 16) {
+        DecodeLaunch L;
+        L.q = qkv;
+        L.q_row_stride = stride;
+        L.kc = kc;
+        L.vc = vc;
+        L.seq_stride = n_kv * max_seq * 64;
+        L.total_rows = n_kv * max_seq;
+        L.lens = nullptr;
+        L.len_const = (int)(pos0 + 1);
+        L.n_seq = 1;
+        L.max_len = pos0 + 1;
+        L.n_q = n_q;
+        L.n_kv = n_kv;
+        L.max_seq = max_seq;
+        L.scale = scale;
+        L.out = out;
+        L.out_row_stride = n_q * 64;
+        L.ws = workspace;
+        L.ws_len = workspace_len;
+        L.dtype = dtype;
+        return launch_decode_mma(stream, L);
+    }
+    if (fast && t > 1)
+        return launch_prefill(stream, qkv, kc, vc, out, 1, t, pos0, n_q, n_kv, max_seq, dtype);
+    GenericAttnArgs a;
+    a.q = static_cast<const uint16_t*>(qkv);
+    a.q_row_stride = (long long)stride;
+    a.kc = static_cast<const uint16_t*>(kc);
+    a.vc = static_cast<const uint16_t*>(vc);
+    a.seq_stride = 0;
+    a.rows_per_seq = (int)t;
+    a.lens = nullptr;
+    a.pos0 = (int)pos0;
+    a.max_len = (int)(pos0 + t);
+    a.n_q = (int)n_q;
+    a.n_kv = (int)n_kv;
+    a.hd = (int)head_dim;
+    a.max_seq = (int)max_seq;
+    a.scale = scale;
+    a.out = static_cast<uint16_t*>(out);
+    a.out_row_stride = (long long)(n_q * head_dim);
+    return launch_generic_attn(stream, a, t, dtype);
+}
+
+size_t kvb_attention_decode_workspace_bytes(size_t n_seq, size_t max_len, size_t n_q,
+                                            size_t n_kv, size_t head_dim) {
+    if (head_dim != 64 || n_kv == 0) return 0;
+    return decode_ws_bytes(n_seq, max_len, n_q, n_kv);
+}
+
+int kvb_attention_decode(kvb_stream_t stream, const void* q, size_t q_row_stride, const void* kc,
+                         const void* vc, size_t seq_stride, size_t cache_len,
+                         const int32_t* lens, size_t n_seq, size_t max_len, size_t n_q,
+                         size_t n_kv, size_t head_dim, size_t max_seq, float scale, void* out,
+                         size_t out_row_stride, void* workspace, size_t workspace_len,
+                         int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    const size_t per_seq = n_kv * max_seq * head_dim;
+    KVB_CHECK(n_kv > 0 && n_q % n_kv == 0, "attention_decode: n_q %zu not a multiple of n_kv %zu",
+              n_q, n_kv);
+    KVB_CHECK(head_dim > 0 && head_dim <= 256, "attention_decode: head_dim %zu unsupported",
+              head_dim);
+    KVB_CHECK(lens != nullptr, "attention_decode: null lengths array");
+    KVB_CHECK(max_len <= max_seq, "attention_decode: max_len %zu exceeds max_seq %zu", max_len,
+              max_seq);
+    KVB_CHECK(seq_stride >= per_seq, "attention_decode: seq_stride %zu < per-sequence cache %zu",
+              seq_stride, per_seq);
+    KVB_CHECK(n_seq == 0 || cache_len >= (n_seq - 1) * seq_stride + per_seq,
+              "attention_decode: cache of %zu elems is too small", cache_len);
+    KVB_CHECK(q_row_stride >= n_q * head_dim, "attention_decode: q_row_stride too small");
+    KVB_CHECK(out_row_stride >= n_q * head_dim, "attention_decode: out_row_stride too small");
+    KVB_CHECK(fits_i32(n_seq) && fits_i32(max_seq) && fits_i32(max_len),
+              "attention_decode: a dimension does not fit in i32");
+    if (n_seq == 0) return KVB_OK;
+    const size_t group = n_q / n_kv;
+    const size_t total_rows = n_seq == 0 ? 0 : ((n_seq - 1) * seq_stride + per_seq) / 64;
+    const bool fast = head_dim == 64 && group <= 16 && seq_stride % 64 == 0 && q_row_stride % 8 == 0 &&
+                      aligned(q, 16) && aligned(kc, 16) && aligned(vc, 16) && fits_i32(total_rows) &&
+                      total_rows < (1ull << 32);
+    if (fast) {
+        DecodeLaunch L;
+        L.q = q;
+        L.q_row_stride = q_row_stride;
+        L.kc = kc;
+        L.vc = vc;
+        L.seq_stride = seq_stride;
+        L.total_rows = total_rows;
+        L.lens = lens;
+        L.len_const = 0;
+        L.n_seq = n_seq;
+        L.max_len = max_len;
+        L.n_q = n_q;
+        L.n_kv = n_kv;
+        L.max_seq = max_seq;
+        L.scale = scale;
+        L.out = out;
+        L.out_row_stride = out_row_stride;
+        L.ws = workspace;
+        L.ws_len = workspace_len;
+        L.dtype = dtype;
+        return launch_decode_mma(stream, L);
+    }
+    GenericAttnArgs a;
+    a.q = static_cast<const uint16_t*>(q);
+    a.q_row_stride = (long long)q_row_stride;
+    a.kc = static_cast<const uint16_t*>(kc);
+    a.vc = static_cast<const uint16_t*>(vc);
+    a.seq_stride = (long long)seq_stride;
+    a.rows_per_seq = 1;
+    a.lens = lens;
+    a.pos0 = 0;
+    a.max_len = (int)max_len;
+    a.n_q = (int)n_q;
+    a.n_kv = (int)n_kv;
+    a.hd = (int)head_dim;
+    a.max_seq = (int)max_seq;
+    a.scale = scale;
+    a.out = static_cast<uint16_t*>(out);
+    a.out_row_stride = (long long)out_row_stride;
+    return launch_generic_attn(stream, a, n_seq, dtype);
+}
+
+int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, const void* kc, const void* vc,
+                          void* out, size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
+                          size_t head_dim, size_t max_seq, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(n_kv > 0 && n_q % n_kv == 0, "attention_prefill: n_q %zu not a multiple of n_kv %zu",
+              n_q, n_kv);
+    KVB_CHECK(head_dim > 0 && head_dim <= 256, "attention_prefill: head_dim %zu unsupported", head_dim);
+    KVB_CHECK(pos0 + t <= max_seq, "attention_prefill: kv length %zu exceeds max_seq %zu", pos0 + t,
+              max_seq);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    KVB_CHECK(fits_i32(n_seq * t) && fits_i32(pos0 + t) && fits_i32(stride) &&
+                  fits_i32(n_seq * n_kv),
+              "attention_prefill: a dimension does not fit in i32");
+    if (n_seq == 0 || t == 0) return KVB_OK;
+    const bool fast = head_dim == 64 && aligned(qkv, 16) && aligned(kc, 16) && aligned(vc, 16) &&
+                      aligned(out, 16);
+    if (fast) return launch_prefill(stream, qkv, kc, vc, out, n_seq, t, pos0, n_q, n_kv, max_seq, dtype);
+    GenericAttnArgs a;
+    a.q = static_cast<const uint16_t*>(qkv);
+    a.q_row_stride = (long long)stride;
+    a.kc = static_cast<const uint16_t*>(kc);
+    a.vc = static_cast<const uint16_t*>(vc);
+    a.seq_stride = (long long)(n_kv * max_seq * head_dim);
+    a.rows_per_seq = (int)t;
+    a.lens = nullptr;
+    a.pos0 = (int)pos0;
+    a.max_len = (int)(pos0 + t);
+    a.n_q = (int)n_q;
+    a.n_kv = (int)n_kv;
+    a.hd = (int)head_dim;
+    a.max_seq = (int)max_seq;
+    a.scale = 1.0f / sqrtf((float)head_dim);
+    a.out = static_cast<uint16_t*>(out);
+    a.out_row_stride = (long long)(n_q * head_dim);
+    return launch_generic_attn(stream, a, n_seq * t, dtype);
+}
+
+// ------------------------------------------------------------------ argmax
+int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
+                   int32_t* ids, int32_t* advance, int32_t* advance2) {
+    KVB_CHECK(vocab > 0 && fits_i32(vocab), "argmax: vocab %zu out of range", vocab);
+    KVB_CHECK(fits_i32(rows), "argmax: rows %zu out of range", rows);
+    if (rows == 0) return KVB_OK;
+    const int vec4 = vocab % 4 == 0 && aligned(logits, 16);
+    argmax_kernel<<<(unsigned)rows, 512, 0, stream>>>(logits, (int)vocab, ids, advance, advance2, vec4);
+    KVB_CHECK_LAUNCH("argmax launch");
+    return KVB_OK;
+}
+
+// ------------------------------------------------------------------ self test
+int kvb_selftest_wait_timeout(kvb_stream_t stream, uint32_t limit_ms) {
+    KVB_CHECK(limit_ms > 0 && limit_ms <= 10000, "selftest: limit %u ms out of range", limit_ms);
+    selftest_wait_kernel<<<1, 32, 0, stream>>>((uint64_t)limit_ms * 1000000ull);
+    KVB_CHECK_LAUNCH("selftest launch");
+    cudaError_t e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "selftest synchronize");
+    uint32_t code = 0;
+    int st = kvb_device_error(&code);
+    if (st) return st;
+    if (code & kDevErrSelfTest)
+        return fail(KVB_ERR_DEVICE, "bounded wait gave up after %u ms (device error word 0x%x)",
+                    limit_ms, code);
+    return fail(KVB_ERR_CUDA, "selftest: the wait completed although nothing arrived");
+}
+
+}  // extern "C"

@@ -1,0 +1,45 @@
+// kvb_host.h -- host-side helpers shared by the C-ABI translation units:
+// thread-local error messages, shape-check macros, device properties and
+// TMA tensor-map encoding.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/kvasir_b200.h"
+
+namespace kvb {
+
+// Records a message for kvb_last_error() and returns `status`.
+int fail(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
+int cuda_fail(cudaError_t e, const char* what);
+
+inline bool fits_i32(size_t x) { return x <= 0x7fffffffull; }
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+inline bool valid_dtype(int d) { return d == KVB_BF16 || d == KVB_F16; }
+
+// Streaming multiprocessors of the current device (cached per device).
+int num_sms();
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+// dims / box are innermost-first; strides_bytes has rank-1 entries (the
+// strides of dims 1..rank-1).  128-byte swizzle, zero fill out of bounds.
+int encode_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
+                const uint64_t* strides_bytes, const uint32_t* box, int dtype);
+
+}  // namespace kvb
+
+#define KVB_CHECK(cond, ...)                                         \
+    do {                                                             \
+        if (!(cond)) return ::kvb::fail(KVB_ERR_SHAPE, __VA_ARGS__); \
+    } while (0)
+
+#define KVB_CHECK_DTYPE(d) KVB_CHECK(::kvb::valid_dtype(d), "unknown dtype tag %d", (int)(d))
+
+#define KVB_CHECK_LAUNCH(what)                                      \
+    do {                                                            \
+        cudaError_t e_ = cudaGetLastError();                        \
+        if (e_ != cudaSuccess) return ::kvb::cuda_fail(e_, (what)); \
+    } while (0)

@@ -1,0 +1,156 @@
+// rope.cuh -- RoPE (rotate_half), KV-cache append, and the fused pass that
+// does both in one read of the qkv row.
+//
+// Reference kernels: engine/kernels/rope.cu:3-19 (one thread per (head, pair),
+// 2-byte loads) and engine/kernels/elementwise.cu:22-34 (kv_append, div/mod per
+// element).  Here one CTA owns one qkv row: each thread rotates 8 pairs of a
+// head with two 16-byte loads, the f32 cos/sin come in as float4s, and with
+// do_append the rotated k and the raw v chunks are also stored to the cache.
+// The rotation is x0*c - x1*s, x1*c + x0*s evaluated with explicitly
+// unfused f32 multiplies and adds, the exact f32 sequence of the reference
+// test (engine/tests/kernels.rs:121-132), then rounded once.
+#pragma once
+
+#include "kvb_common.cuh"
+
+namespace kvb {
+
+struct RopeArgs {
+    uint16_t* qkv;
+    int n_q, n_kv, hd, row_stride;
+    int rows_per_seq;        // rows of one sequence (T for a prefill call, 1 for batched decode)
+    const int32_t* pos_arr;  // per-sequence start position (device) or nullptr
+    int pos0;                // start position when pos_arr == nullptr
+    const float* cos_t;
+    const float* sin_t;
+    int max_pos;             // rows of the cos/sin table
+    uint16_t* kc;
+    uint16_t* vc;
+    long long seq_stride;    // elements between consecutive sequences' caches
+    int max_seq;
+    int do_rope, do_append;
+};
+
+__device__ __forceinline__ float rot_a(float x0, float x1, float c, float s) {
+    return __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+}
+__device__ __forceinline__ float rot_b(float x0, float x1, float c, float s) {
+    return __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
+}
+
+__device__ __forceinline__ bool rope_row_position(const RopeArgs& a, int row, int& seq, int& p) {
+    seq = row / a.rows_per_seq;
+    p = (a.pos_arr ? a.pos_arr[seq] : a.pos0) + row % a.rows_per_seq;
+    const bool bad = p < 0 || (a.do_rope && p >= a.max_pos) || (a.do_append && p >= a.max_seq);
+    if (bad && threadIdx.x == 0) raise_dev_error(kDevErrBadPosition);
+    return !bad;
+}
+
+// head_dim % 16 == 0 and 16-byte aligned rows.
+template <typename T>
+__global__ void __launch_bounds__(256) rope_append_vec_kernel(RopeArgs a) {
+    const int row = blockIdx.x;
+    int seq, p;
+    if (!rope_row_position(a, row, seq, p)) return;
+    const int half = a.hd >> 1;
+    const int cpr = a.hd >> 4;  // 8-pair chunks per head
+    const int n_rope = (a.n_q + a.n_kv) * cpr;
+    const int n_items = n_rope + a.n_kv * (a.hd >> 3);
+    uint16_t* rowp = a.qkv + (size_t)row * a.row_stride;
+    const size_t cache0 = (size_t)seq * a.seq_stride;
+    for (int it = threadIdx.x; it < n_items; it += blockDim.x) {
+        if (it < n_rope) {
+            const int h = it / cpr, j = it - h * cpr;
+            if (h < a.n_q && !a.do_rope) continue;
+            uint4* pa = reinterpret_cast<uint4*>(rowp + h * a.hd + 8 * j);
+            uint4* pb = reinterpret_cast<uint4*>(rowp + h * a.hd + 8 * j + half);
+            uint4 va = *pa, vb = *pb;
+            if (a.do_rope) {
+                float x0[8], x1[8];
+                unpack8<T>(va, x0);
+                unpack8<T>(vb, x1);
+                const float4* c4 = reinterpret_cast<const float4*>(a.cos_t + (size_t)p * half + 8 * j);
+                const float4* s4 = reinterpret_cast<const float4*>(a.sin_t + (size_t)p * half + 8 * j);
+                const float4 c0 = c4[0], c1 = c4[1], s0 = s4[0], s1 = s4[1];
+                const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+                const float s[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+                float ra[8], rb[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    ra[e] = rot_a(x0[e], x1[e], c[e], s[e]);
+                    rb[e] = rot_b(x0[e], x1[e], c[e], s[e]);
+                }
+                va = pack8<T>(ra);
+                vb = pack8<T>(rb);
+                *pa = va;
+                *pb = vb;
+            }
+            if (a.do_append && h >= a.n_q) {
+                const size_t dst = cache0 + ((size_t)(h - a.n_q) * a.max_seq + p) * a.hd;
+                *reinterpret_cast<uint4*>(a.kc + dst + 8 * j) = va;
+                *reinterpret_cast<uint4*>(a.kc + dst + 8 * j + half) = vb;
+            }
+        } else if (a.do_append) {
+            const int vi = it - n_rope;
+            const int per = a.hd >> 3;
+            const int kvh = vi / per, c = vi - kvh * per;
+            const uint4 v =
+                *reinterpret_cast<const uint4*>(rowp + (a.n_q + a.n_kv) * a.hd + kvh * a.hd + 8 * c);
+            const size_t dst = cache0 + ((size_t)kvh * a.max_seq + p) * a.hd;
+            *reinterpret_cast<uint4*>(a.vc + dst + 8 * c) = v;
+        }
+    }
+}
+
+// Any even head_dim, any alignment.
+template <typename T>
+__global__ void __launch_bounds__(256) rope_append_scalar_kernel(RopeArgs a) {
+    const int row = blockIdx.x;
+    int seq, p;
+    if (!rope_row_position(a, row, seq, p)) return;
+    const int half = a.hd >> 1;
+    T* rowp = reinterpret_cast<T*>(a.qkv) + (size_t)row * a.row_stride;
+    T* kc = reinterpret_cast<T*>(a.kc);
+    T* vc = reinterpret_cast<T*>(a.vc);
+    const size_t cache0 = (size_t)seq * a.seq_stride;
+    if (!a.do_rope) {  // plain kv_append: any head_dim, element copies
+        for (int it = threadIdx.x; it < 2 * a.n_kv * a.hd; it += blockDim.x) {
+            const int is_v = it >= a.n_kv * a.hd;
+            const int i = it - is_v * a.n_kv * a.hd;
+            const int kvh = i / a.hd, d = i - kvh * a.hd;
+            const size_t dst = cache0 + ((size_t)kvh * a.max_seq + p) * a.hd + d;
+            (is_v ? vc : kc)[dst] = rowp[(a.n_q + is_v * a.n_kv) * a.hd + i];
+        }
+        return;
+    }
+    const int n_rope = (a.n_q + a.n_kv) * half;
+    const int n_items = n_rope + a.n_kv * a.hd;
+    for (int it = threadIdx.x; it < n_items; it += blockDim.x) {
+        if (it < n_rope) {
+            const int h = it / half, j = it - h * half;
+            if (h < a.n_q && !a.do_rope) continue;
+            T* v = rowp + h * a.hd;
+            T ta = v[j], tb = v[j + half];
+            if (a.do_rope) {
+                const float x0 = Elem<T>::to_f(ta), x1 = Elem<T>::to_f(tb);
+                const float c = a.cos_t[(size_t)p * half + j], s = a.sin_t[(size_t)p * half + j];
+                ta = Elem<T>::from_f(rot_a(x0, x1, c, s));
+                tb = Elem<T>::from_f(rot_b(x0, x1, c, s));
+                v[j] = ta;
+                v[j + half] = tb;
+            }
+            if (a.do_append && h >= a.n_q) {
+                const size_t dst = cache0 + ((size_t)(h - a.n_q) * a.max_seq + p) * a.hd;
+                kc[dst + j] = ta;
+                kc[dst + j + half] = tb;
+            }
+        } else if (a.do_append) {
+            const int vi = it - n_rope;
+            const int kvh = vi / a.hd, d = vi - kvh * a.hd;
+            const size_t dst = cache0 + ((size_t)kvh * a.max_seq + p) * a.hd;
+            vc[dst + d] = rowp[(a.n_q + a.n_kv) * a.hd + kvh * a.hd + d];
+        }
+    }
+}
+
+}  // namespace kvb

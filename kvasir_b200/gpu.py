@@ -1,0 +1,233 @@
+"""Host mirror of the reference's GPU launch-wrapper API (engine/src/gpu).
+
+`Gpu` has one method per reference `impl Gpu` method
+(engine/src/gpu/kernels.rs:58-372) with the same argument order and meaning,
+plus `linear_f16` / `linear_f32` (engine/src/gpu/gemm.rs:63-115).  Buffers are
+CUDA torch tensors standing in for cudarc's CudaView (a device pointer plus an
+element count); every call goes through the C ABI of libkvasir_b200.so.  A
+failed shape check raises `ShapeError` (the reference's KvasirError::Shape)
+before anything is launched; launches are asynchronous on the Gpu's stream.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import torch
+
+from . import _lib as L
+
+
+class KvasirError(RuntimeError):
+    """Base error (reference engine/src/error.rs:3-19)."""
+
+
+class ShapeError(KvasirError):
+    pass
+
+
+class CudaError(KvasirError):
+    pass
+
+
+class UnsupportedError(KvasirError):
+    pass
+
+
+class DeviceError(KvasirError):
+    pass
+
+
+_ERRORS = {L.KVB_ERR_SHAPE: ShapeError, L.KVB_ERR_CUDA: CudaError,
+           L.KVB_ERR_UNSUPPORTED: UnsupportedError, L.KVB_ERR_DEVICE: DeviceError}
+
+
+def check(status: int) -> None:
+    if status != L.KVB_OK:
+        msg = L.lib().kvb_last_error().decode(errors="replace")
+        raise _ERRORS.get(status, KvasirError)(msg)
+
+
+def dtype_tag(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return L.KVB_BF16
+    if t.dtype == torch.float16:
+        return L.KVB_F16
+    raise ShapeError(f"unsupported element type {t.dtype} (bf16 or f16)")
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ShapeError("buffers must be CUDA tensors")
+    if not t.is_contiguous():
+        raise ShapeError("buffers must be contiguous")
+    return C.c_void_p(t.data_ptr())
+
+
+class Gpu:
+    """One device, one stream, one cuBLAS handle (reference device.rs:10-31)."""
+
+    def __init__(self, ordinal: int = 0, stream: torch.cuda.Stream | None = None):
+        self.device = torch.device("cuda", ordinal)
+        torch.cuda.set_device(self.device)
+        self.stream = stream if stream is not None else torch.cuda.current_stream(self.device)
+        self._lib = L.lib()
+        h = C.c_void_p()
+        check(self._lib.kvb_blas_create(C.byref(h)))
+        self._blas = h
+
+    @classmethod
+    def new(cls, ordinal: int = 0) -> "Gpu":
+        return cls(ordinal)
+
+    def __del__(self):
+        try:
+            if getattr(self, "_blas", None):
+                self._lib.kvb_blas_destroy(self._blas)
+                self._blas = None
+        except Exception:
+            pass
+
+    @property
+    def _s(self):
+        return C.c_void_p(self.stream.cuda_stream)
+
+    def synchronize(self) -> None:
+        self.stream.synchronize()
+
+    def device_error(self) -> int:
+        code = C.c_uint32()
+        check(self._lib.kvb_device_error(C.byref(code)))
+        return code.value
+
+    # ------------------------------------------------ reference kernels.rs methods
+    def embedding_gather(self, ids, table, out, hidden):
+        """kernels.rs:59-88"""
+        check(self._lib.kvb_embedding_gather(self._s, _ptr(ids), ids.numel(), _ptr(table),
+                                             table.numel(), _ptr(out), out.numel(), hidden,
+                                             dtype_tag(table)))
+
+    def rmsnorm(self, x, w, out, rows, hidden, eps):
+        """kernels.rs:90-121"""
+        check(self._lib.kvb_rmsnorm(self._s, _ptr(x), x.numel(), _ptr(w), w.numel(), _ptr(out),
+                                    out.numel(), rows, hidden, eps, dtype_tag(x)))
+
+    def rope_inplace(self, qkv, cos, sin, t, pos0, n_q, n_kv, head_dim):
+        """kernels.rs:124-169"""
+        check(self._lib.kvb_rope_inplace(self._s, _ptr(qkv), qkv.numel(), _ptr(cos), cos.numel(),
+                                         _ptr(sin), sin.numel(), t, pos0, n_q, n_kv, head_dim,
+                                         dtype_tag(qkv)))
+
+    def silu_mul(self, gu, out, t, inter):
+        """kernels.rs:171-194"""
+        check(self._lib.kvb_silu_mul(self._s, _ptr(gu), gu.numel(), _ptr(out), out.numel(), t,
+                                     inter, dtype_tag(gu)))
+
+    def add_inplace(self, x, y):
+        """kernels.rs:196-209"""
+        check(self._lib.kvb_add_inplace(self._s, _ptr(x), x.numel(), _ptr(y), y.numel(),
+                                        dtype_tag(x)))
+
+    def bf16_to_f16(self, src, dst, bad):
+        """kernels.rs:211-235"""
+        check(self._lib.kvb_bf16_to_f16(self._s, _ptr(src), src.numel(), _ptr(dst), dst.numel(),
+                                        _ptr(bad), bad.numel()))
+
+    def kv_append(self, qkv, kc, vc, t, pos0, n_q, n_kv, head_dim, max_seq):
+        """kernels.rs:238-291"""
+        check(self._lib.kvb_kv_append(self._s, _ptr(qkv), qkv.numel(), _ptr(kc), kc.numel(),
+                                      _ptr(vc), vc.numel(), t, pos0, n_q, n_kv, head_dim, max_seq,
+                                      dtype_tag(qkv)))
+
+    def attention(self, qkv, kc, vc, out, t, pos0, n_q, n_kv, head_dim, max_seq, workspace=None):
+        """kernels.rs:294-371.  `workspace` (optional, a uint8 CUDA tensor of
+        attention_workspace_bytes(...)) lets a long decode split across CTAs."""
+        ws_len = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        check(self._lib.kvb_attention(self._s, _ptr(qkv), qkv.numel(), _ptr(kc), kc.numel(),
+                                      _ptr(vc), vc.numel(), _ptr(out), out.numel(), t, pos0, n_q,
+                                      n_kv, head_dim, max_seq, _ptr(workspace), ws_len,
+                                      dtype_tag(qkv)))
+
+    def attention_workspace_bytes(self, t, pos0, n_q, n_kv, head_dim) -> int:
+        return int(self._lib.kvb_attention_workspace_bytes(t, pos0, n_q, n_kv, head_dim))
+
+    # ------------------------------------------------ reference gemm.rs
+    def linear_f16(self, x, w, y, t, in_dim, out_dim):
+        """gemm.rs:63-88 (16-bit output; bf16 or f16 by the tensors' type)"""
+        check(self._lib.kvb_linear(self._blas, self._s, _ptr(x), x.numel(), _ptr(w), w.numel(),
+                                   _ptr(y), y.numel(), t, in_dim, out_dim, dtype_tag(x), 0))
+
+    def linear_f32(self, x, w, y, t, in_dim, out_dim):
+        """gemm.rs:90-115 (f32 output)"""
+        if y.dtype != torch.float32:
+            raise ShapeError("linear_f32: y must be float32")
+        check(self._lib.kvb_linear(self._blas, self._s, _ptr(x), x.numel(), _ptr(w), w.numel(),
+                                   _ptr(y), y.numel(), t, in_dim, out_dim, dtype_tag(x), 1))
+
+    # ------------------------------------------------ fused / batched additions
+    def rope_kv_append(self, qkv, cos, sin, kc, vc, t, pos0, n_q, n_kv, head_dim, max_seq):
+        if cos.numel() != sin.numel():
+            raise ShapeError("rope: bad cos/sin table sizes")
+        if kc.numel() != vc.numel():
+            raise ShapeError("kv_append: bad cache sizes")
+        check(self._lib.kvb_rope_kv_append(self._s, _ptr(qkv), qkv.numel(), _ptr(cos), _ptr(sin),
+                                           cos.numel(), _ptr(kc), _ptr(vc), kc.numel(), t, pos0,
+                                           n_q, n_kv, head_dim, max_seq, dtype_tag(qkv)))
+
+    def rope_kv_append_batched(self, qkv, pos, cos, sin, kc, vc, seq_stride, n_q, n_kv, head_dim,
+                               max_seq):
+        if pos.dtype != torch.int32:
+            raise ShapeError("positions must be int32")
+        check(self._lib.kvb_rope_kv_append_batched(
+            self._s, _ptr(qkv), pos.numel(), _ptr(pos), _ptr(cos), _ptr(sin), cos.numel(),
+            _ptr(kc), _ptr(vc), seq_stride, kc.numel(), n_q, n_kv, head_dim, max_seq,
+            dtype_tag(qkv)))
+
+    def add_rmsnorm(self, x, y, w, out, rows, hidden, eps):
+        for t, n in ((x, rows * hidden), (y, rows * hidden), (w, hidden), (out, rows * hidden)):
+            if t.numel() != n:
+                raise ShapeError(f"add_rmsnorm: buffer has {t.numel()} elems, want {n}")
+        check(self._lib.kvb_add_rmsnorm(self._s, _ptr(x), _ptr(y), _ptr(w), _ptr(out), rows,
+                                        hidden, eps, dtype_tag(x)))
+
+    def attention_decode_workspace_bytes(self, n_seq, max_len, n_q, n_kv, head_dim) -> int:
+        return int(self._lib.kvb_attention_decode_workspace_bytes(n_seq, max_len, n_q, n_kv,
+                                                                  head_dim))
+
+    def attention_decode(self, q, q_row_stride, kc, vc, seq_stride, lens, max_len, n_q, n_kv,
+                         head_dim, max_seq, out, out_row_stride, scale=None, workspace=None):
+        if lens.dtype != torch.int32:
+            raise ShapeError("lengths must be int32")
+        scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
+        ws_len = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        check(self._lib.kvb_attention_decode(
+            self._s, _ptr(q), q_row_stride, _ptr(kc), _ptr(vc), seq_stride, kc.numel(),
+            _ptr(lens), lens.numel(), max_len, n_q, n_kv, head_dim, max_seq, scale, _ptr(out),
+            out_row_stride, _ptr(workspace), ws_len, dtype_tag(q)))
+
+    def attention_prefill(self, qkv, kc, vc, out, n_seq, t, pos0, n_q, n_kv, head_dim, max_seq):
+        stride = (n_q + 2 * n_kv) * head_dim
+        if qkv.numel() != n_seq * t * stride:
+            raise ShapeError(f"attention_prefill: qkv has {qkv.numel()} elems, "
+                             f"want {n_seq * t}x{stride}")
+        if kc.numel() != n_seq * n_kv * max_seq * head_dim or vc.numel() != kc.numel():
+            raise ShapeError("attention_prefill: bad cache sizes")
+        if out.numel() != n_seq * t * n_q * head_dim:
+            raise ShapeError("attention_prefill: bad output size")
+        check(self._lib.kvb_attention_prefill(self._s, _ptr(qkv), _ptr(kc), _ptr(vc), _ptr(out),
+                                              n_seq, t, pos0, n_q, n_kv, head_dim, max_seq,
+                                              dtype_tag(qkv)))
+
+    def argmax(self, logits, rows, vocab, ids, advance=None, advance2=None):
+        if logits.dtype != torch.float32 or ids.dtype != torch.int32:
+            raise ShapeError("argmax: f32 logits and int32 ids expected")
+        if logits.numel() != rows * vocab or ids.numel() != rows:
+            raise ShapeError("argmax: bad sizes")
+        check(self._lib.kvb_argmax_f32(self._s, _ptr(logits), rows, vocab, _ptr(ids),
+                                       _ptr(advance), _ptr(advance2)))
+
+    def selftest_wait_timeout(self, limit_ms: int) -> int:
+        """Runs the bounded-wait self test; returns the status code."""
+        return int(self._lib.kvb_selftest_wait_timeout(self._s, limit_ms))

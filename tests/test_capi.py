@@ -1,0 +1,79 @@
+"""The C-ABI library: it loads without a GPU, exports every function the
+header declares, the Python binding knows every one of them, and the argument
+checks (reference ensure_shape!, engine/src/error.rs:23-30) reject bad shapes
+before anything touches the device."""
+import ctypes as C
+
+import numpy as np
+import pytest
+
+from kvasir_b200 import _lib as L
+from oracle import oracle as O
+
+
+def test_library_exports_every_header_symbol():
+    lib = L.lib()
+    declared = L.header_symbols()
+    assert len(declared) >= 30
+    missing = [s for s in declared if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_binding_covers_header():
+    assert sorted(L.SIGNATURES) == L.header_symbols()
+
+
+def _status(fn, *args):
+    st = fn(*args)
+    msg = L.lib().kvb_last_error().decode()
+    return st, msg
+
+
+def test_shape_errors_are_reported_not_launched():
+    """engine/tests/kernels.rs:366-374: a bad length is an error, not a panic."""
+    lib = L.lib()
+    fake = C.c_void_p(0x1000)  # never dereferenced: the checks fail first
+    st, msg = _status(lib.kvb_rmsnorm, None, fake, 10, fake, 10, fake, 10, 2, 4, 1e-5, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "rmsnorm" in msg
+    st, msg = _status(lib.kvb_add_inplace, None, fake, 10, fake, 5, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "lengths differ (10 vs 5)" in msg
+    st, msg = _status(lib.kvb_linear, fake, None, fake, 10, fake, 10, fake, 10, 2, 4, 3,
+                      L.KVB_BF16, 0)
+    assert st == L.KVB_ERR_SHAPE and "linear" in msg
+    st, msg = _status(lib.kvb_attention, None, fake, 12 * 64, fake, 2 * 16 * 64, fake,
+                      2 * 16 * 64, fake, 8 * 64, 1, 20, 8, 2, 64, 16, None, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "max_seq" in msg
+    st, msg = _status(lib.kvb_attention, None, fake, 12 * 48, fake, 2 * 16 * 48, fake,
+                      2 * 16 * 48, fake, 8 * 48, 1, 0, 8, 2, 48, 16, None, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "divide 128" in msg
+    st, msg = _status(lib.kvb_rope_inplace, None, fake, 5 * 768, fake, 32 * 32, fake, 32 * 32, 5,
+                      30, 8, 2, 64, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "exceed table" in msg
+    st, msg = _status(lib.kvb_kv_append, None, fake, 3 * 512, fake, 2 * 16 * 64, fake, 2 * 16 * 64,
+                      3, 14, 4, 2, 64, 16, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "max_seq" in msg
+    st, msg = _status(lib.kvb_bf16_to_f16, None, fake, 10, fake, 10, fake, 2)
+    assert st == L.KVB_ERR_SHAPE and "exactly one u32" in msg
+    st, msg = _status(lib.kvb_embedding_gather, None, fake, 5, fake, 301, fake, 5 * 300, 300,
+                      L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "multiple of hidden" in msg
+    st, msg = _status(lib.kvb_silu_mul, None, fake, 3 * 2000, fake, 3 * 999, 3, 1000, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "silu_mul" in msg
+    st, msg = _status(lib.kvb_rmsnorm, None, fake, 8, fake, 4, fake, 8, 2, 4, 1e-5, 7)
+    assert st == L.KVB_ERR_SHAPE and "dtype" in msg
+
+
+@pytest.mark.parametrize("scaled", [True, False])
+def test_rope_table_matches_oracle_bitwise(scaled):
+    """kvb_rope_table (product, engine/src/model/rope.rs:3-39) and the oracle's
+    restatement evaluate the same f64 formula with the same libm."""
+    lib = L.lib()
+    max_pos, hd = 2048, 64
+    c = np.empty(max_pos * 32, np.float32)
+    s = np.empty(max_pos * 32, np.float32)
+    st = lib.kvb_rope_table(hd, 500000.0, int(scaled), 32.0, 1.0, 4.0, 8192.0, max_pos,
+                            c.ctypes.data_as(C.c_void_p), s.ctypes.data_as(C.c_void_p))
+    assert st == L.KVB_OK
+    oc, os_ = O.cos_sin_table(hd, max_pos, 500000.0, scaled)
+    np.testing.assert_array_equal(c, oc)
+    np.testing.assert_array_equal(s, os_)

@@ -1,0 +1,231 @@
+"""Parity of the attention kernels against the CPU oracle (f64 softmax
+attention, engine/tests/kernels.rs:264-289), through the C ABI.
+
+Tolerance: |got - want| <= 2e-3 + 2^-8 |want| -- the 2e-3 max-abs bar for
+unit-scale inputs plus one rounding of the 16-bit output itself.  The f16
+runs also meet the reference's own bound (rtol 2e-3, atol 1e-3)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import assert_close, dev, host_f32, normal16
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-3, 2.0 ** -8
+
+
+@pytest.fixture(scope="module")
+def g():
+    from kvasir_b200 import Gpu
+    return Gpu(0)
+
+
+def _ref_inputs(rng, n_q, n_kv, hd, t, max_seq, dtype, amp=2.0):
+    stride = (n_q + 2 * n_kv) * hd
+    qkv = O.uniform16(rng, t * stride, amp, dtype)
+    kc = O.uniform16(rng, n_kv * max_seq * hd, amp, dtype)
+    vc = O.uniform16(rng, n_kv * max_seq * hd, amp, dtype)
+    return qkv, kc, vc
+
+
+# The reference's five attention cases (engine/tests/kernels.rs:293-316)
+REF_CASES = [(8, 2, 64, 7, 0, 32), (8, 2, 64, 1, 12, 32), (8, 2, 64, 4, 5, 32),
+             (32, 8, 64, 3, 397, 512), (4, 2, 128, 2, 20, 64)]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("case", REF_CASES)
+def test_attention_reference_cases(g, dtype, case):
+    n_q, n_kv, hd, t, pos0, max_seq = case
+    rng = np.random.default_rng(100 + t * 31 + pos0)
+    qkv, kc, vc = _ref_inputs(rng, n_q, n_kv, hd, t, max_seq, dtype)
+    out = torch.empty(t * n_q * hd, dtype=dev(qkv, dtype).dtype, device="cuda")
+    g.attention(dev(qkv, dtype), dev(kc, dtype), dev(vc, dtype), out, t, pos0, n_q, n_kv, hd,
+                max_seq)
+    want = O.attention(qkv, kc, vc, t, pos0, n_q, n_kv, hd, max_seq, dtype)
+    got = host_f32(out, dtype)
+    assert_close(got, want, RTOL, ATOL, f"attention{case}")
+    if dtype == "f16":
+        assert_close(got, want, 2e-3, 1e-3, f"attention{case}")
+
+
+@pytest.mark.parametrize("pos0", [0, 63, 64, 255, 256, 511, 4095, 16383])
+def test_attention_decode_single_sequence_split_and_unsplit(g, pos0):
+    """T = 1 through the reference API, without and with a split-KV workspace."""
+    n_q, n_kv, hd = 32, 8, 64
+    max_seq = pos0 + 1
+    rng = np.random.default_rng(pos0)
+    stride = (n_q + 2 * n_kv) * hd
+    qkv = normal16(rng, stride)
+    kc, vc = normal16(rng, n_kv * max_seq * hd), normal16(rng, n_kv * max_seq * hd)
+    want = O.attention(qkv, kc, vc, 1, pos0, n_q, n_kv, hd, max_seq)
+    out = torch.empty(n_q * hd, dtype=torch.bfloat16, device="cuda")
+    g.attention(dev(qkv), dev(kc), dev(vc), out, 1, pos0, n_q, n_kv, hd, max_seq)
+    a = host_f32(out)
+    assert_close(a, want, RTOL, ATOL, "decode/no-split")
+    nbytes = g.attention_workspace_bytes(1, pos0, n_q, n_kv, hd)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device="cuda")
+    g.attention(dev(qkv), dev(kc), dev(vc), out, 1, pos0, n_q, n_kv, hd, max_seq, workspace=ws)
+    assert_close(host_f32(out), want, RTOL, ATOL, "decode/split")
+
+
+def _batched_case(rng, lens, n_q=32, n_kv=8, hd=64, max_seq=None):
+    n_seq = len(lens)
+    max_seq = max_seq or max(max(lens), 1)
+    q = normal16(rng, n_seq * n_q * hd)
+    per = n_kv * max_seq * hd
+    kc, vc = normal16(rng, n_seq * per), normal16(rng, n_seq * per)
+    return q, kc, vc, max_seq, per
+
+
+def _run_batched(g, q, kc, vc, lens, n_q, n_kv, hd, max_seq, per, use_ws=True, dtype="bf16"):
+    n_seq = len(lens)
+    out = torch.empty(n_seq * n_q * hd, dtype=torch.bfloat16 if dtype == "bf16" else torch.float16,
+                      device="cuda")
+    max_len = int(max(lens)) if len(lens) else 0
+    nbytes = g.attention_decode_workspace_bytes(n_seq, max_len, n_q, n_kv, hd)
+    ws = torch.empty(max(nbytes, 16), dtype=torch.uint8, device="cuda") if use_ws else None
+    g.attention_decode(dev(q, dtype), n_q * hd, dev(kc, dtype), dev(vc, dtype), per,
+                       torch.tensor(lens, dtype=torch.int32, device="cuda"), max_len, n_q, n_kv,
+                       hd, max_seq, out, n_q * hd, workspace=ws)
+    return host_f32(out, dtype)
+
+
+def test_batched_decode_config2(g):
+    """64 sequences, lengths U[1, 4096], 32/8 heads, hd 64,
+    N(0,1) Q/K/V, scale 1/8."""
+    rng = np.random.default_rng(2026)
+    lens = rng.integers(1, 4097, 64).astype(np.int32)
+    n_q, n_kv, hd = 32, 8, 64
+    q, kc, vc, max_seq, per = _batched_case(rng, lens, max_seq=4096)
+    got = _run_batched(g, q, kc, vc, lens, n_q, n_kv, hd, max_seq, per)
+    O.set_threads(8)
+    want = O.attention_decode(q, n_q * hd, kc, vc, lens, n_q, n_kv, hd, max_seq, 1 / 8.0)
+    O.set_threads(1)
+    assert_close(got, want, RTOL, ATOL, "decode config 2")
+    assert g.device_error() == 0
+
+
+def test_batched_decode_edge_lengths(g):
+    """Empty sequence (zero row), single key, tile and chunk boundaries."""
+    lens = np.array([0, 1, 2, 63, 64, 65, 255, 256, 257, 1000, 1023, 1024, 1025, 4096], np.int32)
+    n_q, n_kv, hd = 32, 8, 64
+    rng = np.random.default_rng(7)
+    q, kc, vc, max_seq, per = _batched_case(rng, lens, max_seq=4096)
+    want = O.attention_decode(q, n_q * hd, kc, vc, lens, n_q, n_kv, hd, max_seq, 1 / 8.0)
+    want = want.reshape(len(lens), -1)
+    want[0] = 0.0  # no keys: zero row by definition
+    for use_ws in (True, False):
+        got = _run_batched(g, q, kc, vc, lens, n_q, n_kv, hd, max_seq, per, use_ws=use_ws)
+        assert_close(got, want, RTOL, ATOL, f"decode edges ws={use_ws}")
+
+
+@pytest.mark.parametrize("group", [1, 2, 8, 16])
+def test_batched_decode_group_sizes(g, group):
+    n_kv, hd = 2, 64
+    n_q = n_kv * group
+    lens = np.array([5, 300, 129], np.int32)
+    rng = np.random.default_rng(group)
+    q, kc, vc, max_seq, per = _batched_case(rng, lens, n_q=n_q, n_kv=n_kv, max_seq=320)
+    got = _run_batched(g, q, kc, vc, lens, n_q, n_kv, hd, max_seq, per)
+    want = O.attention_decode(q, n_q * hd, kc, vc, lens, n_q, n_kv, hd, max_seq, 1 / 8.0)
+    assert_close(got, want, RTOL, ATOL, f"decode group {group}")
+
+
+def test_batched_decode_general_kernel_head_dim_32(g):
+    n_q, n_kv, hd = 8, 2, 32
+    lens = np.array([1, 33, 100], np.int32)
+    rng = np.random.default_rng(5)
+    q, kc, vc, max_seq, per = _batched_case(rng, lens, n_q=n_q, n_kv=n_kv, hd=hd, max_seq=100)
+    got = _run_batched(g, q, kc, vc, lens, n_q, n_kv, hd, max_seq, per)
+    want = O.attention_decode(q, n_q * hd, kc, vc, lens, n_q, n_kv, hd, max_seq,
+                              1 / math.sqrt(hd))
+    assert_close(got, want, RTOL, ATOL, "decode hd 32")
+
+
+def test_batched_decode_f16(g):
+    lens = np.array([17, 1000, 64], np.int32)
+    rng = np.random.default_rng(9)
+    q, kc, vc, max_seq, per = _batched_case(rng, lens, max_seq=1024)
+    q, kc, vc = (O.from_f32(O.to_f32(a), "f16") for a in (q, kc, vc))
+    got = _run_batched(g, q, kc, vc, lens, 32, 8, 64, max_seq, per, dtype="f16")
+    want = O.attention_decode(q, 32 * 64, kc, vc, lens, 32, 8, 64, max_seq, 1 / 8.0, "f16")
+    assert_close(got, want, 2e-3, 1e-3, "decode f16")
+
+
+@pytest.mark.parametrize("t,pos0", [(7, 0), (4, 5), (128, 0), (129, 0), (300, 17), (1000, 0)])
+def test_prefill_tcgen05_against_oracle(g, t, pos0):
+    """Causal prefill through the reference API (T > 1, head_dim 64)."""
+    n_q, n_kv, hd = 8, 2, 64
+    max_seq = pos0 + t
+    rng = np.random.default_rng(t * 7 + pos0)
+    stride = (n_q + 2 * n_kv) * hd
+    qkv = normal16(rng, t * stride)
+    kc, vc = normal16(rng, n_kv * max_seq * hd), normal16(rng, n_kv * max_seq * hd)
+    out = torch.empty(t * n_q * hd, dtype=torch.bfloat16, device="cuda")
+    g.attention(dev(qkv), dev(kc), dev(vc), out, t, pos0, n_q, n_kv, hd, max_seq)
+    O.set_threads(8)
+    want = O.attention(qkv, kc, vc, t, pos0, n_q, n_kv, hd, max_seq)
+    O.set_threads(1)
+    assert_close(host_f32(out), want, RTOL, ATOL, f"prefill t={t} pos0={pos0}")
+    assert g.device_error() == 0
+
+
+def test_prefill_config3_shape(g):
+    """4 sequences x 2048 tokens, 32/8 heads, hd 64, N(0,1),
+    empty cache filled by the fused RoPE + KV append.  The oracle checks
+    sequences 0 and 3 on kv head 0 and 7 (its f64 cost is ~68 GFLOP for all)."""
+    n_seq, t, n_q, n_kv, hd = 4, 2048, 32, 8, 64
+    rng = np.random.default_rng(33)
+    stride = (n_q + 2 * n_kv) * hd
+    qkv = normal16(rng, n_seq * t * stride)
+    per = n_kv * t * hd
+    kc, vc = normal16(rng, n_seq * per), normal16(rng, n_seq * per)
+    out = torch.empty(n_seq * t * n_q * hd, dtype=torch.bfloat16, device="cuda")
+    g.attention_prefill(dev(qkv), dev(kc), dev(vc), out, n_seq, t, 0, n_q, n_kv, hd, t)
+    got = host_f32(out).reshape(n_seq, t, n_q, hd)
+    q4 = qkv.reshape(n_seq, t, n_q + 2 * n_kv, hd)
+    O.set_threads(8)
+    for seq in (0, 3):
+        for kvh in (0, 7):
+            heads = list(range(kvh * 4, kvh * 4 + 4))
+            sub = np.concatenate([q4[seq][:, heads], q4[seq][:, n_q + kvh:n_q + kvh + 1],
+                                  q4[seq][:, n_q + n_kv + kvh:n_q + n_kv + kvh + 1]], axis=1)
+            kk = kc.reshape(n_seq, n_kv, t, hd)[seq, kvh:kvh + 1]
+            vv = vc.reshape(n_seq, n_kv, t, hd)[seq, kvh:kvh + 1]
+            want = O.attention(sub, kk, vv, t, 0, 4, 1, hd, t).reshape(t, 4, hd)
+            assert_close(got[seq][:, heads], want, RTOL, ATOL, f"prefill seq {seq} kvh {kvh}")
+    O.set_threads(1)
+
+
+def test_prefill_rows_are_prefix_consistent(g):
+    """Size-independent property at full length: causal row i only depends on
+    tokens <= i, so a prefill of the first 1000 tokens reproduces the first
+    1000 rows of a 2048-token prefill bit for bit."""
+    n_q, n_kv, hd, t = 32, 8, 64, 2048
+    rng = np.random.default_rng(44)
+    stride = (n_q + 2 * n_kv) * hd
+    qkv = normal16(rng, t * stride)
+    kc, vc = normal16(rng, n_kv * t * hd), normal16(rng, n_kv * t * hd)
+    full = torch.empty(t * n_q * hd, dtype=torch.bfloat16, device="cuda")
+    g.attention(dev(qkv), dev(kc), dev(vc), full, t, 0, n_q, n_kv, hd, t)
+    k = 1024
+    part = torch.empty(k * n_q * hd, dtype=torch.bfloat16, device="cuda")
+    g.attention(dev(qkv[:k * stride]), dev(kc), dev(vc), part, k, 0, n_q, n_kv, hd, t)
+    assert torch.equal(full[:k * n_q * hd], part)
+
+
+def test_bounded_wait_selftest_keeps_context_usable(g):
+    """A device-side wait on a barrier nobody completes gives up after its
+    limit and reports KVB_ERR_DEVICE; later launches still work."""
+    from kvasir_b200 import _lib as L
+    st = g.selftest_wait_timeout(50)
+    assert st == L.KVB_ERR_DEVICE
+    assert g.device_error() == 0  # the self test read and cleared the word
+    x = torch.ones(16, dtype=torch.bfloat16, device="cuda")
+    g.add_inplace(x, x)
+    assert float(x[0]) == 2.0

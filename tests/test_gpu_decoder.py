@@ -1,0 +1,120 @@
+"""The decode-step driver (kvb_decoder_*) against the oracle's composed decode
+step on a small Llama-shaped model: same weights, same prefilled KV cache,
+several greedy steps.  Logits agree to within the bf16 activation rounding
+that the two accumulation orders (cuBLAS f32 vs oracle f64) can flip;
+greedy ids must agree wherever the oracle's top-2 margin is clear."""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import dev, host_bits
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _tiny_cfg():
+    from kvasir_b200.config import LlamaConfig
+    return LlamaConfig(hidden_size=256, intermediate_size=512, num_layers=2, num_heads=4,
+                       num_kv_heads=1, head_dim=64, vocab_size=1000, rms_norm_eps=1e-5,
+                       rope_theta=500000.0, max_position_embeddings=4096)
+
+
+def _weights_bits(rng, cfg):
+    h, i = cfg.hidden_size, cfg.intermediate_size
+    n = lambda k, s=0.05: O.from_f32(rng.normal(0, s, k).astype(np.float32))
+    one = lambda: O.from_f32((1 + 0.02 * rng.normal(0, 1, h)).astype(np.float32))
+    L = cfg.num_layers
+    return dict(embed=n(cfg.vocab_size * h, 0.5), final_norm=one(),
+                attn_norm=[one() for _ in range(L)], mlp_norm=[one() for _ in range(L)],
+                w_qkv=[n(cfg.qkv_dim * h) for _ in range(L)], w_o=[n(h * cfg.q_dim) for _ in range(L)],
+                w_gu=[n(2 * i * h) for _ in range(L)], w_down=[n(h * i) for _ in range(L)])
+
+
+def _to_torch(wb, cfg):
+    h, i = cfg.hidden_size, cfg.intermediate_size
+    t = lambda b, *shape: dev(b).view(*shape)
+    return dict(embed=t(wb["embed"], cfg.vocab_size, h), final_norm=t(wb["final_norm"], h),
+                attn_norm=[t(b, h) for b in wb["attn_norm"]],
+                mlp_norm=[t(b, h) for b in wb["mlp_norm"]],
+                w_qkv=[t(b, cfg.qkv_dim, h) for b in wb["w_qkv"]],
+                w_o=[t(b, h, cfg.q_dim) for b in wb["w_o"]],
+                w_gu=[t(b, 2 * i, h) for b in wb["w_gu"]],
+                w_down=[t(b, h, i) for b in wb["w_down"]])
+
+
+def test_decoder_matches_oracle_steps():
+    from kvasir_b200.decoder import Decoder
+    from kvasir_b200.rope import cos_sin_table
+    cfg = _tiny_cfg()
+    rng = np.random.default_rng(21)
+    n_seq, max_seq = 3, 96
+    wb = _weights_bits(rng, cfg)
+    dec = Decoder(cfg, n_seq, max_seq, weights=_to_torch(wb, cfg))
+    L, nkv, hd = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim
+    # prefilled context: random K/V at positions < cur_len
+    cur = np.array([5, 40, 64], np.int32)
+    kv_shape = (L, n_seq, nkv, max_seq, hd)
+    kc = O.from_f32(rng.normal(0, 1, int(np.prod(kv_shape))).astype(np.float32)).reshape(kv_shape)
+    vc = O.from_f32(rng.normal(0, 1, int(np.prod(kv_shape))).astype(np.float32)).reshape(kv_shape)
+    dec.kc.copy_(dev(kc).view(kv_shape))
+    dec.vc.copy_(dev(vc).view(kv_shape))
+    dec.set_lengths(cur)
+    ids = np.array([3, 500, 999], np.int32)
+    dec.ids_in.copy_(torch.from_numpy(ids).cuda())
+    # oracle state, cache layout [seq][layer][...]
+    okc = np.ascontiguousarray(kc.transpose(1, 0, 2, 3, 4))
+    ovc = np.ascontiguousarray(vc.transpose(1, 0, 2, 3, 4))
+    cos, sin = cos_sin_table(cfg, max_seq)
+    dims = dict(hidden=cfg.hidden_size, inter=cfg.intermediate_size, n_layers=L, n_q=cfg.num_heads,
+                n_kv=nkv, head_dim=hd, vocab=cfg.vocab_size, max_seq=max_seq, eps=cfg.rms_norm_eps)
+    pos = cur.copy()
+    for step in range(4):
+        dec.step()
+        torch.cuda.synchronize()
+        logits_want, ids_want = O.decode_step(dims, wb, cos, sin, okc, ovc, ids, pos)
+        got = dec.logits.cpu().numpy()
+        scale = np.abs(logits_want).max()
+        assert np.abs(got - logits_want).max() <= 0.03 * scale + 0.02, f"step {step}"
+        got_ids = dec.ids_out.cpu().numpy()
+        top2 = np.sort(logits_want, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 0.1 * scale
+        np.testing.assert_array_equal(got_ids[clear], ids_want[clear])
+        # the cache slot of this step holds the rotated K / raw V of the new token
+        new_k = host_bits(dec.kc).reshape(kv_shape)
+        for b in range(n_seq):
+            assert new_k[:, b, :, pos[b]].any()
+        ids = got_ids.astype(np.int32)  # continue from the GPU's choice (drivers diverge otherwise)
+        pos = pos + 1
+    own, lib = dec.launches_per_step()
+    assert own > 0 and lib == 4 * L + 1
+    dec.close()
+
+
+def test_decoder_step_host_equals_device_step():
+    from kvasir_b200.decoder import Decoder
+    cfg = _tiny_cfg()
+    n_seq, max_seq = 4, 64
+    a = Decoder(cfg, n_seq, max_seq, seed=5)
+    b = Decoder(cfg, n_seq, max_seq, weights=a.w)
+    for d in (a, b):
+        d.kc.copy_(a.kc.normal_(0, 1) if d is a else a.kc)
+        d.vc.copy_(a.vc.normal_(0, 1) if d is a else a.vc)
+        d.set_lengths([10, 11, 12, 13])
+    ids = torch.tensor([1, 2, 3, 4], dtype=torch.int32)
+    a.ids_in.copy_(ids.cuda())
+    outs_dev = []
+    for _ in range(3):
+        a.step()
+        outs_dev.append(a.ids_out.cpu().clone())
+    host_in = ids.clone().pin_memory()
+    host_out = torch.empty(n_seq, dtype=torch.int32).pin_memory()
+    outs_host = []
+    for _ in range(3):
+        b.step_host(host_in, host_out)
+        outs_host.append(host_out.clone())
+        host_in.copy_(host_out)
+    for x, y in zip(outs_dev, outs_host):
+        assert torch.equal(x, y)
+    a.close()
+    b.close()
