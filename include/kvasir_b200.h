@@ -151,8 +151,9 @@ int kvb_rope_kv_append_batched(kvb_stream_t stream, void* qkv, size_t n_seq, con
 
 /* kvb_add_inplace(x, y) followed by kvb_rmsnorm(x, w, out): the residual
  * stream x is updated in place and its normalised copy written to out. */
-int kvb_add_rmsnorm(kvb_stream_t stream, void* x, const void* y, const void* w, void* out,
-                    size_t rows, size_t hidden, float eps, int dtype);
+int kvb_add_rmsnorm(kvb_stream_t stream, void* x, size_t x_len, const void* y, size_t y_len,
+                    const void* w, size_t w_len, void* out, size_t out_len, size_t rows,
+                    size_t hidden, float eps, int dtype);
 
 /* Batched single-query decode attention, one query row per sequence:
  * q row b at q + b*q_row_stride (head h at h*head_dim), sequence b attends
@@ -174,8 +175,9 @@ size_t kvb_attention_decode_workspace_bytes(size_t n_seq, size_t max_len, size_t
  * length, positions pos0 .. pos0+t-1): qkv rows [n_seq*t, (n_q+2n_kv)*hd],
  * caches [n_seq][n_kv][max_seq][hd] already holding keys [0, pos0+t); out
  * [n_seq*t, n_q*hd].  tcgen05/TMEM kernel for head_dim 64. */
-int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, const void* kc, const void* vc,
-                          void* out, size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
+int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, const void* kc,
+                          const void* vc, size_t cache_len, void* out, size_t out_len,
+                          size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
                           size_t head_dim, size_t max_seq, int dtype);
 
 /* Greedy sampling: ids[r] = first index of the maximum of logits[r, 0:vocab)

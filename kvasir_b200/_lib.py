@@ -62,11 +62,12 @@ SIGNATURES = {
                                   _sz, _int]),
     "kvb_rope_kv_append_batched": (_int, [_p, _p, _sz, _p, _p, _p, _sz, _p, _p, _sz, _sz, _sz,
                                           _sz, _sz, _sz, _int]),
-    "kvb_add_rmsnorm": (_int, [_p, _p, _p, _p, _p, _sz, _sz, C.c_float, _int]),
+    "kvb_add_rmsnorm": (_int, [_p, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _sz, _sz, C.c_float, _int]),
     "kvb_attention_decode": (_int, [_p, _p, _sz, _p, _p, _sz, _sz, _p, _sz, _sz, _sz, _sz, _sz,
                                     _sz, C.c_float, _p, _sz, _p, _sz, _int]),
     "kvb_attention_decode_workspace_bytes": (_sz, [_sz, _sz, _sz, _sz, _sz]),
-    "kvb_attention_prefill": (_int, [_p, _p, _p, _p, _p, _sz, _sz, _sz, _sz, _sz, _sz, _sz, _int]),
+    "kvb_attention_prefill": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _sz, _sz, _sz, _sz, _sz, _sz,
+                                     _sz, _sz, _int]),
     "kvb_argmax_f32": (_int, [_p, _p, _sz, _sz, _p, _p, _p]),
     "kvb_decoder_workspace_bytes": (_sz, [C.POINTER(DecoderConfig)]),
     "kvb_decoder_create": (_int, [C.POINTER(_p), C.POINTER(DecoderConfig),

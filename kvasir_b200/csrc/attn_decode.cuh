@@ -187,22 +187,27 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
             o[j][2] *= al1;
             o[j][3] *= al1;
         }
-        // ---- O += P V : P from registers, V^T fragments via ldmatrix.trans
+        // ---- O += P V : P from registers, V^T fragments via ldmatrix.trans.
+        // P is split into a 16-bit head and a 16-bit remainder (P = hi + lo)
+        // and both are multiplied: a single 16-bit P would carry a 2^-9
+        // relative error into every weight, above the 2e-3 attention bar.
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-            uint32_t pa[4];
-            pa[0] = Elem<T>::pack(s[2 * kk][0], s[2 * kk][1]);
-            pa[1] = Elem<T>::pack(s[2 * kk][2], s[2 * kk][3]);
-            pa[2] = Elem<T>::pack(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-            pa[3] = Elem<T>::pack(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+            uint32_t ph[4], pl[4];
+            split_pack<T>(s[2 * kk][0], s[2 * kk][1], ph[0], pl[0]);
+            split_pack<T>(s[2 * kk][2], s[2 * kk][3], ph[1], pl[1]);
+            split_pack<T>(s[2 * kk + 1][0], s[2 * kk + 1][1], ph[2], pl[2]);
+            split_pack<T>(s[2 * kk + 1][2], s[2 * kk + 1][3], ph[3], pl[3]);
             const int key = 16 * kk + (lane & 7) + 8 * ((lane >> 3) & 1);
 #pragma unroll
             for (int jp = 0; jp < 4; ++jp) {
                 const int ch = 2 * jp + (lane >> 4);
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4_t(vb + key * 128 + ((ch ^ (lane & 7)) << 4), b0, b1, b2, b3);
-                mma_16816<T>(o[2 * jp], pa, b0, b1);
-                mma_16816<T>(o[2 * jp + 1], pa, b2, b3);
+                mma_16816<T>(o[2 * jp], ph, b0, b1);
+                mma_16816<T>(o[2 * jp + 1], ph, b2, b3);
+                mma_16816<T>(o[2 * jp], pl, b0, b1);
+                mma_16816<T>(o[2 * jp + 1], pl, b2, b3);
             }
         }
         __syncwarp();

@@ -32,8 +32,8 @@ struct GenericAttnArgs {
 template <typename T>
 __global__ void __launch_bounds__(128) attn_generic_kernel(GenericAttnArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.x * 4 + warp;
-    const int row = blockIdx.y;
+    const int h = blockIdx.y * 4 + warp;
+    const int row = blockIdx.x;
     if (h >= a.n_q) return;
     const int seq = row / a.rows_per_seq;
     int len;

@@ -26,7 +26,7 @@ constexpr int kPfKeys = 64;      // keys per K/V tile (MMA N of S, K of O)
 constexpr int kPfQBytes = kPfRows * 64 * 2;    // 16 KB
 constexpr int kPfKVBytes = kPfKeys * 64 * 2;   // 8 KB
 constexpr int kPfPBytes = kPfRows * kPfKeys * 2;  // 16 KB
-constexpr int kPfSmemBytes = kPfQBytes + 4 * kPfKVBytes + kPfPBytes + 1024;
+constexpr int kPfSmemBytes = kPfQBytes + 4 * kPfKVBytes + 2 * kPfPBytes + 1024;
 constexpr uint32_t kPfTmemCols = 128;  // S: cols [0,64), O tile: cols [64,128)
 
 struct PrefillArgs {
@@ -37,7 +37,7 @@ struct PrefillArgs {
 };
 
 template <typename T>
-__global__ void __launch_bounds__(128, 3) attn_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+__global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                                                               const __grid_constant__ CUtensorMap kmap,
                                                               const __grid_constant__ CUtensorMap vmap,
                                                               PrefillArgs a) {
@@ -155,24 +155,27 @@ __global__ void __launch_bounds__(128, 3) attn_prefill_kernel(const __grid_const
         }
         l = l * alpha + sum;
         m = mn;
-        // P row -> shared memory, 128B-swizzled K-major (16-byte chunk ch of row r at
-        // r*128 + ((ch ^ (r & 7)) * 16))
+        // P row -> shared memory as two 16-bit tiles, head and remainder
+        // (P = hi + lo, see split_pack), each 128B-swizzled K-major: 16-byte
+        // chunk ch of row r at r*128 + ((ch ^ (r & 7)) * 16).
         {
-            uint8_t* prow = sp + tid * 128;
+            uint8_t* prow_h = sp + tid * 128;
+            uint8_t* prow_l = sp + kPfPBytes + tid * 128;
 #pragma unroll
             for (int ch = 0; ch < 8; ++ch) {
-                uint4 v;
-                v.x = Elem<T>::pack(s[8 * ch + 0], s[8 * ch + 1]);
-                v.y = Elem<T>::pack(s[8 * ch + 2], s[8 * ch + 3]);
-                v.z = Elem<T>::pack(s[8 * ch + 4], s[8 * ch + 5]);
-                v.w = Elem<T>::pack(s[8 * ch + 6], s[8 * ch + 7]);
-                *reinterpret_cast<uint4*>(prow + ((ch ^ (tid & 7)) << 4)) = v;
+                uint4 vh, vl;
+                split_pack<T>(s[8 * ch + 0], s[8 * ch + 1], vh.x, vl.x);
+                split_pack<T>(s[8 * ch + 2], s[8 * ch + 3], vh.y, vl.y);
+                split_pack<T>(s[8 * ch + 4], s[8 * ch + 5], vh.z, vl.z);
+                split_pack<T>(s[8 * ch + 6], s[8 * ch + 7], vh.w, vl.w);
+                *reinterpret_cast<uint4*>(prow_h + ((ch ^ (tid & 7)) << 4)) = vh;
+                *reinterpret_cast<uint4*>(prow_l + ((ch ^ (tid & 7)) << 4)) = vl;
             }
         }
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-        // ---- O_t = P V
+        // ---- O_t = P_hi V + P_lo V
         if (tid == 0) {
             tc_fence_after();
             if (!s_err) {
@@ -180,6 +183,10 @@ __global__ void __launch_bounds__(128, 3) attn_prefill_kernel(const __grid_const
                 for (int ks = 0; ks < 4; ++ks)
                     umma_f16(t_o, sdesc_sw128(sp_a + 32 * ks, 16, 1024),
                              sdesc_sw128(sv_a + ks * 16 * 128, 64 * 128, 1024), idesc_o, ks > 0);
+#pragma unroll
+                for (int ks = 0; ks < 4; ++ks)
+                    umma_f16(t_o, sdesc_sw128(sp_a + kPfPBytes + 32 * ks, 16, 1024),
+                             sdesc_sw128(sv_a + ks * 16 * 128, 64 * 128, 1024), idesc_o, 1);
             }
             umma_commit(&bar_o);
         }

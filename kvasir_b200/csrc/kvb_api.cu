@@ -34,6 +34,7 @@ int fail(int status, const char* fmt, ...) {
 }
 
 int cuda_fail(cudaError_t e, const char* what) {
+    cudaGetLastError();  // reset the runtime's last error so later checks do not see it again
     return fail(KVB_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }
 
@@ -222,7 +223,7 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
 static int launch_generic_attn(kvb_stream_t stream, const GenericAttnArgs& a, size_t rows,
                                int dtype) {
     if (rows == 0) return KVB_OK;
-    dim3 grid((unsigned)((a.n_q + 3) / 4), (unsigned)rows);
+    dim3 grid((unsigned)rows, (unsigned)((a.n_q + 3) / 4));
     if (dtype == KVB_BF16)
         attn_generic_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(a);
     else
@@ -392,9 +393,14 @@ int kvb_rmsnorm(kvb_stream_t stream, const void* x, size_t x_len, const void* w,
                                  dtype);
 }
 
-int kvb_add_rmsnorm(kvb_stream_t stream, void* x, const void* y, const void* w, void* out,
-                    size_t rows, size_t hidden, float eps, int dtype) {
+int kvb_add_rmsnorm(kvb_stream_t stream, void* x, size_t x_len, const void* y, size_t y_len,
+                    const void* w, size_t w_len, void* out, size_t out_len, size_t rows,
+                    size_t hidden, float eps, int dtype) {
     KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(x_len == rows * hidden && y_len == x_len && out_len == x_len,
+              "add_rmsnorm: x/y/out have %zu/%zu/%zu elems, want %zux%zu", x_len, y_len, out_len,
+              rows, hidden);
+    KVB_CHECK(w_len == hidden, "add_rmsnorm: w has %zu elems, want %zu", w_len, hidden);
     KVB_CHECK(fits_i32(hidden) && fits_i32(rows), "add_rmsnorm: rows/hidden do not fit in i32");
     KVB_CHECK(hidden > 0 || rows == 0, "add_rmsnorm: hidden must be > 0");
     KVB_CHECK(x != out, "add_rmsnorm: out must not alias the residual x");
@@ -711,7 +717,8 @@ int kvb_attention_decode(kvb_stream_t stream, const void* q, size_t q_row_stride
     if (n_seq == 0) return KVB_OK;
     const size_t group = n_q / n_kv;
     const size_t total_rows = n_seq == 0 ? 0 : ((n_seq - 1) * seq_stride + per_seq) / 64;
-    const bool fast = head_dim == 64 && group <= 16 && seq_stride % 64 == 0 && q_row_stride % 8 == 0 &&
+    const bool fast = head_dim == 64 && group <= 16 && n_seq <= 65535 && n_kv <= 65535 &&
+                      seq_stride % 64 == 0 && q_row_stride % 8 == 0 && out_row_stride % 8 == 0 &&
                       aligned(q, 16) && aligned(kc, 16) && aligned(vc, 16) && fits_i32(total_rows) &&
                       total_rows < (1ull << 32);
     if (fast) {
@@ -757,10 +764,17 @@ int kvb_attention_decode(kvb_stream_t stream, const void* q, size_t q_row_stride
     return launch_generic_attn(stream, a, n_seq, dtype);
 }
 
-int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, const void* kc, const void* vc,
-                          void* out, size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
+int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, const void* kc,
+                          const void* vc, size_t cache_len, void* out, size_t out_len,
+                          size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
                           size_t head_dim, size_t max_seq, int dtype) {
     KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(qkv_len == n_seq * t * (n_q + 2 * n_kv) * head_dim,
+              "attention_prefill: qkv has %zu elems, want %zux%zu", qkv_len, n_seq * t,
+              (n_q + 2 * n_kv) * head_dim);
+    KVB_CHECK(cache_len == n_seq * n_kv * max_seq * head_dim, "attention_prefill: bad cache sizes");
+    KVB_CHECK(out_len == n_seq * t * n_q * head_dim, "attention_prefill: out has %zu elems, want %zux%zu",
+              out_len, n_seq * t, n_q * head_dim);
     KVB_CHECK(n_kv > 0 && n_q % n_kv == 0, "attention_prefill: n_q %zu not a multiple of n_kv %zu",
               n_q, n_kv);
     KVB_CHECK(head_dim > 0 && head_dim <= 256, "attention_prefill: head_dim %zu unsupported", head_dim);
@@ -771,8 +785,8 @@ int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, const void* kc, 
                   fits_i32(n_seq * n_kv),
               "attention_prefill: a dimension does not fit in i32");
     if (n_seq == 0 || t == 0) return KVB_OK;
-    const bool fast = head_dim == 64 && aligned(qkv, 16) && aligned(kc, 16) && aligned(vc, 16) &&
-                      aligned(out, 16);
+    const bool fast = head_dim == 64 && n_seq <= 65535 && aligned(qkv, 16) && aligned(kc, 16) &&
+                      aligned(vc, 16) && aligned(out, 16);
     if (fast) return launch_prefill(stream, qkv, kc, vc, out, n_seq, t, pos0, n_q, n_kv, max_seq, dtype);
     GenericAttnArgs a;
     a.q = static_cast<const uint16_t*>(qkv);

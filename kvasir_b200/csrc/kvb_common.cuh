@@ -63,6 +63,15 @@ __device__ __forceinline__ uint4 pack8(const float* f) {
     return v;
 }
 
+// Two floats as a packed 16-bit pair `hi` (round to nearest) plus the packed
+// 16-bit remainder `lo` = round(x - hi): hi + lo carries ~16 significant bits.
+template <typename T>
+__device__ __forceinline__ void split_pack(float a, float b, uint32_t& hi, uint32_t& lo) {
+    hi = Elem<T>::pack(a, b);
+    const float2 h = Elem<T>::unpack(hi);
+    lo = Elem<T>::pack(a - h.x, b - h.y);
+}
+
 // streaming 16-byte loads/stores (data touched once)
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
     uint4 v;

@@ -76,6 +76,7 @@ struct kvb_decoder_s {
     const float* cos_t = nullptr;
     const float* sin_t = nullptr;
     kvb_blas_t blas = nullptr;
+    cudaStream_t capture_stream = nullptr;  // private: the legacy stream cannot be captured
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;
     int own_launches = 0, lib_launches = 0;
@@ -130,7 +131,8 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
         STEP(kvb_linear(d->blas, s, d->at(L.attn), B * qd, d->w_o[l], H * qd, d->at(L.o), B * H, B,
                         qd, H, dt, 0),
              true);
-        STEP(kvb_add_rmsnorm(s, d->at(L.x), d->at(L.o), d->mlp_norm[l], d->at(L.h), B, H, c.eps, dt),
+        STEP(kvb_add_rmsnorm(s, d->at(L.x), B * H, d->at(L.o), B * H, d->mlp_norm[l], H, d->at(L.h),
+                             B * H, B, H, c.eps, dt),
              false);
         STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->w_gu[l], 2 * I * H, d->at(L.gu), B * 2 * I,
                         B, H, 2 * I, dt, 0),
@@ -140,7 +142,8 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
                         I, H, dt, 0),
              true);
         const void* next_norm = (l + 1 < c.n_layers) ? d->attn_norm[l + 1] : d->final_norm;
-        STEP(kvb_add_rmsnorm(s, d->at(L.x), d->at(L.o), next_norm, d->at(L.h), B, H, c.eps, dt),
+        STEP(kvb_add_rmsnorm(s, d->at(L.x), B * H, d->at(L.o), B * H, next_norm, H, d->at(L.h), B * H,
+                             B, H, c.eps, dt),
              false);
     }
     STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->embed, (size_t)c.vocab * H,
@@ -201,11 +204,16 @@ int kvb_decoder_create(kvb_decoder_t* out, const kvb_decoder_config* cfg,
     int st = kvb_blas_create(&d->blas);
     if (st == KVB_OK) st = kvb_blas_set_workspace(d->blas, d->at(L.blas_ws), kBlasWorkspace);
     if (st == KVB_OK) {
+        cudaError_t e = cudaStreamCreateWithFlags(&d->capture_stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) st = kvb::cuda_fail(e, "decoder_create: capture stream");
+    }
+    if (st == KVB_OK) {
         cudaError_t e = cudaMemset(d->ws, 0, L.blas_ws);  // activations, counters, ids
         if (e == cudaSuccess) e = cudaDeviceSynchronize();
         if (e != cudaSuccess) st = kvb::cuda_fail(e, "decoder_create: workspace clear");
     }
     if (st != KVB_OK) {
+        if (d->capture_stream) cudaStreamDestroy(d->capture_stream);
         kvb_blas_destroy(d->blas);
         delete d;
         return st;
@@ -218,6 +226,7 @@ int kvb_decoder_destroy(kvb_decoder_t d) {
     if (!d) return KVB_OK;
     if (d->exec) cudaGraphExecDestroy(d->exec);
     if (d->graph) cudaGraphDestroy(d->graph);
+    if (d->capture_stream) cudaStreamDestroy(d->capture_stream);
     kvb_blas_destroy(d->blas);
     delete d;
     return KVB_OK;
@@ -248,13 +257,15 @@ const float* kvb_decoder_logits(kvb_decoder_t d) { return d ? d->at<float>(d->la
 int kvb_decoder_step(kvb_decoder_t d, kvb_stream_t s) {
     KVB_CHECK(d != nullptr, "decoder_step: null decoder");
     if (!d->exec) {
-        // Record the step once; host-side work (argument checks, tensor-map
-        // encoding) happens only here, replays are a single graph launch.
-        cudaError_t e = cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal);
+        // Record the step once on the private capture stream (recording runs
+        // nothing); host-side work (argument checks, tensor-map encoding)
+        // happens only here, every step is then one graph launch on `s`.
+        cudaStream_t cs = d->capture_stream;
+        cudaError_t e = cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal);
         if (e != cudaSuccess) return kvb::cuda_fail(e, "decoder_step: begin capture");
-        const int st = record_step(d, s);
+        const int st = record_step(d, cs);
         cudaGraph_t g = nullptr;
-        e = cudaStreamEndCapture(s, &g);
+        e = cudaStreamEndCapture(cs, &g);
         if (st != KVB_OK) {
             if (g) cudaGraphDestroy(g);
             return st;

@@ -186,11 +186,9 @@ class Gpu:
             dtype_tag(qkv)))
 
     def add_rmsnorm(self, x, y, w, out, rows, hidden, eps):
-        for t, n in ((x, rows * hidden), (y, rows * hidden), (w, hidden), (out, rows * hidden)):
-            if t.numel() != n:
-                raise ShapeError(f"add_rmsnorm: buffer has {t.numel()} elems, want {n}")
-        check(self._lib.kvb_add_rmsnorm(self._s, _ptr(x), _ptr(y), _ptr(w), _ptr(out), rows,
-                                        hidden, eps, dtype_tag(x)))
+        check(self._lib.kvb_add_rmsnorm(self._s, _ptr(x), x.numel(), _ptr(y), y.numel(), _ptr(w),
+                                        w.numel(), _ptr(out), out.numel(), rows, hidden, eps,
+                                        dtype_tag(x)))
 
     def attention_decode_workspace_bytes(self, n_seq, max_len, n_q, n_kv, head_dim) -> int:
         return int(self._lib.kvb_attention_decode_workspace_bytes(n_seq, max_len, n_q, n_kv,
@@ -208,17 +206,11 @@ class Gpu:
             out_row_stride, _ptr(workspace), ws_len, dtype_tag(q)))
 
     def attention_prefill(self, qkv, kc, vc, out, n_seq, t, pos0, n_q, n_kv, head_dim, max_seq):
-        stride = (n_q + 2 * n_kv) * head_dim
-        if qkv.numel() != n_seq * t * stride:
-            raise ShapeError(f"attention_prefill: qkv has {qkv.numel()} elems, "
-                             f"want {n_seq * t}x{stride}")
-        if kc.numel() != n_seq * n_kv * max_seq * head_dim or vc.numel() != kc.numel():
+        if vc.numel() != kc.numel():
             raise ShapeError("attention_prefill: bad cache sizes")
-        if out.numel() != n_seq * t * n_q * head_dim:
-            raise ShapeError("attention_prefill: bad output size")
-        check(self._lib.kvb_attention_prefill(self._s, _ptr(qkv), _ptr(kc), _ptr(vc), _ptr(out),
-                                              n_seq, t, pos0, n_q, n_kv, head_dim, max_seq,
-                                              dtype_tag(qkv)))
+        check(self._lib.kvb_attention_prefill(self._s, _ptr(qkv), qkv.numel(), _ptr(kc), _ptr(vc),
+                                              kc.numel(), _ptr(out), out.numel(), n_seq, t, pos0,
+                                              n_q, n_kv, head_dim, max_seq, dtype_tag(qkv)))
 
     def argmax(self, logits, rows, vocab, ids, advance=None, advance2=None):
         if logits.dtype != torch.float32 or ids.dtype != torch.int32:
