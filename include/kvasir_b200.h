@@ -171,6 +171,30 @@ int kvb_attention_decode(kvb_stream_t stream, const void* q, size_t q_row_stride
 size_t kvb_attention_decode_workspace_bytes(size_t n_seq, size_t max_len, size_t n_q,
                                             size_t n_kv, size_t head_dim);
 
+/* No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory.  Same arguments and result as kvb_attention_decode
+ * minus the workspace: the split-KV partials go to a scratch array that the
+ * library itself holds in device memory (a file-scope __device__ array of
+ * KVB_NOALLOC_SCRATCH_BYTES, present on every GPU that loads the library until
+ * the process exits).  It serves callers that own no spare device buffer and
+ * may not call cudaMalloc -- for example a host engine whose device memory
+ * all belongs to long-lived weight / cache structs (the reference's own rule
+ * for its launch wrappers), or code running where an allocation's implicit
+ * device synchronisation is not acceptable.  The call allocates and frees
+ * nothing.  Requests whose partials need more than KVB_NOALLOC_SCRATCH_BYTES
+ * (kvb_attention_decode_workspace_bytes) return KVB_ERR_SHAPE.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress) with
+ * that device current; make that first call before any stream capture.  All
+ * calls on a device share the one array: calls that may overlap on the GPU
+ * (different streams, or graphs replayed concurrently) race on it. */
+#define KVB_NOALLOC_SCRATCH_BYTES (8u << 20)
+int kvb_attention_decode_noalloc(kvb_stream_t stream, const void* q, size_t q_row_stride,
+                                 const void* kc, const void* vc, size_t seq_stride,
+                                 size_t cache_len, const int32_t* lens, size_t n_seq,
+                                 size_t max_len, size_t n_q, size_t n_kv, size_t head_dim,
+                                 size_t max_seq, float scale, void* out, size_t out_row_stride,
+                                 int dtype);
+
 /* Causal prefill attention for n_seq sequences of t tokens each (uniform
  * length, positions pos0 .. pos0+t-1): qkv rows [n_seq*t, (n_q+2n_kv)*hd],
  * caches [n_seq][n_kv][max_seq][hd] already holding keys [0, pos0+t); out

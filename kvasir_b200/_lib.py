@@ -66,6 +66,8 @@ SIGNATURES = {
     "kvb_attention_decode": (_int, [_p, _p, _sz, _p, _p, _sz, _sz, _p, _sz, _sz, _sz, _sz, _sz,
                                     _sz, C.c_float, _p, _sz, _p, _sz, _int]),
     "kvb_attention_decode_workspace_bytes": (_sz, [_sz, _sz, _sz, _sz, _sz]),
+    "kvb_attention_decode_noalloc": (_int, [_p, _p, _sz, _p, _p, _sz, _sz, _p, _sz, _sz, _sz, _sz,
+                                            _sz, _sz, C.c_float, _p, _sz, _int]),
     "kvb_attention_prefill": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _sz, _sz, _sz, _sz, _sz, _sz,
                                      _sz, _sz, _int]),
     "kvb_argmax_f32": (_int, [_p, _p, _sz, _sz, _p, _p, _p]),

@@ -808,6 +808,69 @@ int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, 
     return launch_generic_attn(stream, a, n_seq * t, dtype);
 }
 
+}  // extern "C"
+
+// ------------------------------------------------------------------ decode attention without allocation
+// Scratch for kvb_attention_decode_noalloc: the split-KV partials of one call.
+// It lives in the library's own device memory on every GPU that loads the
+// library.  In host code this name is only a host-side stand-in for the
+// device array; the device address comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KVB_NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on the current device, looked up once
+// per device (with that device current) and cached.
+static void* noalloc_scratch_address(int* status) {
+    static std::mutex mu;
+    static void* addr[64] = {};
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) {
+        *status = cuda_fail(e, "attention_decode_noalloc: cudaGetDevice");
+        return nullptr;
+    }
+    if (dev < 0 || dev >= 64) {
+        *status = fail(KVB_ERR_UNSUPPORTED, "attention_decode_noalloc: device ordinal %d > 63", dev);
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            *status = cuda_fail(e, "attention_decode_noalloc: cudaGetSymbolAddress");
+            return nullptr;
+        }
+        addr[dev] = p;
+    }
+    return addr[dev];
+}
+
+extern "C" {
+
+int kvb_attention_decode_noalloc(kvb_stream_t stream, const void* q, size_t q_row_stride,
+                                 const void* kc, const void* vc, size_t seq_stride,
+                                 size_t cache_len, const int32_t* lens, size_t n_seq,
+                                 size_t max_len, size_t n_q, size_t n_kv, size_t head_dim,
+                                 size_t max_seq, float scale, void* out, size_t out_row_stride,
+                                 int dtype) {
+    // Every partial the combine pass reads is written earlier in the same
+    // call, so no part of the shared array has to start at zero.
+    const size_t need = kvb_attention_decode_workspace_bytes(n_seq, max_len, n_q, n_kv, head_dim);
+    KVB_CHECK(need <= KVB_NOALLOC_SCRATCH_BYTES,
+              "attention_decode_noalloc: the split-KV partials need %zu bytes, more than the "
+              "%u-byte scratch array; use kvb_attention_decode with a workspace",
+              need, (unsigned)KVB_NOALLOC_SCRATCH_BYTES);
+    void* ws = nullptr;
+    if (need > 0) {
+        int st = KVB_OK;
+        ws = noalloc_scratch_address(&st);
+        if (!ws) return st;
+    }
+    return kvb_attention_decode(stream, q, q_row_stride, kc, vc, seq_stride, cache_len, lens,
+                                n_seq, max_len, n_q, n_kv, head_dim, max_seq, scale, out,
+                                out_row_stride, ws, need, dtype);
+}
+
 // ------------------------------------------------------------------ argmax
 int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
                    int32_t* ids, int32_t* advance, int32_t* advance2) {
