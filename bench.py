@@ -294,12 +294,15 @@ def run_decode(args):
     attn_ms = a0.elapsed_time(a1) / reps
     alg_bytes = int(lens_host.sum()) * nkv * hd * 2 * 2 + n_local * nq * hd * 2 * 2
     achieved = alg_bytes / (attn_ms / 1e3) / 1e9
+    # DRAM traffic per launch: the ncu-measured (read + write) / algorithmic ratio of the
+    # committed capture (profiles/attn_decode_cfg5_small.md), scaled to this launch
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "attn_decode_traffic.json")
+    tp = os.path.join(ROOT, "profiles", "attn_decode_cfg5_small.md")
     if os.path.exists(tp):
         with open(tp) as f:
-            tr = json.load(f)
-        traffic = int(tr["dram_bytes_per_alg_byte"] * alg_bytes)
+            for line in f:
+                if line.startswith("dram_bytes_per_alg_byte:"):
+                    traffic = int(float(line.split(":", 1)[1]) * alg_bytes)
     clocks = clk.summary()
 
     cpu = None
