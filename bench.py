@@ -114,13 +114,16 @@ def dist_env():
     return world, rank, local
 
 
-def init_dist(world):
+def init_dist(world, local):
     if world <= 1:
         return None
     import datetime
+
+    import torch
     import torch.distributed as dist
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                            device_id=torch.device("cuda", local))
     return dist
 
 
@@ -219,7 +222,7 @@ def run_decode(args):
 
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
-    dist = init_dist(world)
+    dist = init_dist(world, local)
     peaks, peak_kind = load_peaks()
     cfg = LlamaConfig.llama_3_2_1b()
     n_total, ctx = args.seqs, args.context

@@ -1,0 +1,333 @@
+"""Per-kernel measurements for BASELINE configs 1-4 (`bench.py --workload cfgN`).
+
+Each config prints one JSON line per measured item.  Device times are CUDA
+events on the launching stream after warm-up; HBM-bound kernels whose working
+set fits in L2 are timed one launch at a time with a 256 MB L2 flush between
+launches (the flush is outside the timed interval).  CPU numbers are the
+oracle (oracle/, the reference's CPU-reference computations restated) on all
+host cores, timed on the same inputs or a stated sample.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import time
+
+import numpy as np
+import torch
+
+from . import Gpu
+from .config import LlamaConfig
+from .rope import cos_sin_table
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class _Flusher:
+    def __init__(self):
+        self.buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def __call__(self):
+        self.buf.zero_()
+
+
+def time_each(fn, reps: int, flush=None) -> float:
+    """Mean ms of fn over reps launches, each bracketed by its own events
+    (optionally after an L2 flush that is not timed)."""
+    s = torch.cuda.current_stream()
+    evs = []
+    for _ in range(reps):
+        if flush:
+            flush()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        fn()
+        b.record(s)
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    return float(np.mean([a.elapsed_time(b) for a, b in evs]))
+
+
+def time_loop(fn, reps: int) -> float:
+    """Mean ms of reps back-to-back calls (for working sets far above L2)."""
+    s = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(s)
+    for _ in range(reps):
+        fn()
+    b.record(s)
+    b.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+def _emit(d):
+    print(json.dumps(d), flush=True)
+
+
+def _cpu_threads():
+    return os.cpu_count() or 1
+
+
+def _bits(t):
+    return t.contiguous().cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+# ----------------------------------------------------------------------------- config 1
+def cfg1(args):
+    """One decoder layer's kernel chain at batch 1: embedding gather, RMSNorm,
+    RoPE + KV append at position 512, GQA decode attention over 513 keys,
+    SiLU*mul on one [1, 16384] gate/up row.  Launch-latency bound: reported as
+    microseconds per chain, eager and as a CUDA graph."""
+    from oracle import oracle as O
+    cfg = LlamaConfig.llama_3_2_1b()
+    g = Gpu(0)
+    gen = torch.Generator(device="cuda").manual_seed(1)
+    H, hd, nq, nkv, I, V = 2048, 64, 32, 8, 8192, 128256
+    pos, max_seq = 512, 1024
+    table = (torch.randn(V, H, generator=gen, device="cuda") * 0.02).to(torch.bfloat16)
+    w = (1 + 0.02 * torch.randn(H, generator=gen, device="cuda")).to(torch.bfloat16)
+    ids = torch.randint(0, V, (1,), dtype=torch.int32, device="cuda", generator=gen)
+    x = torch.empty(H, dtype=torch.bfloat16, device="cuda")
+    h = torch.empty_like(x)
+    qkv0 = torch.randn(cfg.qkv_dim, generator=gen, device="cuda").to(torch.bfloat16)
+    qkv = qkv0.clone()
+    kc = torch.randn(nkv * max_seq * hd, generator=gen, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(nkv * max_seq * hd, generator=gen, device="cuda").to(torch.bfloat16)
+    c, s = cos_sin_table(cfg, max_seq)
+    cos, sin = torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
+    out = torch.empty(nq * hd, dtype=torch.bfloat16, device="cuda")
+    ws = torch.empty(max(16, g.attention_workspace_bytes(1, pos, nq, nkv, hd)), dtype=torch.uint8,
+                     device="cuda")
+    gu = torch.randn(2 * I, generator=gen, device="cuda").to(torch.bfloat16)
+    act = torch.empty(I, dtype=torch.bfloat16, device="cuda")
+
+    def chain():
+        g.embedding_gather(ids, table, x, H)
+        g.rmsnorm(x, w, h, 1, H, 1e-5)
+        g.rope_kv_append(qkv, cos, sin, kc, vc, 1, pos, nq, nkv, hd, max_seq)
+        g.attention(qkv, kc, vc, out, 1, pos, nq, nkv, hd, max_seq, workspace=ws)
+        g.silu_mul(gu, act, 1, I)
+
+    for _ in range(5):
+        chain()
+    eager_ms = time_loop(chain, 200)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    g.stream = stream
+    with torch.cuda.stream(stream):
+        chain()  # warm on the capture stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            chain()
+    g.stream = torch.cuda.current_stream()
+    for _ in range(5):
+        graph.replay()
+    graph_ms = time_loop(graph.replay, 500)
+    alg = (2 * H * 2) + (3 * H * 2) + (40 * hd * 2 * 2 + 8 * hd * 2 * 2 + 256 * 4) + \
+          (513 * nkv * hd * 4 + 2 * nq * hd * 2) + (3 * I * 2)
+    # CPU: the same chain through the oracle
+    O.set_threads(_cpu_threads())
+    tb, wb, qb = _bits(table), _bits(w), _bits(qkv0)
+    kb, vb, gb = _bits(kc), _bits(vc), _bits(gu)
+    idh = ids.cpu().numpy()
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < 2.0 or n < 3:
+        xb = O.embedding_gather(idh, tb, H)
+        O.rmsnorm(xb, wb, 1, H, 1e-5)
+        r = O.from_f32(O.rope(qb, c, s, 1, pos, nq, nkv, hd))
+        k2, v2 = O.kv_append(r, kb, vb, 1, pos, nq, nkv, hd, max_seq)
+        O.attention(r, k2, v2, 1, pos, nq, nkv, hd, max_seq)
+        O.silu_mul(gb, 1, I)
+        n += 1
+    cpu_us = (time.perf_counter() - t0) / n * 1e6
+    O.set_threads(1)
+    _emit({"workload": "cfg1: one decoder layer chain, batch-1 decode at position 512 (513 keys)",
+           "metric": "us per chain", "value": graph_ms * 1e3, "eager_us": eager_ms * 1e3,
+           "graph_us": graph_ms * 1e3, "unit": "us", "higher_is_better": False,
+           "launches_per_chain": 5 + (1 if ws.numel() > 16 else 0),
+           "alg_bytes": alg, "gbs_informative": alg / (graph_ms * 1e-3) / 1e9,
+           "cpu_oracle_us": cpu_us, "cpu_threads": _cpu_threads()})
+
+
+# ----------------------------------------------------------------------------- config 2
+def cfg2(args):
+    """Batched decode attention: 64 sequences, lengths U[1, 4096], 32/8 heads,
+    hd 64, N(0,1) Q/K/V, scale 1/8."""
+    from oracle import oracle as O
+    peaks, kind = _peaks()
+    g = Gpu(0)
+    rng = np.random.default_rng(2)
+    n_seq, nq, nkv, hd, max_seq = 64, 32, 8, 64, 4096
+    lens = rng.integers(1, max_seq + 1, n_seq).astype(np.int32)
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    per = nkv * max_seq * hd
+    q = torch.randn(n_seq * nq * hd, generator=gen, device="cuda").to(torch.bfloat16)
+    kc = torch.empty(n_seq * per, dtype=torch.bfloat16, device="cuda").normal_(generator=gen)
+    vc = torch.empty(n_seq * per, dtype=torch.bfloat16, device="cuda").normal_(generator=gen)
+    out = torch.empty(n_seq * nq * hd, dtype=torch.bfloat16, device="cuda")
+    lens_t = torch.from_numpy(lens).cuda()
+    nb = g.attention_decode_workspace_bytes(n_seq, max_seq, nq, nkv, hd)
+    ws = torch.empty(max(nb, 16), dtype=torch.uint8, device="cuda")
+
+    def run():
+        g.attention_decode(q, nq * hd, kc, vc, per, lens_t, max_seq, nq, nkv, hd, max_seq, out,
+                           nq * hd, scale=0.125, workspace=ws)
+
+    for _ in range(5):
+        run()
+    flush = _Flusher()
+    ms = time_each(run, 50, flush)
+    alg = int(lens.sum()) * nkv * hd * 2 * 2 + n_seq * nq * hd * 2 * 2
+    gbs = alg / (ms * 1e-3) / 1e9
+    O.set_threads(_cpu_threads())
+    qb, kb, vb = _bits(q), _bits(kc), _bits(vc)
+    t0 = time.perf_counter()
+    O.attention_decode(qb, nq * hd, kb, vb, lens, nq, nkv, hd, max_seq, 0.125)
+    cpu_s = time.perf_counter() - t0
+    O.set_threads(1)
+    _emit({"workload": "cfg2: batched decode attention, 64 seqs, lens U[1,4096], 32/8 heads, hd 64",
+           "metric": "attention HBM GB/s", "value": gbs, "unit": "GB/s", "us": ms * 1e3,
+           "alg_bytes": alg, "frac_of_peak": gbs / peaks["hbm_gbs"],
+           "peak": f"{peaks['hbm_gbs']} GB/s ({kind})", "l2": "flushed between launches",
+           "cpu_oracle_ms": cpu_s * 1e3, "cpu_threads": _cpu_threads(),
+           "cpu_gbs": alg / cpu_s / 1e9})
+
+
+# ----------------------------------------------------------------------------- config 3
+def cfg3(args):
+    """Prefill, batch 4 x 2048 tokens: RMSNorm [8192, 2048]; RoPE (llama3,
+    positions 0..2047) fused with KV append into empty caches; causal GQA
+    attention 32/8 heads hd 64 on tcgen05; SiLU*mul on [8192, 8192] gate/up."""
+    from oracle import oracle as O
+    peaks, kind = _peaks()
+    cfg = LlamaConfig.llama_3_2_1b()
+    g = Gpu(0)
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    n_seq, T, H, hd, nq, nkv, I = 4, 2048, 2048, 64, 32, 8, 8192
+    rows = n_seq * T
+    flush = _Flusher()
+    res = {}
+    # RMSNorm
+    x = torch.randn(rows * H, generator=gen, device="cuda").to(torch.bfloat16)
+    w = (1 + 0.02 * torch.randn(H, generator=gen, device="cuda")).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    f = lambda: g.rmsnorm(x, w, y, rows, H, 1e-5)
+    f()
+    ms = time_each(f, 30, flush)
+    res["rmsnorm"] = (ms, rows * H * 2 * 2 + H * 2)
+    # RoPE + KV append (each sequence into its own empty cache)
+    qkv = torch.randn(rows * cfg.qkv_dim, generator=gen, device="cuda").to(torch.bfloat16)
+    qkv_work = qkv.clone()
+    kc = torch.zeros(n_seq * nkv * T * hd, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    c, s = cos_sin_table(cfg, T)
+    cos, sin = torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
+    per_seq = T * cfg.qkv_dim
+    per_cache = nkv * T * hd
+
+    def rope_all():
+        for b in range(n_seq):
+            g.rope_kv_append(qkv_work[b * per_seq:(b + 1) * per_seq], cos, sin,
+                             kc[b * per_cache:(b + 1) * per_cache],
+                             vc[b * per_cache:(b + 1) * per_cache], T, 0, nq, nkv, hd, T)
+
+    def rope_reset():
+        qkv_work.copy_(qkv)
+        flush()
+
+    rope_all()
+    ms = time_each(rope_all, 30, rope_reset)
+    res["rope_kv_append"] = (ms, rows * ((nq + nkv) * hd * 2 * 2 + nkv * hd * 2 + 2 * nkv * hd * 2))
+    # attention (tcgen05)
+    out = torch.empty(rows * nq * hd, dtype=torch.bfloat16, device="cuda")
+    att = lambda: g.attention_prefill(qkv_work, kc, vc, out, n_seq, T, 0, nq, nkv, hd, T)
+    att()
+    ms_att = time_each(att, 30, flush)
+    flops = 4.0 * n_seq * nq * (T * (T + 1) / 2) * hd
+    # SiLU*mul
+    gu = torch.randn(rows * 2 * I, generator=gen, device="cuda").to(torch.bfloat16)
+    act = torch.empty(rows * I, dtype=torch.bfloat16, device="cuda")
+    f = lambda: g.silu_mul(gu, act, rows, I)
+    f()
+    ms = time_each(f, 30, flush)
+    res["silu_mul"] = (ms, rows * I * 2 * 3)
+    for name, (ms, b) in res.items():
+        gbs = b / (ms * 1e-3) / 1e9
+        _emit({"workload": f"cfg3: prefill 4 x 2048, {name}", "metric": "HBM GB/s", "value": gbs,
+               "unit": "GB/s", "us": ms * 1e3, "alg_bytes": b, "frac_of_peak": gbs / peaks["hbm_gbs"],
+               "peak": f"{peaks['hbm_gbs']} GB/s ({kind})", "l2": "flushed between launches"})
+    tflops = flops / (ms_att * 1e-3) / 1e12
+    # CPU: one (sequence, kv head) group of the causal attention, scaled to all 32
+    O.set_threads(_cpu_threads())
+    qb = _bits(qkv_work[:per_seq]).reshape(T, nq + 2 * nkv, hd)
+    sub = np.ascontiguousarray(np.concatenate([qb[:, 0:4], qb[:, nq:nq + 1], qb[:, nq + nkv:nq + nkv + 1]], 1))
+    kb = _bits(kc[:T * hd])
+    vb = _bits(vc[:T * hd])
+    t0 = time.perf_counter()
+    O.attention(sub, kb, vb, T, 0, 4, 1, hd, T)
+    cpu_s = (time.perf_counter() - t0) * (n_seq * nkv)
+    O.set_threads(1)
+    _emit({"workload": "cfg3: prefill 4 x 2048, causal GQA attention 32/8 heads hd 64 (tcgen05)",
+           "metric": "TFLOP/s", "value": tflops, "unit": "TFLOP/s", "us": ms_att * 1e3,
+           "flops": flops, "frac_of_peak": tflops / peaks["bf16_tflops"],
+           "peak": f"{peaks['bf16_tflops']} TFLOP/s ({kind}, burst)",
+           "cpu_oracle_s_scaled": cpu_s, "cpu_sample": "1 of 32 (sequence, kv head) groups, x32",
+           "cpu_threads": _cpu_threads()})
+
+
+# ----------------------------------------------------------------------------- config 4
+def cfg4(args):
+    """Full 16-layer decode, context 1024, batch 1 and 32, 256 greedy steps
+    from uniform random prompt ids (random-init weights, N(0,1) context KV)."""
+    from .decoder import Decoder
+    peaks, kind = _peaks()
+    cfg = LlamaConfig.llama_3_2_1b()
+    steps, ctx = 256, 1024
+    weights = None
+    for B in (1, 32):
+        dec = Decoder(cfg, B, ctx + steps + 8, weights=weights, seed=0)
+        weights = dec.w
+        dec.fill_kv_normal(seed=4)
+        dec.set_lengths(ctx)
+        rng = np.random.default_rng(4)
+        dec.ids_in.copy_(torch.from_numpy(rng.integers(0, cfg.vocab_size, B).astype(np.int32)).cuda())
+        for _ in range(3):
+            dec.step()
+        dec.set_lengths(ctx)
+        torch.cuda.synchronize()
+        s = torch.cuda.current_stream()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        for _ in range(steps):
+            dec.step()
+        b.record(s)
+        b.synchronize()
+        ms = a.elapsed_time(b)
+        tps = B * steps / (ms * 1e-3)
+        # bytes per step: weights + KV read at the mean context of the run
+        kv = B * (ctx + steps / 2) * cfg.num_layers * cfg.num_kv_heads * cfg.head_dim * 2 * 2
+        step_bytes = dec.weight_bytes() + kv + B * cfg.vocab_size * 4
+        roof_tps = B / (step_bytes / (peaks["hbm_gbs"] * 1e9))
+        _emit({"workload": f"cfg4: 16-layer decode, batch {B}, context 1024, 256 greedy steps",
+               "metric": "tokens/s", "value": tps, "unit": "tokens/s", "ms_per_step": ms / steps,
+               "bytes_per_step": step_bytes, "hbm_roofline_tokens_s": roof_tps,
+               "frac_of_roofline": tps / roof_tps, "peak": f"{peaks['hbm_gbs']} GB/s ({kind})"})
+        dec.close()
+        del dec
+        torch.cuda.empty_cache()
+
+
+def run(name, args):
+    {"cfg1": cfg1, "cfg2": cfg2, "cfg3": cfg3, "cfg4": cfg4}[name](args)

@@ -9,6 +9,8 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <utility>
+#include <vector>
 
 #include "attn_decode.cuh"
 #include "attn_generic.cuh"
@@ -100,10 +102,20 @@ static unsigned grid_for(size_t work, int block) {
     return g ? (unsigned)g : 1u;
 }
 
+// Raises a kernel's dynamic shared-memory limit once per (device, kernel), so
+// that launches recorded into a CUDA graph make no attribute calls.
 template <typename F>
 static void set_max_smem(F* kernel, int bytes) {
-    // Idempotent; called before the first launch of each instantiation.
+    static std::mutex mu;
+    static std::vector<std::pair<int, const void*>> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const void* key = reinterpret_cast<const void*>(kernel);
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto& d : done)
+        if (d.first == dev && d.second == key) return;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    done.emplace_back(dev, key);
 }
 
 // ---------------------------------------------------------------- rope / kv append launcher
@@ -283,7 +295,18 @@ static int launch_rmsnorm(kvb_stream_t stream, void* x, const void* y, const voi
     const size_t chunks = hidden / 8;
     const bool vec = hidden % 8 == 0 && aligned(x, 16) && aligned(w, 16) && aligned(out, 16) &&
                      (!kAdd || aligned(y, 16)) && chunks <= 32 * 16;
-    if (vec) {
+    // Decode-sized batches (fewer rows than 4 per SM): a CTA per row.
+    const bool per_row = vec && chunks % 32 == 0 && chunks <= 1024 &&
+                         rows <= (size_t)num_sms() * 4;
+    if (per_row) {
+        const float ih = 1.0f / (float)hidden;
+        if (dtype == KVB_BF16)
+            rmsnorm_row_kernel<__nv_bfloat16, kAdd><<<(unsigned)rows, (unsigned)chunks, 0, stream>>>(
+                (uint4*)x, (const uint4*)y, (const uint4*)w, (uint4*)out, (int)chunks, ih, eps);
+        else
+            rmsnorm_row_kernel<__half, kAdd><<<(unsigned)rows, (unsigned)chunks, 0, stream>>>(
+                (uint4*)x, (const uint4*)y, (const uint4*)w, (uint4*)out, (int)chunks, ih, eps);
+    } else if (vec) {
         const unsigned grid = (unsigned)((rows + 3) / 4);
         const float ih = 1.0f / (float)hidden;
         const int nv = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : chunks <= 256 ? 8 : 16;

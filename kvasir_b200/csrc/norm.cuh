@@ -58,6 +58,48 @@ __global__ void __launch_bounds__(128) rmsnorm_warp_kernel(uint4* __restrict__ x
     }
 }
 
+// Few rows (decode batches): one CTA per row, one 16-byte chunk per thread
+// (blockDim = hidden / 8), so a row's loads are all in flight at once.
+template <typename T, bool kAdd>
+__global__ void __launch_bounds__(1024) rmsnorm_row_kernel(uint4* __restrict__ x,
+                                                          const uint4* __restrict__ y,
+                                                          const uint4* __restrict__ w,
+                                                          uint4* __restrict__ out, int chunks,
+                                                          float inv_hidden, float eps) {
+    __shared__ float red[32];
+    const size_t row = blockIdx.x;
+    const int c = threadIdx.x;
+    const int lane = c & 31, warp = c >> 5;
+    float v[8], wf[8];
+    unpack8<T>(x[row * chunks + c], v);
+    unpack8<T>(w[c], wf);
+    if (kAdd) {
+        float d[8];
+        unpack8<T>(y[row * chunks + c], d);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d[e] += v[e];
+        const uint4 s = pack8<T>(d);  // residual rounded to the activation type
+        x[row * chunks + c] = s;
+        unpack8<T>(s, v);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+        float r = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+        r = warp_sum(r);
+        if (lane == 0) red[0] = r;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] * inv_hidden + eps);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) v[e] = v[e] * inv * wf[e];
+    out[row * chunks + c] = pack8<T>(v);
+}
+
 // Any width, any alignment: one CTA per row, two passes over the row.
 template <typename T, bool kAdd>
 __global__ void __launch_bounds__(256) rmsnorm_generic_kernel(T* __restrict__ x,
