@@ -1,242 +1,356 @@
 // attn_prefill.cuh -- causal GQA prefill attention on the 5th-generation
-// tensor cores (tcgen05 / TMEM), head_dim 64.
+// tensor cores (tcgen05 / TMEM), head_dim 64, warp-specialised.
 //
-// One CTA computes a 128-query tile of one head of one sequence.  Q (128x64),
-// and double-buffered K/V tiles (64 keys x 64 dims) arrive by TMA with
-// 128-byte swizzle (no multicast), each completing an mbarrier.  Per K/V tile:
-//   S = Q K^T      tcgen05.mma kind::f16, M=128 N=64, K=64 (4 x K16), D in TMEM
-//   softmax        each of the 128 threads owns one query row: tcgen05.ld the
-//                  S row, causal mask on the diagonal tiles, online max/sum in
-//                  the log2 domain, P rounded to 16 bits and stored to shared
-//                  memory in the canonical 128B-swizzled K-major layout
-//   O_t = P V      tcgen05.mma, M=128 N=64 K=64, V read MN-major from the
-//                  same TMA tile; O_t lands in TMEM and is folded into the
-//                  row's f32 accumulator in registers (O = O*alpha + O_t)
-// Causal tile skipping: a 128-row tile at query offset q0 only visits keys
-// [0, pos0 + q0 + 128).  Grid order puts the longest tiles first.
-// Every mbarrier wait is bounded; TMEM is released on every exit path.
+// One CTA (one per SM) computes 256 query rows of one head of one sequence as
+// two 128-row tiles, A and B, that share every K/V tile:
+//   warp 16  TMA producer: Q_A, Q_B once, then 64-key K/V tiles into a
+//            3-stage ring (cp.async.bulk.tensor, 128B swizzle, no multicast)
+//   warp 17  MMA issuer (one lane): S_q = Q_q K^T (tcgen05.mma kind::f16,
+//            M=128 N=64, f32 accumulators in TMEM, two S buffers per tile)
+//            and O_q = P_q V (M=128 N=64, V read MN-major from the same tile)
+//   warps 0-7 / 8-15  softmax for tile A / B, two threads per query row (32
+//            columns each): tcgen05.ld of the S row half, causal mask on the
+//            diagonal, online max/sum in the log2 domain, P to shared memory as
+//            a 16-bit head plus a 16-bit remainder (two MMAs, so P keeps ~16
+//            significant bits), O tile folded into f32 accumulators in registers.
+// Issue order per K/V tile j: S_A(j+1), S_B(j+1), then P_A(j) V, P_B(j) V as each P
+// arrives, so the next S is ready when a softmax thread finishes the current one.
+// P, O and S are double-buffered; each buffer has its own ready barrier.
+// Every mbarrier wait is bounded; a failed wait sets a CTA-wide flag that
+// every role checks before its next wait; TMEM is freed on every path.
 #pragma once
 
 #include "kvb_ptx.cuh"
 
 namespace kvb {
 
-constexpr int kPfRows = 128;     // query rows per CTA (MMA M)
-constexpr int kPfKeys = 64;      // keys per K/V tile (MMA N of S, K of O)
-constexpr int kPfQBytes = kPfRows * 64 * 2;    // 16 KB
-constexpr int kPfKVBytes = kPfKeys * 64 * 2;   // 8 KB
-constexpr int kPfPBytes = kPfRows * kPfKeys * 2;  // 16 KB
-constexpr int kPfSmemBytes = kPfQBytes + 4 * kPfKVBytes + 2 * kPfPBytes + 1024;
-constexpr uint32_t kPfTmemCols = 128;  // S: cols [0,64), O tile: cols [64,128)
+constexpr int kPfRows = 128;                      // rows per Q tile (MMA M)
+constexpr int kPfTiles = 2;                       // Q tiles per CTA
+constexpr int kPfKeys = 64;                       // keys per K/V tile
+constexpr int kPfStages = 3;                      // K/V ring depth
+constexpr int kPfQBytes = kPfRows * 64 * 2;       // 16 KB
+constexpr int kPfKVBytes = kPfKeys * 64 * 2;      // 8 KB (K or V)
+constexpr int kPfPBytes = kPfRows * kPfKeys * 2;  // 16 KB (one P half)
+// Q[2] + K/V ring + P[tile][buffer][hi | lo]
+constexpr int kPfSmemBytes =
+    kPfTiles * kPfQBytes + kPfStages * 2 * kPfKVBytes + kPfTiles * 2 * 2 * kPfPBytes + 1024;
+constexpr int kPfSoftmaxWarps = 16;               // 8 per Q tile, two threads per row
+constexpr int kTmaWarp = kPfSoftmaxWarps, kMmaWarp = kPfSoftmaxWarps + 1;
+constexpr int kPfThreads = (kPfSoftmaxWarps + 2) * 32;
+constexpr uint32_t kPfTmemCols = 512;             // S[tile][2] and O[tile][2], 64 columns each
+
+// acc[0:16] = acc * alpha + (16 TMEM columns of this thread's lane at taddr)
+__device__ __forceinline__ void fold_o16(uint32_t taddr, float* acc, float alpha) {
+    float ot[16];
+    tmem_ld16(taddr, ot);
+    tmem_wait_ld();
+#pragma unroll
+    for (int d = 0; d < 16; ++d) acc[d] = fmaf(acc[d], alpha, ot[d]);
+}
 
 struct PrefillArgs {
-    int t, pos0, n_q, n_kv, group, n_qtiles;
+    int t, pos0, n_q, n_kv, group, n_qblocks;
     float scale_log2;
     uint16_t* out;
     long long out_row_stride;
 };
 
+struct PrefillBars {
+    uint64_t q_full;
+    uint64_t kv_full[kPfStages], kv_empty[kPfStages];
+    uint64_t s_full[kPfTiles][2], s_free[kPfTiles][2];
+    // One P-ready and one O-ready barrier per buffer: a warp that runs one tile
+    // ahead arrives on the other buffer's barrier, never on a phase still in use.
+    uint64_t p_full[kPfTiles][2], o_full[kPfTiles][2];
+    uint64_t mma_done;  // every MMA of the CTA has completed (before TMEM is freed)
+};
+
 template <typename T>
-__global__ void __launch_bounds__(128, 2) attn_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
-                                                              const __grid_constant__ CUtensorMap kmap,
-                                                              const __grid_constant__ CUtensorMap vmap,
-                                                              PrefillArgs a) {
+// 18 warps: two SM sub-partitions host 5 warps each, which caps a thread at 96 registers.
+__global__ void __launch_bounds__(kPfThreads, 1)
+    attn_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
+                        const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap, PrefillArgs a) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t bar_q, bar_s, bar_o;
-    __shared__ uint64_t bar_kv[2];
+    __shared__ PrefillBars bars;
     __shared__ uint32_t tmem_slot;
+    __shared__ volatile int s_err;
+    // Row-max exchange between the two threads of a row, per tile parity (slots 0, 1),
+    // and the final row-sum exchange (slot 2, never shared with a row-max round).
+    __shared__ float xmax[kPfTiles][3][2][kPfRows];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
-    uint8_t* sq = smem;
-    uint8_t* skv = smem + kPfQBytes;  // [buf][K | V]
-    uint8_t* sp = skv + 4 * kPfKVBytes;
+    uint8_t* sq = smem;                                  // [tile] Q
+    uint8_t* skv = sq + kPfTiles * kPfQBytes;            // [stage][K | V]
+    uint8_t* sp = skv + kPfStages * 2 * kPfKVBytes;      // [tile][hi | lo] P
 
     const int h = blockIdx.x, seq = blockIdx.y;
-    const int qt = a.n_qtiles - 1 - (int)blockIdx.z;  // longest tiles first
-    const int q0 = qt * kPfRows;
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int qb = a.n_qblocks - 1 - (int)blockIdx.z;    // longest blocks first
+    const int q0 = qb * kPfTiles * kPfRows;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int kvh = h / a.group;
-    const int rows_valid = min(kPfRows, a.t - q0);
-    const int key_end = a.pos0 + q0 + rows_valid;  // keys [0, key_end) are visible to this tile
-    const int n_tiles = (key_end + kPfKeys - 1) / kPfKeys;
-    const int diag_key = a.pos0 + q0;               // tiles with keys > diag_key need the mask
-    const int my_pos = a.pos0 + q0 + tid;           // absolute position of this thread's row
+    const int kv_plane = seq * a.n_kv + kvh;
+
+    // Per tile: valid rows and the number of K/V tiles it visits (causal).
+    // (Scalars, not arrays: a runtime-indexed array would live in local memory.)
+    const int rows_valid0 = max(0, min(kPfRows, a.t - q0));
+    const int rows_valid1 = max(0, min(kPfRows, a.t - q0 - kPfRows));
+    const int n_tiles0 = rows_valid0 ? (a.pos0 + q0 + rows_valid0 + kPfKeys - 1) / kPfKeys : 0;
+    const int n_tiles1 =
+        rows_valid1 ? (a.pos0 + q0 + kPfRows + rows_valid1 + kPfKeys - 1) / kPfKeys : 0;
+    const int n_kv_tiles = max(n_tiles0, n_tiles1);
+    auto n_tiles = [&](int q) { return q ? n_tiles1 : n_tiles0; };
 
     if (tid == 0) {
-        mbar_init(&bar_q, 1);
-        mbar_init(&bar_s, 1);
-        mbar_init(&bar_o, 1);
-        mbar_init(&bar_kv[0], 1);
-        mbar_init(&bar_kv[1], 1);
+        mbar_init(&bars.q_full, 1);
+        for (int s = 0; s < kPfStages; ++s) {
+            mbar_init(&bars.kv_full[s], 1);
+            mbar_init(&bars.kv_empty[s], 1);
+        }
+        for (int q = 0; q < kPfTiles; ++q) {
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&bars.s_full[q][b], 1);
+                mbar_init(&bars.s_free[q][b], 2 * kPfRows);
+            }
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&bars.p_full[q][b], 2 * kPfRows);
+                mbar_init(&bars.o_full[q][b], 1);
+            }
+        }
+        mbar_init(&bars.mma_done, 1);
+        s_err = 0;
         fence_mbar_init();
     }
-    if (warp == 0) tmem_alloc(&tmem_slot, kPfTmemCols);
+    if (warp == kMmaWarp) tmem_alloc(&tmem_slot, kPfTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-    const uint32_t t_s = tmem, t_o = tmem + 64;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-
     const uint32_t fmt = Elem<T>::kDtype == KVB_BF16 ? 1u : 0u;
-    const uint32_t idesc_s = idesc_f16(kPfRows, kPfKeys, fmt, 0, 0);
-    const uint32_t idesc_o = idesc_f16(kPfRows, 64, fmt, 0, 1);
-    const int kv_plane = seq * a.n_kv + kvh;
 
-    // Error state shared by the CTA so that every thread leaves the tile loop
-    // at the same barrier.
-    __shared__ volatile int s_err;
-    if (tid == 0) s_err = 0;
-    uint32_t kv_issued[2] = {0, 0}, kv_done[2] = {0, 0};  // meaningful in thread 0 only
-    __syncthreads();
-    if (tid == 0) {
-        tma_prefetch_desc(&qmap);
-        mbar_expect_tx(&bar_q, kPfQBytes);
-        tma_load_3d(sq, &qmap, &bar_q, h * 64, q0, seq);
-        for (int j = 0; j < 2 && j < n_tiles; ++j) {
-            mbar_expect_tx(&bar_kv[j], 2 * kPfKVBytes);
-            tma_load_3d(skv + (2 * j) * kPfKVBytes, &kmap, &bar_kv[j], 0, j * kPfKeys, kv_plane);
-            tma_load_3d(skv + (2 * j + 1) * kPfKVBytes, &vmap, &bar_kv[j], 0, j * kPfKeys, kv_plane);
-            kv_issued[j]++;
-        }
-        if (!mbar_wait(&bar_q, 0)) s_err = 1;
-    }
-
-    float oacc[64];
-#pragma unroll
-    for (int d = 0; d < 64; ++d) oacc[d] = 0.f;
-    float m = -INFINITY, l = 0.f;
-    const uint32_t sq_a = smem_u32(sq), sp_a = smem_u32(sp);
-
-    for (int j = 0; j < n_tiles; ++j) {
-        const int buf = j & 1;
-        const uint32_t sk_a = smem_u32(skv + (2 * buf) * kPfKVBytes);
-        const uint32_t sv_a = smem_u32(skv + (2 * buf + 1) * kPfKVBytes);
-        // ---- S = Q K^T
-        if (tid == 0) {
-            if (!s_err) {
-                if (mbar_wait(&bar_kv[buf], kv_done[buf] & 1))
-                    kv_done[buf]++;
-                else
+    if (warp == kTmaWarp) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&kmap);
+            tma_prefetch_desc(&vmap);
+            const int nq_tiles = rows_valid1 ? 2 : 1;
+            mbar_expect_tx(&bars.q_full, nq_tiles * kPfQBytes);
+            for (int q = 0; q < nq_tiles; ++q)
+                tma_load_3d(sq + q * kPfQBytes, &qmap, &bars.q_full, h * 64, q0 + q * kPfRows, seq);
+            int issued = 0;
+            for (int j = 0; j < n_kv_tiles; ++j) {
+                const int st = j % kPfStages;
+                if (j >= kPfStages && !mbar_wait(&bars.kv_empty[st], ((j - kPfStages) / kPfStages) & 1)) {
                     s_err = 1;
+                    break;
+                }
+                if (s_err) break;
+                mbar_expect_tx(&bars.kv_full[st], 2 * kPfKVBytes);
+                tma_load_3d(skv + (2 * st) * kPfKVBytes, &kmap, &bars.kv_full[st], 0, j * kPfKeys,
+                            kv_plane);
+                tma_load_3d(skv + (2 * st + 1) * kPfKVBytes, &vmap, &bars.kv_full[st], 0,
+                            j * kPfKeys, kv_plane);
+                issued = j + 1;
             }
-            tc_fence_after();
-            if (!s_err) {
+            if (s_err) {
+                // let every copy this CTA issued land before the CTA exits (bounded)
+                for (int j = max(0, issued - kPfStages); j < issued; ++j)
+                    mbar_wait(&bars.kv_full[j % kPfStages], (j / kPfStages) & 1);
+                mbar_wait(&bars.q_full, 0);
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc_s = idesc_f16(kPfRows, kPfKeys, fmt, 0, 0);
+            const uint32_t idesc_o = idesc_f16(kPfRows, 64, fmt, 0, 1);
+            const uint32_t sq_a = smem_u32(sq), skv_a = smem_u32(skv), sp_a = smem_u32(sp);
+            auto t_s = [&](int q, int b) { return tmem + (uint32_t)((q * 2 + b) * 64); };
+            auto t_o = [&](int q, int b) { return tmem + (uint32_t)(256 + (q * 2 + b) * 64); };
+            auto issue_s = [&](int q, int j) -> bool {  // S_q[j & 1] = Q_q K_j^T
+                const int st = j % kPfStages, b = j & 1;
+                if (j >= 2 && !mbar_wait(&bars.s_free[q][b], ((j - 2) >> 1) & 1)) return false;
+                tc_fence_after();
+                const uint32_t k_a = skv_a + (2 * st) * kPfKVBytes;
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks)
-                    umma_f16(t_s, sdesc_sw128(sq_a + 32 * ks, 16, 1024),
-                             sdesc_sw128(sk_a + 32 * ks, 16, 1024), idesc_s, ks > 0);
+                    umma_f16(t_s(q, b), sdesc_sw128(sq_a + q * kPfQBytes + 32 * ks, 16, 1024),
+                             sdesc_sw128(k_a + 32 * ks, 16, 1024), idesc_s, ks > 0);
+                umma_commit(&bars.s_full[q][b]);
+                return true;
+            };
+            auto issue_pv = [&](int q, int j) -> bool {  // O_q[j&1] = P_q,hi V_j + P_q,lo V_j
+                const int st = j % kPfStages, b = j & 1;
+                if (!mbar_wait(&bars.p_full[q][b], (j >> 1) & 1)) return false;
+                tc_fence_after();
+                const uint32_t v_a = skv_a + (2 * st + 1) * kPfKVBytes;
+                const uint32_t p_a = sp_a + (q * 2 + b) * 2 * kPfPBytes;
+#pragma unroll
+                for (int half = 0; half < 2; ++half)
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+                        umma_f16(t_o(q, b), sdesc_sw128(p_a + half * kPfPBytes + 32 * ks, 16, 1024),
+                                 sdesc_sw128(v_a + ks * 16 * 128, 64 * 128, 1024), idesc_o,
+                                 (half | ks) != 0);
+                umma_commit(&bars.o_full[q][b]);
+                return true;
+            };
+            bool ok = mbar_wait(&bars.q_full, 0);
+            // prologue: S for tile 0 of both Q tiles
+            if (ok) ok = mbar_wait(&bars.kv_full[0], 0);
+            for (int q = 0; q < kPfTiles && ok; ++q)
+                if (n_tiles(q) > 0) ok = issue_s(q, 0);
+            // Per K/V tile j: first S(j+1) for both tiles (their S buffers were read by
+            // softmax one tile ago), then P(j) V for both as their P arrive -- so the
+            // next S is ready when a softmax warpgroup finishes with the current one.
+            for (int j = 0; j < n_kv_tiles && ok; ++j) {
+                if (j + 1 < n_kv_tiles)
+                    ok = mbar_wait(&bars.kv_full[(j + 1) % kPfStages], ((j + 1) / kPfStages) & 1);
+                for (int q = 0; q < kPfTiles && ok; ++q)
+                    if (j + 1 < n_tiles(q)) ok = issue_s(q, j + 1);
+                for (int q = 0; q < kPfTiles && ok; ++q) {
+                    if (j < n_tiles(q)) ok = issue_pv(q, j);
+                    if (s_err) ok = false;
+                }
+                if (ok) umma_commit(&bars.kv_empty[j % kPfStages]);  // stage j free once all MMAs so far finish
             }
-            umma_commit(&bar_s);  // arrives even when nothing was issued
+            if (!ok) s_err = 1;
+            // No MMA may still be running when TMEM is released below.
+            umma_commit(&bars.mma_done);
+            mbar_wait(&bars.mma_done, 0);
         }
-        if (!mbar_wait(&bar_s, j & 1)) s_err = 1;
-        tc_fence_after();
-        // ---- softmax on this thread's row
-        float s[64];
-        tmem_ld32(t_s + lane_off, s);
-        tmem_ld32(t_s + lane_off + 32, s + 32);
-        tmem_wait_ld();
-        const bool need_mask = j * kPfKeys + kPfKeys - 1 > diag_key;
-        float mx = -INFINITY;
+    } else {
+        // ------------------------------------------------------------ softmax warps
+        // Two threads per query row: warps 8q..8q+3 take columns 0-31 and warps
+        // 8q+4..8q+7 columns 32-63 of the same 128 TMEM lanes.  The row maximum is
+        // exchanged once per tile through shared memory (a 64-thread named barrier
+        // per warp pair); the row sum stays per thread until the end.  Error
+        // decisions are exchanged through the same barrier, so both threads of a
+        // row always take the same number of barrier steps.
+        const int q = warp >> 3;                // Q tile
+        const int half = (warp >> 2) & 1;       // column half of the S / O tiles
+        const int quarter = warp & 3;           // TMEM lane quarter
+        const int row = quarter * 32 + lane;    // row of the tile (= TMEM lane)
+        const int col0 = half * 32;
+        const uint32_t bar_id = 1 + q * 4 + quarter;
+        const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+        auto t_o = [&](int b) {
+            return tmem + (uint32_t)(256 + (q * 2 + b) * 64 + col0) + lane_off;
+        };
+        const int my_pos = a.pos0 + q0 + q * kPfRows + row;
+        const int diag_key = a.pos0 + q0 + q * kPfRows;  // keys above need the causal mask
+        const int nt = n_tiles(q);
+        float oacc[32];
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-            float v = s[c] * a.scale_log2;
-            if (need_mask && j * kPfKeys + c > my_pos) v = -INFINITY;
-            s[c] = v;
-            mx = fmaxf(mx, v);
+        for (int d = 0; d < 32; ++d) oacc[d] = 0.f;
+        float m = -INFINITY, l = 0.f, alpha_pending = 1.f;
+        bool ok = true;
+        for (int j = 0; j < nt; ++j) {
+            const int b = j & 1;
+            const bool good = ok && !s_err && mbar_wait(&bars.s_full[q][b], (j >> 1) & 1);
+            float s[32];
+            float mx = -INFINITY;
+            if (good) {
+                tc_fence_after();
+                tmem_ld32(tmem + (uint32_t)((q * 2 + b) * 64 + col0) + lane_off, s);
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(&bars.s_free[q][b]);
+                if (j * kPfKeys + kPfKeys - 1 > diag_key) {
+#pragma unroll
+                    for (int c = 0; c < 32; ++c)
+                        if (j * kPfKeys + col0 + c > my_pos) s[c] = -INFINITY;
+                }
+                float mx4[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) mx4[i] = s[i];
+#pragma unroll
+                for (int c = 4; c < 32; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+                mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+            }
+            xmax[q][b][half][row] = good ? mx : __int_as_float(0x7fffffff);  // NaN = failed
+            named_bar_sync(bar_id, 64);
+            const float pmx = xmax[q][b][half ^ 1][row];
+            if (!good || isnan(pmx)) ok = false;
+            if (!ok) continue;
+            // Raw scores: the max is taken before scaling (the scale is positive).
+            const float mn = fmaxf(m, fmaxf(mx, pmx) * a.scale_log2);  // running max, log2
+            const float alpha = ex2_approx(m - mn);
+            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+                s[c] = ex2_approx(fmaf(s[c], a.scale_log2, -mn));  // exp2(s*scale - max)
+                sum4[c & 3] += s[c];
+            }
+            l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+            m = mn;
+            // P_j -> shared buffer j&1 (PV_{j-2}, its last reader, completed: o_full was
+            // waited for it in the previous iteration).  16-byte chunk ch of row r at
+            // r*128 + ((ch ^ (r & 7)) * 16); this thread owns chunks 4*half .. 4*half+3.
+            {
+                uint8_t* prow_h = sp + (q * 2 + b) * 2 * kPfPBytes + row * 128;
+                uint8_t* prow_l = prow_h + kPfPBytes;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    uint4 vh, vl;
+                    split_pack<T>(s[8 * k + 0], s[8 * k + 1], vh.x, vl.x);
+                    split_pack<T>(s[8 * k + 2], s[8 * k + 3], vh.y, vl.y);
+                    split_pack<T>(s[8 * k + 4], s[8 * k + 5], vh.z, vl.z);
+                    split_pack<T>(s[8 * k + 6], s[8 * k + 7], vh.w, vl.w);
+                    const int ch = (4 * half + k) ^ (row & 7);
+                    *reinterpret_cast<uint4*>(prow_h + (ch << 4)) = vh;
+                    *reinterpret_cast<uint4*>(prow_l + (ch << 4)) = vl;
+                }
+            }
+            fence_async_smem();
+            tc_fence_before();
+            mbar_arrive(&bars.p_full[q][b]);
+            if (j > 0) {  // fold the previous tile's P V (TMEM buffer (j-1)&1)
+                if (s_err || !mbar_wait(&bars.o_full[q][b ^ 1], ((j - 1) >> 1) & 1)) {
+                    ok = false;
+                    continue;
+                }
+                tc_fence_after();
+                fold_o16(t_o(b ^ 1), oacc, alpha_pending);
+                fold_o16(t_o(b ^ 1) + 16, oacc + 16, alpha_pending);
+                tc_fence_before();
+            }
+            alpha_pending = alpha;
         }
-        const float mn = fmaxf(m, mx);
-        const float alpha = exp2f(m - mn);
-        float sum = 0.f;
+        if (nt > 0) {
+            const bool good = ok && !s_err &&
+                              mbar_wait(&bars.o_full[q][(nt - 1) & 1], ((nt - 1) >> 1) & 1);
+            if (good) {
+                tc_fence_after();
+                fold_o16(t_o((nt - 1) & 1), oacc, alpha_pending);
+                fold_o16(t_o((nt - 1) & 1) + 16, oacc + 16, alpha_pending);
+            }
+            xmax[q][2][half][row] = good ? l : __int_as_float(0x7fffffff);
+            named_bar_sync(bar_id, 64);
+            const float pl = xmax[q][2][half ^ 1][row];
+            if (good && !isnan(pl)) {
+                if (row < (q ? rows_valid1 : rows_valid0)) {
+                    const float inv = 1.f / (l + pl);
+                    T* orow = reinterpret_cast<T*>(a.out) +
+                              ((size_t)seq * a.t + q0 + q * kPfRows + row) * a.out_row_stride +
+                              (size_t)h * 64 + col0;
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-            s[c] = exp2f(s[c] - mn);
-            sum += s[c];
-        }
-        l = l * alpha + sum;
-        m = mn;
-        // P row -> shared memory as two 16-bit tiles, head and remainder
-        // (P = hi + lo, see split_pack), each 128B-swizzled K-major: 16-byte
-        // chunk ch of row r at r*128 + ((ch ^ (r & 7)) * 16).
-        {
-            uint8_t* prow_h = sp + tid * 128;
-            uint8_t* prow_l = sp + kPfPBytes + tid * 128;
+                    for (int k = 0; k < 4; ++k) {
+                        float f[8];
 #pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-                uint4 vh, vl;
-                split_pack<T>(s[8 * ch + 0], s[8 * ch + 1], vh.x, vl.x);
-                split_pack<T>(s[8 * ch + 2], s[8 * ch + 3], vh.y, vl.y);
-                split_pack<T>(s[8 * ch + 4], s[8 * ch + 5], vh.z, vl.z);
-                split_pack<T>(s[8 * ch + 6], s[8 * ch + 7], vh.w, vl.w);
-                *reinterpret_cast<uint4*>(prow_h + ((ch ^ (tid & 7)) << 4)) = vh;
-                *reinterpret_cast<uint4*>(prow_l + ((ch ^ (tid & 7)) << 4)) = vl;
+                        for (int e = 0; e < 8; ++e) f[e] = oacc[8 * k + e] * inv;
+                        *reinterpret_cast<uint4*>(orow + 8 * k) = pack8<T>(f);
+                    }
+                }
+            } else {
+                s_err = 1;
             }
         }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        // ---- O_t = P_hi V + P_lo V
-        if (tid == 0) {
-            tc_fence_after();
-            if (!s_err) {
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks)
-                    umma_f16(t_o, sdesc_sw128(sp_a + 32 * ks, 16, 1024),
-                             sdesc_sw128(sv_a + ks * 16 * 128, 64 * 128, 1024), idesc_o, ks > 0);
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks)
-                    umma_f16(t_o, sdesc_sw128(sp_a + kPfPBytes + 32 * ks, 16, 1024),
-                             sdesc_sw128(sv_a + ks * 16 * 128, 64 * 128, 1024), idesc_o, 1);
-            }
-            umma_commit(&bar_o);
-        }
-        if (!mbar_wait(&bar_o, j & 1)) s_err = 1;
-        tc_fence_after();
-        if (tid == 0 && !s_err && j + 2 < n_tiles) {  // both MMAs on this buffer are done
-            mbar_expect_tx(&bar_kv[buf], 2 * kPfKVBytes);
-            tma_load_3d(skv + (2 * buf) * kPfKVBytes, &kmap, &bar_kv[buf], 0, (j + 2) * kPfKeys,
-                        kv_plane);
-            tma_load_3d(skv + (2 * buf + 1) * kPfKVBytes, &vmap, &bar_kv[buf], 0,
-                        (j + 2) * kPfKeys, kv_plane);
-            kv_issued[buf]++;
-        }
-        float ot[64];
-        tmem_ld32(t_o + lane_off, ot);
-        tmem_ld32(t_o + lane_off + 32, ot + 32);
-        tmem_wait_ld();
-#pragma unroll
-        for (int d = 0; d < 64; ++d) oacc[d] = oacc[d] * alpha + ot[d];
-        tc_fence_before();
-        __syncthreads();
-        if (s_err) break;  // read after the barrier: the same value in every thread
-    }
-    const bool ok = !s_err;
-    if (!ok && tid == 0) {
-        // Give every copy this CTA issued a bounded chance to land before exit.
-        for (int b2 = 0; b2 < 2; ++b2)
-            while (kv_done[b2] < kv_issued[b2]) {
-                mbar_wait(&bar_kv[b2], kv_done[b2] & 1);
-                kv_done[b2]++;
-            }
-        mbar_wait(&bar_q, 0);
-    }
-
-    // ---- epilogue: normalise and store this thread's row
-    if (ok && tid < rows_valid) {
-        const float inv = 1.f / l;
-        T* orow = reinterpret_cast<T*>(a.out) + ((size_t)seq * a.t + q0 + tid) * a.out_row_stride +
-                  (size_t)h * 64;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = oacc[8 * ch + e] * inv;
-            *reinterpret_cast<uint4*>(orow + 8 * ch) = pack8<T>(f);
-        }
+        if (!ok) s_err = 1;
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) {
+    if (warp == kMmaWarp) {
         tc_fence_after();
         tmem_dealloc(tmem, kPfTmemCols);
     }

@@ -271,17 +271,19 @@ static int launch_prefill(kvb_stream_t stream, const void* qkv, const void* kc, 
     a.n_q = (int)n_q;
     a.n_kv = (int)n_kv;
     a.group = (int)(n_q / n_kv);
-    a.n_qtiles = (int)((t + kPfRows - 1) / kPfRows);
+    const size_t rows_per_block = (size_t)kPfTiles * kPfRows;
+    a.n_qblocks = (int)((t + rows_per_block - 1) / rows_per_block);
     a.scale_log2 = (1.0f / sqrtf(64.0f)) * 1.4426950408889634f;
     a.out = static_cast<uint16_t*>(out);
     a.out_row_stride = (long long)(n_q * 64);
-    dim3 grid((unsigned)n_q, (unsigned)n_seq, (unsigned)a.n_qtiles);
+    dim3 grid((unsigned)n_q, (unsigned)n_seq, (unsigned)a.n_qblocks);
     if (dtype == KVB_BF16) {
         set_max_smem(attn_prefill_kernel<__nv_bfloat16>, kPfSmemBytes);
-        attn_prefill_kernel<__nv_bfloat16><<<grid, 128, kPfSmemBytes, stream>>>(qmap, kmap, vmap, a);
+        attn_prefill_kernel<__nv_bfloat16><<<grid, kPfThreads, kPfSmemBytes, stream>>>(qmap, kmap,
+                                                                                       vmap, a);
     } else {
         set_max_smem(attn_prefill_kernel<__half>, kPfSmemBytes);
-        attn_prefill_kernel<__half><<<grid, 128, kPfSmemBytes, stream>>>(qmap, kmap, vmap, a);
+        attn_prefill_kernel<__half><<<grid, kPfThreads, kPfSmemBytes, stream>>>(qmap, kmap, vmap, a);
     }
     KVB_CHECK_LAUNCH("attention prefill launch");
     return KVB_OK;

@@ -7,7 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/kvasir_b200.h"
+#include "kvasir_b200.h"  // include/ (on the compiler's include path)
 
 namespace kvb {
 

@@ -8,7 +8,7 @@
 #include <stddef.h>
 #include <stdint.h>
 
-#include "../../include/kvasir_b200.h"
+#include "kvasir_b200.h"  // include/ (on the compiler's include path)
 
 namespace kvb {
 
