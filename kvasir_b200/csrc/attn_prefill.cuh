@@ -27,13 +27,11 @@ namespace kvb {
 constexpr int kPfRows = 128;                      // rows per Q tile (MMA M)
 constexpr int kPfTiles = 2;                       // Q tiles per CTA
 constexpr int kPfKeys = 64;                       // keys per K/V tile
-constexpr int kPfStages = 3;                      // K/V ring depth
+constexpr int kPfStages = 6;                      // K/V ring depth
 constexpr int kPfQBytes = kPfRows * 64 * 2;       // 16 KB
 constexpr int kPfKVBytes = kPfKeys * 64 * 2;      // 8 KB (K or V)
-constexpr int kPfPBytes = kPfRows * kPfKeys * 2;  // 16 KB (one P half)
-// Q[2] + K/V ring + P[tile][buffer][hi | lo]
-constexpr int kPfSmemBytes =
-    kPfTiles * kPfQBytes + kPfStages * 2 * kPfKVBytes + kPfTiles * 2 * 2 * kPfPBytes + 1024;
+// Q[2] + K/V ring (P lives in TMEM, over the S columns it was computed from)
+constexpr int kPfSmemBytes = kPfTiles * kPfQBytes + kPfStages * 2 * kPfKVBytes + 1024;
 constexpr int kPfSoftmaxWarps = 16;               // 8 per Q tile, two threads per row
 constexpr int kTmaWarp = kPfSoftmaxWarps, kMmaWarp = kPfSoftmaxWarps + 1;
 constexpr int kPfThreads = (kPfSoftmaxWarps + 2) * 32;
@@ -58,7 +56,7 @@ struct PrefillArgs {
 struct PrefillBars {
     uint64_t q_full;
     uint64_t kv_full[kPfStages], kv_empty[kPfStages];
-    uint64_t s_full[kPfTiles][2], s_free[kPfTiles][2];
+    uint64_t s_full[kPfTiles][2];
     // One P-ready and one O-ready barrier per buffer: a warp that runs one tile
     // ahead arrives on the other buffer's barrier, never on a phase still in use.
     uint64_t p_full[kPfTiles][2], o_full[kPfTiles][2];
@@ -82,7 +80,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                                ~uintptr_t(1023));
     uint8_t* sq = smem;                                  // [tile] Q
     uint8_t* skv = sq + kPfTiles * kPfQBytes;            // [stage][K | V]
-    uint8_t* sp = skv + kPfStages * 2 * kPfKVBytes;      // [tile][hi | lo] P
 
     const int h = blockIdx.x, seq = blockIdx.y;
     const int qb = a.n_qblocks - 1 - (int)blockIdx.z;    // longest blocks first
@@ -110,9 +107,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         for (int q = 0; q < kPfTiles; ++q) {
             for (int b = 0; b < 2; ++b) {
                 mbar_init(&bars.s_full[q][b], 1);
-                mbar_init(&bars.s_free[q][b], 2 * kPfRows);
-            }
-            for (int b = 0; b < 2; ++b) {
                 mbar_init(&bars.p_full[q][b], 2 * kPfRows);
                 mbar_init(&bars.o_full[q][b], 1);
             }
@@ -164,34 +158,42 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (lane == 0) {
             const uint32_t idesc_s = idesc_f16(kPfRows, kPfKeys, fmt, 0, 0);
             const uint32_t idesc_o = idesc_f16(kPfRows, 64, fmt, 0, 1);
-            const uint32_t sq_a = smem_u32(sq), skv_a = smem_u32(skv), sp_a = smem_u32(sp);
-            auto t_s = [&](int q, int b) { return tmem + (uint32_t)((q * 2 + b) * 64); };
-            auto t_o = [&](int q, int b) { return tmem + (uint32_t)(256 + (q * 2 + b) * 64); };
-            auto issue_s = [&](int q, int j) -> bool {  // S_q[j & 1] = Q_q K_j^T
+            // Descriptors are built once; per MMA only the 16-byte start-address field
+            // (bits 0-13) moves, by adding a constant: issue cost, not the tensor core,
+            // otherwise bounds a single issuing thread at these small N.
+            const uint64_t dq0 = sdesc_sw128(smem_u32(sq), 16, 1024);
+            const uint64_t dk0 = sdesc_sw128(smem_u32(skv), 16, 1024);
+            const uint64_t dv0 = sdesc_sw128(smem_u32(skv) + kPfKVBytes, 64 * 128, 1024);
+            constexpr uint64_t kQTile = kPfQBytes >> 4, kStage = (2 * kPfKVBytes) >> 4;
+            // S_q[j & 1] = Q_q K_j^T.  Buffer j&1 last held P(j-2), read by P(j-2) V, which
+            // this thread issued earlier: MMAs of one thread run in issue order.
+            auto issue_s = [&](int q, int j) {
                 const int st = j % kPfStages, b = j & 1;
-                if (j >= 2 && !mbar_wait(&bars.s_free[q][b], ((j - 2) >> 1) & 1)) return false;
-                tc_fence_after();
-                const uint32_t k_a = skv_a + (2 * st) * kPfKVBytes;
-#pragma unroll
-                for (int ks = 0; ks < 4; ++ks)
-                    umma_f16(t_s(q, b), sdesc_sw128(sq_a + q * kPfQBytes + 32 * ks, 16, 1024),
-                             sdesc_sw128(k_a + 32 * ks, 16, 1024), idesc_s, ks > 0);
+                const uint32_t d = tmem + (uint32_t)((q * 2 + b) * 64);
+                const uint64_t da = dq0 + kQTile * q, db = dk0 + kStage * st;
+                umma_f16(d, da, db, idesc_s, 0);
+                umma_f16(d, da + 2, db + 2, idesc_s, 1);  // +32 bytes: next 16 dims
+                umma_f16(d, da + 4, db + 4, idesc_s, 1);
+                umma_f16(d, da + 6, db + 6, idesc_s, 1);
                 umma_commit(&bars.s_full[q][b]);
-                return true;
             };
-            auto issue_pv = [&](int q, int j) -> bool {  // O_q[j&1] = P_q,hi V_j + P_q,lo V_j
+            // O_q[j&1] = P_q,hi V_j + P_q,lo V_j with P read from TMEM (the S buffer:
+            // P_hi in its columns 0-31, P_lo in 32-63, two keys per column).
+            auto issue_pv = [&](int q, int j) -> bool {
                 const int st = j % kPfStages, b = j & 1;
                 if (!mbar_wait(&bars.p_full[q][b], (j >> 1) & 1)) return false;
                 tc_fence_after();
-                const uint32_t v_a = skv_a + (2 * st + 1) * kPfKVBytes;
-                const uint32_t p_a = sp_a + (q * 2 + b) * 2 * kPfPBytes;
-#pragma unroll
-                for (int half = 0; half < 2; ++half)
-#pragma unroll
-                    for (int ks = 0; ks < 4; ++ks)
-                        umma_f16(t_o(q, b), sdesc_sw128(p_a + half * kPfPBytes + 32 * ks, 16, 1024),
-                                 sdesc_sw128(v_a + ks * 16 * 128, 64 * 128, 1024), idesc_o,
-                                 (half | ks) != 0);
+                const uint32_t d = tmem + (uint32_t)(256 + (q * 2 + b) * 64);
+                const uint32_t p = tmem + (uint32_t)((q * 2 + b) * 64);
+                const uint64_t dv = dv0 + kStage * st;  // +2048 bytes (>> 4 = 128): next 16 keys
+                umma_f16_ts(d, p + 0, dv + 0, idesc_o, 0);
+                umma_f16_ts(d, p + 8, dv + 128, idesc_o, 1);
+                umma_f16_ts(d, p + 16, dv + 256, idesc_o, 1);
+                umma_f16_ts(d, p + 24, dv + 384, idesc_o, 1);
+                umma_f16_ts(d, p + 32, dv + 0, idesc_o, 1);
+                umma_f16_ts(d, p + 40, dv + 128, idesc_o, 1);
+                umma_f16_ts(d, p + 48, dv + 256, idesc_o, 1);
+                umma_f16_ts(d, p + 56, dv + 384, idesc_o, 1);
                 umma_commit(&bars.o_full[q][b]);
                 return true;
             };
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             // prologue: S for tile 0 of both Q tiles
             if (ok) ok = mbar_wait(&bars.kv_full[0], 0);
             for (int q = 0; q < kPfTiles && ok; ++q)
-                if (n_tiles(q) > 0) ok = issue_s(q, 0);
+                if (n_tiles(q) > 0) issue_s(q, 0);
             // Per K/V tile j: first S(j+1) for both tiles (their S buffers were read by
             // softmax one tile ago), then P(j) V for both as their P arrive -- so the
             // next S is ready when a softmax warpgroup finishes with the current one.
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 if (j + 1 < n_kv_tiles)
                     ok = mbar_wait(&bars.kv_full[(j + 1) % kPfStages], ((j + 1) / kPfStages) & 1);
                 for (int q = 0; q < kPfTiles && ok; ++q)
-                    if (j + 1 < n_tiles(q)) ok = issue_s(q, j + 1);
+                    if (j + 1 < n_tiles(q)) issue_s(q, j + 1);
                 for (int q = 0; q < kPfTiles && ok; ++q) {
                     if (j < n_tiles(q)) ok = issue_pv(q, j);
                     if (s_err) ok = false;
@@ -250,12 +252,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const bool good = ok && !s_err && mbar_wait(&bars.s_full[q][b], (j >> 1) & 1);
             float s[32];
             float mx = -INFINITY;
+            const uint32_t t_sp = tmem + (uint32_t)((q * 2 + b) * 64) + lane_off;  // S, then P
             if (good) {
                 tc_fence_after();
-                tmem_ld32(tmem + (uint32_t)((q * 2 + b) * 64 + col0) + lane_off, s);
+                tmem_ld32(t_sp + col0, s);
                 tmem_wait_ld();
-                tc_fence_before();
-                mbar_arrive(&bars.s_free[q][b]);
                 if (j * kPfKeys + kPfKeys - 1 > diag_key) {
 #pragma unroll
                     for (int c = 0; c < 32; ++c)
@@ -284,25 +285,25 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
             m = mn;
-            // P_j -> shared buffer j&1 (PV_{j-2}, its last reader, completed: o_full was
-            // waited for it in the previous iteration).  16-byte chunk ch of row r at
-            // r*128 + ((ch ^ (r & 7)) * 16); this thread owns chunks 4*half .. 4*half+3.
+            // P_j -> TMEM over the S columns it came from: P_hi (two keys per 32-bit
+            // column) in columns 16*half .. +15, P_lo in 32 + 16*half .. +15.  Both
+            // threads of the row have their S in registers (the max exchange above
+            // came after both loads), so overwriting S here is safe.
             {
-                uint8_t* prow_h = sp + (q * 2 + b) * 2 * kPfPBytes + row * 128;
-                uint8_t* prow_l = prow_h + kPfPBytes;
+                uint32_t pk[16];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    uint4 vh, vl;
-                    split_pack<T>(s[8 * k + 0], s[8 * k + 1], vh.x, vl.x);
-                    split_pack<T>(s[8 * k + 2], s[8 * k + 3], vh.y, vl.y);
-                    split_pack<T>(s[8 * k + 4], s[8 * k + 5], vh.z, vl.z);
-                    split_pack<T>(s[8 * k + 6], s[8 * k + 7], vh.w, vl.w);
-                    const int ch = (4 * half + k) ^ (row & 7);
-                    *reinterpret_cast<uint4*>(prow_h + (ch << 4)) = vh;
-                    *reinterpret_cast<uint4*>(prow_l + (ch << 4)) = vl;
+                for (int k = 0; k < 16; ++k) {  // heads; s keeps the remainders
+                    pk[k] = Elem<T>::pack(s[2 * k], s[2 * k + 1]);
+                    const float2 hv = Elem<T>::unpack(pk[k]);
+                    s[2 * k] -= hv.x;
+                    s[2 * k + 1] -= hv.y;
                 }
+                tmem_st16(t_sp + 16 * half, pk);
+#pragma unroll
+                for (int k = 0; k < 16; ++k) pk[k] = Elem<T>::pack(s[2 * k], s[2 * k + 1]);
+                tmem_st16(t_sp + 32 + 16 * half, pk);
+                tmem_wait_st();
             }
-            fence_async_smem();
             tc_fence_before();
             mbar_arrive(&bars.p_full[q][b]);
             if (j > 0) {  // fold the previous tile's P V (TMEM buffer (j-1)&1)
