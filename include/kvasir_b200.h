@@ -149,6 +149,17 @@ int kvb_rope_kv_append_batched(kvb_stream_t stream, void* qkv, size_t n_seq, con
                                size_t n_q, size_t n_kv, size_t head_dim, size_t max_seq,
                                int dtype);
 
+/* Batched prefill form, one launch for n_seq sequences of t rows each, all
+ * starting at pos0 (the layout kvb_attention_prefill reads): qkv is
+ * [n_seq * t, (n_q + 2 n_kv) * head_dim]; sequence b's cache is kc/vc +
+ * b * n_kv * max_seq * head_dim, cache_len = n_seq * n_kv * max_seq * head_dim.
+ * Equal, bit for bit, to kvb_rope_kv_append on each sequence in turn. */
+int kvb_rope_kv_append_prefill(kvb_stream_t stream, void* qkv, size_t qkv_len,
+                               const float* cos_t, const float* sin_t, size_t table_len, void* kc,
+                               void* vc, size_t cache_len, size_t n_seq, size_t t, size_t pos0,
+                               size_t n_q, size_t n_kv, size_t head_dim, size_t max_seq,
+                               int dtype);
+
 /* kvb_add_inplace(x, y) followed by kvb_rmsnorm(x, w, out): the residual
  * stream x is updated in place and its normalised copy written to out. */
 int kvb_add_rmsnorm(kvb_stream_t stream, void* x, size_t x_len, const void* y, size_t y_len,

@@ -2,8 +2,10 @@
 
 Each config prints one JSON line per measured item.  Device times are CUDA
 events on the launching stream after warm-up; HBM-bound kernels whose working
-set fits in L2 are timed one launch at a time with a 256 MB L2 flush between
-launches (the flush is outside the timed interval).  CPU numbers are the
+set fits in L2 are timed one launch at a time with an L2 flush between
+launches (a 256 MB write, then a 256 MB read so that no dirty flush line is
+left for the timed launch to write back; the flush is outside the timed
+interval).  CPU numbers are the
 oracle (oracle/, the reference's CPU-reference computations restated) on all
 host cores, timed on the same inputs or a stated sample.
 """
@@ -33,11 +35,18 @@ def _peaks():
 
 
 class _Flusher:
+    """L2 flush between timed launches: write a 256 MB buffer, then read another
+    256 MB buffer.  The write evicts the previous launch's lines; the read leaves
+    L2 holding clean lines only, so the timed launch does not pay for writing
+    the flush's own dirty lines back to HBM."""
+
     def __init__(self):
-        self.buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        self.wbuf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+        self.rbuf = torch.ones(64 << 20, dtype=torch.float32, device="cuda")
 
     def __call__(self):
-        self.buf.zero_()
+        self.wbuf.zero_()
+        torch.sum(self.rbuf)
 
 
 def time_each(fn, reps: int, flush=None) -> float:
@@ -235,13 +244,9 @@ def cfg3(args):
     c, s = cos_sin_table(cfg, T)
     cos, sin = torch.from_numpy(c).cuda(), torch.from_numpy(s).cuda()
     per_seq = T * cfg.qkv_dim
-    per_cache = nkv * T * hd
 
-    def rope_all():
-        for b in range(n_seq):
-            g.rope_kv_append(qkv_work[b * per_seq:(b + 1) * per_seq], cos, sin,
-                             kc[b * per_cache:(b + 1) * per_cache],
-                             vc[b * per_cache:(b + 1) * per_cache], T, 0, nq, nkv, hd, T)
+    def rope_all():  # one launch over the 4 sequences
+        g.rope_kv_append_prefill(qkv_work, cos, sin, kc, vc, n_seq, T, 0, nq, nkv, hd, T)
 
     def rope_reset():
         qkv_work.copy_(qkv)

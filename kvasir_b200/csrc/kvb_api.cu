@@ -495,25 +495,28 @@ int kvb_kv_append(kvb_stream_t stream, const void* qkv, size_t qkv_len, void* kc
     return launch_rope(stream, a, (int)t, dtype, vec);
 }
 
-int kvb_rope_kv_append(kvb_stream_t stream, void* qkv, size_t qkv_len, const float* cos_t,
-                       const float* sin_t, size_t table_len, void* kc, void* vc, size_t cache_len,
-                       size_t t, size_t pos0, size_t n_q, size_t n_kv, size_t head_dim,
-                       size_t max_seq, int dtype) {
+// n_seq sequences of t rows each, all starting at pos0; sequence b's cache is
+// kc/vc + b * n_kv * max_seq * head_dim.
+static int rope_kv_append_seqs(kvb_stream_t stream, void* qkv, size_t qkv_len, const float* cos_t,
+                               const float* sin_t, size_t table_len, void* kc, void* vc,
+                               size_t cache_len, size_t n_seq, size_t t, size_t pos0, size_t n_q,
+                               size_t n_kv, size_t head_dim, size_t max_seq, int dtype) {
     KVB_CHECK_DTYPE(dtype);
     const size_t stride = (n_q + 2 * n_kv) * head_dim;
     KVB_CHECK(head_dim > 0 && head_dim % 2 == 0, "rope: odd head_dim %zu", head_dim);
-    KVB_CHECK(qkv_len == t * stride, "rope_kv_append: qkv has %zu elems, want %zux%zu", qkv_len, t,
-              stride);
+    KVB_CHECK(qkv_len == n_seq * t * stride, "rope_kv_append: qkv has %zu elems, want %zux%zux%zu",
+              qkv_len, n_seq, t, stride);
     KVB_CHECK(table_len % (head_dim / 2) == 0, "rope: bad cos/sin table sizes");
     const size_t max_pos = table_len / (head_dim / 2);
     KVB_CHECK(pos0 + t <= max_pos, "rope: positions up to %zu exceed table of %zu", pos0 + t, max_pos);
-    KVB_CHECK(cache_len == n_kv * max_seq * head_dim, "kv_append: bad cache sizes");
+    const size_t per_seq = n_kv * max_seq * head_dim;
+    KVB_CHECK(cache_len == n_seq * per_seq, "kv_append: bad cache sizes");
     KVB_CHECK(pos0 + t <= max_seq, "kv_append: positions up to %zu exceed max_seq %zu", pos0 + t,
               max_seq);
-    KVB_CHECK(fits_i32(pos0) && fits_i32(stride) && fits_i32(t) && fits_i32(max_seq) &&
-                  fits_i32(max_pos),
+    KVB_CHECK(fits_i32(pos0) && fits_i32(stride) && fits_i32(t) && fits_i32(n_seq * t) &&
+                  fits_i32(max_seq) && fits_i32(max_pos),
               "rope_kv_append: a dimension does not fit in i32");
-    if (t == 0) return KVB_OK;
+    if (t == 0 || n_seq == 0) return KVB_OK;
     RopeArgs a = rope_args(qkv, n_q, n_kv, head_dim);
     a.rows_per_seq = (int)t;
     a.pos0 = (int)pos0;
@@ -522,12 +525,30 @@ int kvb_rope_kv_append(kvb_stream_t stream, void* qkv, size_t qkv_len, const flo
     a.max_pos = (int)max_pos;
     a.kc = static_cast<uint16_t*>(kc);
     a.vc = static_cast<uint16_t*>(vc);
+    a.seq_stride = (long long)per_seq;
     a.max_seq = (int)max_seq;
     a.do_rope = 1;
     a.do_append = 1;
     const bool vec = head_dim % 16 == 0 && aligned(qkv, 16) && aligned(cos_t, 16) &&
                      aligned(sin_t, 16) && aligned(kc, 16) && aligned(vc, 16);
-    return launch_rope(stream, a, (int)t, dtype, vec);
+    return launch_rope(stream, a, (int)(n_seq * t), dtype, vec);
+}
+
+int kvb_rope_kv_append(kvb_stream_t stream, void* qkv, size_t qkv_len, const float* cos_t,
+                       const float* sin_t, size_t table_len, void* kc, void* vc, size_t cache_len,
+                       size_t t, size_t pos0, size_t n_q, size_t n_kv, size_t head_dim,
+                       size_t max_seq, int dtype) {
+    return rope_kv_append_seqs(stream, qkv, qkv_len, cos_t, sin_t, table_len, kc, vc, cache_len, 1,
+                               t, pos0, n_q, n_kv, head_dim, max_seq, dtype);
+}
+
+int kvb_rope_kv_append_prefill(kvb_stream_t stream, void* qkv, size_t qkv_len,
+                               const float* cos_t, const float* sin_t, size_t table_len, void* kc,
+                               void* vc, size_t cache_len, size_t n_seq, size_t t, size_t pos0,
+                               size_t n_q, size_t n_kv, size_t head_dim, size_t max_seq,
+                               int dtype) {
+    return rope_kv_append_seqs(stream, qkv, qkv_len, cos_t, sin_t, table_len, kc, vc, cache_len,
+                               n_seq, t, pos0, n_q, n_kv, head_dim, max_seq, dtype);
 }
 
 int kvb_rope_kv_append_batched(kvb_stream_t stream, void* qkv, size_t n_seq, const int32_t* pos,

@@ -176,6 +176,18 @@ class Gpu:
                                            cos.numel(), _ptr(kc), _ptr(vc), kc.numel(), t, pos0,
                                            n_q, n_kv, head_dim, max_seq, dtype_tag(qkv)))
 
+    def rope_kv_append_prefill(self, qkv, cos, sin, kc, vc, n_seq, t, pos0, n_q, n_kv, head_dim,
+                               max_seq):
+        """kvb_rope_kv_append_prefill: rope_kv_append over n_seq sequences of t rows
+        each in one launch; caches [n_seq, n_kv, max_seq, head_dim]."""
+        if cos.numel() != sin.numel():
+            raise ShapeError("rope: bad cos/sin table sizes")
+        if kc.numel() != vc.numel():
+            raise ShapeError("kv_append: bad cache sizes")
+        check(self._lib.kvb_rope_kv_append_prefill(
+            self._s, _ptr(qkv), qkv.numel(), _ptr(cos), _ptr(sin), cos.numel(), _ptr(kc), _ptr(vc),
+            kc.numel(), n_seq, t, pos0, n_q, n_kv, head_dim, max_seq, dtype_tag(qkv)))
+
     def rope_kv_append_batched(self, qkv, pos, cos, sin, kc, vc, seq_stride, n_q, n_kv, head_dim,
                                max_seq):
         if pos.dtype != torch.int32:

@@ -52,6 +52,13 @@ def test_shape_errors_are_reported_not_launched():
     st, msg = _status(lib.kvb_kv_append, None, fake, 3 * 512, fake, 2 * 16 * 64, fake, 2 * 16 * 64,
                       3, 14, 4, 2, 64, 16, L.KVB_BF16)
     assert st == L.KVB_ERR_SHAPE and "max_seq" in msg
+    # prefill rope: 2 sequences x 3 rows need a cache of 2 * 2 * 16 * 64 elements
+    st, msg = _status(lib.kvb_rope_kv_append_prefill, None, fake, 2 * 3 * 768, fake, fake, 16 * 32,
+                      fake, fake, 2 * 16 * 64, 2, 3, 0, 8, 2, 64, 16, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "cache sizes" in msg
+    st, msg = _status(lib.kvb_rope_kv_append_prefill, None, fake, 2 * 3 * 768, fake, fake, 16 * 32,
+                      fake, fake, 2 * 2 * 16 * 64, 2, 3, 14, 8, 2, 64, 16, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "exceed" in msg
     st, msg = _status(lib.kvb_bf16_to_f16, None, fake, 10, fake, 10, fake, 2)
     assert st == L.KVB_ERR_SHAPE and "exactly one u32" in msg
     st, msg = _status(lib.kvb_embedding_gather, None, fake, 5, fake, 301, fake, 5 * 300, 300,

@@ -279,6 +279,39 @@ def test_rope_kv_append_batched_per_sequence_positions(g):
         np.testing.assert_array_equal(got_v[b], wv)
 
 
+@pytest.mark.parametrize("n_seq,t,pos0,max_seq", [(3, 5, 2, 16), (4, 300, 0, 320), (2, 1, 7, 8)])
+def test_rope_kv_append_prefill_equals_per_sequence(g, n_seq, t, pos0, max_seq):
+    """One launch over n_seq sequences == kvb_rope_kv_append on each in turn == oracle."""
+    rng = np.random.default_rng(21)
+    n_q, n_kv, hd = 32, 8, 64
+    stride = (n_q + 2 * n_kv) * hd
+    qkv = normal16(rng, n_seq * t * stride)
+    cos, sin = O.cos_sin_table(hd, max_seq, **O.LLAMA3_ROPE)
+    c, s = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    per = n_kv * max_seq * hd
+    a = dev(qkv)
+    kc_a = torch.zeros(n_seq * per, dtype=torch.bfloat16, device="cuda")
+    vc_a = torch.zeros_like(kc_a)
+    g.rope_kv_append_prefill(a, c, s, kc_a, vc_a, n_seq, t, pos0, n_q, n_kv, hd, max_seq)
+    assert g.device_error() == 0
+    b = dev(qkv)
+    kc_b, vc_b = torch.zeros_like(kc_a), torch.zeros_like(kc_a)
+    for i in range(n_seq):
+        g.rope_kv_append(b[i * t * stride:(i + 1) * t * stride], c, s, kc_b[i * per:(i + 1) * per],
+                         vc_b[i * per:(i + 1) * per], t, pos0, n_q, n_kv, hd, max_seq)
+    np.testing.assert_array_equal(host_bits(a), host_bits(b))
+    np.testing.assert_array_equal(host_bits(kc_a), host_bits(kc_b))
+    np.testing.assert_array_equal(host_bits(vc_a), host_bits(vc_b))
+    z = np.zeros(per, np.uint16)
+    for i in range(n_seq):
+        rows = qkv[i * t * stride:(i + 1) * t * stride]
+        rot = O.from_f32(O.rope(rows, cos, sin, t, pos0, n_q, n_kv, hd))
+        np.testing.assert_array_equal(host_bits(a)[i * t * stride:(i + 1) * t * stride], rot)
+        wk, wv = O.kv_append(rot, z, z, t, pos0, n_q, n_kv, hd, max_seq)
+        np.testing.assert_array_equal(host_bits(kc_a)[i * per:(i + 1) * per], wk)
+        np.testing.assert_array_equal(host_bits(vc_a)[i * per:(i + 1) * per], wv)
+
+
 def test_rope_batched_rejects_position_outside_cache(g):
     """A position beyond the cache is skipped and flagged, never written."""
     n_q, n_kv, hd, max_seq = 4, 2, 64, 8
