@@ -6,18 +6,27 @@
 //   warp 8   TMA producer: Q_A, Q_B once, then K/V tiles (128 keys x 64 dims,
 //            16 KB each) into a 4-stage ring (cp.async.bulk.tensor, 128-byte
 //            swizzle, no multicast)
-//   warp 9   MMA issuer (one lane):
+//   warp 9   MMA issuer (whole warp, one elected lane issues):
 //              S_q  = Q_q K_j^T       tcgen05.mma kind::f16, M=128 N=128 K=64,
 //                                     f32 accumulator in TMEM
-//              O_q += P_q,j V_j       M=128 N=64 K=128, P read from TMEM (TS form),
-//                                     O accumulated in TMEM across all key tiles
+//              O_q += P_q,j V_j       M=128 N=64 K=128, f16 P read from TMEM (TS
+//                                     form), f16 V; O accumulated in TMEM across
+//                                     all key tiles
+//   warps 10-11  (bf16 inputs) convert each V tile in shared memory to f16,
+//            in place, scaled by 2^-E (below)
 //   warps 0-3 / 4-7  softmax for tile A / B, one thread per query row (= TMEM
 //            lane): the whole 128-key S row in registers, causal mask on the
 //            diagonal tile, row max and sum in the log2 domain without any
-//            exchange between threads.  P goes back to TMEM over the S columns
-//            it came from as a 16-bit head plus a 16-bit remainder (two MMAs,
-//            so P keeps ~16 significant bits: 2e-3 absolute accuracy needs more
-//            than the 8 of bf16).
+//            exchange between threads; P goes back to TMEM over the S columns
+//            it came from as f16.
+// Why f16 for P V: P in [0, 256] as bf16 (8 significant bits) puts the output
+// ~3e-3 off for unit-scale inputs; f16 (11 bits) keeps it within ~5e-4, inside
+// the 2e-3 bar.  The tensor core takes one type for both operands, so bf16 V
+// becomes f16 as V * 2^-E.  E starts at 0 and is raised (never lowered) when a
+// tile holds an |entry| >= 2^(15+E), so no scaled entry overflows f16; O is
+// kept in units of 2^E, rescaled with the running max when E moves, and the
+// final O is multiplied back by 2^E.  Entries below 2^-14 * 2^E lose relative
+// precision in f16 (absolute error <= 2^-25 * 2^E each).
 // Lazy rescaling: the running max m is raised only when a tile's max exceeds it
 // by more than 2^8; P = 2^(s - m) then stays below 256, and O (in TMEM) and the
 // row sum are rescaled only on those rare raises.  When the softmax thread holds
@@ -45,7 +54,9 @@ constexpr int kPfKVBytes = kPfKeys * 64 * 2;      // 16 KB (K or V)
 constexpr int kPfSmemBytes = kPfTiles * kPfQBytes + kPfStages * 2 * kPfKVBytes + 1024;
 constexpr int kPfSoftmaxWarps = 8;                // 4 per Q tile, one thread per row
 constexpr int kTmaWarp = kPfSoftmaxWarps, kMmaWarp = kPfSoftmaxWarps + 1;
-constexpr int kPfThreads = (kPfSoftmaxWarps + 2) * 32;
+constexpr int kConvWarp = kPfSoftmaxWarps + 2;    // two V-conversion warps
+constexpr int kPfThreads = (kPfSoftmaxWarps + 4) * 32;
+constexpr int kMaxVShift = 112;                   // E cap (2^-E stays a normal f32)
 // S_A, S_B (128 columns each, P over them), O_A, O_B (64 each): 384 of 512.
 constexpr uint32_t kPfTmemCols = 512;
 constexpr uint32_t kPfTmemO = 2 * kPfKeys;
@@ -64,15 +75,27 @@ struct PrefillBars {
     uint64_t s_full[kPfTiles];   // S_q(j) in TMEM (phase j)
     uint64_t p_full[kPfTiles];   // P_q(j) in TMEM, O_q row rescaled (128 arrivals, phase j)
     uint64_t o_done[kPfTiles];   // last P_q V completed: O_q final
+    uint64_t v_ready[kPfStages]; // V tile of the stage converted to f16 (64 arrivals)
     uint64_t mma_done;           // every MMA of the CTA has completed (before TMEM is freed)
 };
 
 __device__ __forceinline__ bool warp_all(bool p) { return __all_sync(0xffffffffu, p); }
 
+// f32 pair -> packed f16x2 (round to nearest even), a in the low half.
+__device__ __forceinline__ uint32_t pack_f16x2(float a, float b) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+    return r;
+}
+// Nonzero if either bf16 half of w has |x| >= the bf16 magnitude `thr` (thr <=
+// 0x7f80): 15-bit magnitudes plus (0x8000 - thr) carry into bit 15 exactly then.
+__device__ __forceinline__ uint32_t bf16x2_at_least(uint32_t w, uint32_t add2) {
+    return ((w & 0x7fff7fffu) + add2) & 0x80008000u;
+}
+
 template <typename T>
-// 10 warps put 3 on two SM sub-partitions (16K registers each): at most 168
-// registers a thread, which a 384-thread bound gives the compiler.
-__global__ void __launch_bounds__(384, 1)
+// 12 warps, three per SM sub-partition (16K registers each): at most 168 registers.
+__global__ void __launch_bounds__(kPfThreads, 1)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap qmap,
                         const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap, PrefillArgs a) {
@@ -80,6 +103,9 @@ __global__ void __launch_bounds__(384, 1)
     __shared__ PrefillBars bars;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int s_err;
+    __shared__ int v_shift[kPfStages];      // E in force for the stage's converted V tile
+    __shared__ uint32_t conv_xchg[2][2];    // per conversion warp: overflow flag, max magnitude
+    constexpr bool kConvertV = Elem<T>::kDtype == KVB_BF16;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
     uint8_t* sq = smem;                                  // [tile] Q
@@ -107,6 +133,8 @@ __global__ void __launch_bounds__(384, 1)
         for (int s = 0; s < kPfStages; ++s) {
             mbar_init(&bars.kv_full[s], 1);
             mbar_init(&bars.kv_empty[s], 1);
+            mbar_init(&bars.v_ready[s], 64);
+            v_shift[s] = 0;
         }
         for (int q = 0; q < kPfTiles; ++q) {
             mbar_init(&bars.s_full[q], 1);
@@ -157,69 +185,140 @@ __global__ void __launch_bounds__(384, 1)
         }
     } else if (warp == kMmaWarp) {
         // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc_s = idesc_f16(kPfRows, kPfKeys, fmt, 0, 0);
-            const uint32_t idesc_o = idesc_f16(kPfRows, 64, fmt, 0, 1);
-            // Descriptors are built once; per MMA only the 16-byte start-address field
-            // (bits 0-13) moves, by adding a constant.
-            const uint64_t dq0 = sdesc_sw128(smem_u32(sq), 16, 1024);
-            const uint64_t dk0 = sdesc_sw128(smem_u32(skv), 16, 1024);
-            const uint64_t dv0 = sdesc_sw128(smem_u32(skv) + kPfKVBytes, 64 * 128, 1024);
-            constexpr uint64_t kQTile = kPfQBytes >> 4, kStage = (2 * kPfKVBytes) >> 4;
-            // S_q = Q_q K_j^T: four K=16 steps of 32 bytes along the 128-byte rows.
-            auto issue_s = [&](int q, int j) {
-                const uint32_t d = tmem + (uint32_t)(q * kPfKeys);
-                const uint64_t da = dq0 + kQTile * q, db = dk0 + kStage * (j % kPfStages);
-                umma_f16(d, da, db, idesc_s, 0);
-                umma_f16(d, da + 2, db + 2, idesc_s, 1);
-                umma_f16(d, da + 4, db + 4, idesc_s, 1);
-                umma_f16(d, da + 6, db + 6, idesc_s, 1);
-                umma_commit(&bars.s_full[q]);
-            };
-            // O_q += P_q,hi V_j + P_q,lo V_j: P_hi in the S columns 0-63, P_lo in 64-127
-            // (two keys per column); V_j read MN-major, 16 keys (2048 bytes) per step.
-            auto issue_pv = [&](int q, int j) {
-                const uint32_t d = tmem + kPfTmemO + (uint32_t)(q * 64);
-                const uint32_t p = tmem + (uint32_t)(q * kPfKeys);
-                const uint64_t dv = dv0 + kStage * (j % kPfStages);
+        // The whole warp runs this loop converged; umma_* / umma_commit issue from
+        // one elected lane.  Wait results are made warp-uniform.
+        const uint32_t idesc_s = idesc_f16(kPfRows, kPfKeys, fmt, 0, 0);
+        const uint32_t idesc_o = idesc_f16(kPfRows, 64, 0, 0, 1);  // f16 P, f16 V
+        // Descriptors are built once; per MMA only the 16-byte start-address field
+        // (bits 0-13) moves, by adding a constant.
+        const uint64_t dq0 = sdesc_sw128(smem_u32(sq), 16, 1024);
+        const uint64_t dk0 = sdesc_sw128(smem_u32(skv), 16, 1024);
+        const uint64_t dv0 = sdesc_sw128(smem_u32(skv) + kPfKVBytes, 64 * 128, 1024);
+        constexpr uint64_t kQTile = kPfQBytes >> 4, kStage = (2 * kPfKVBytes) >> 4;
+        // S_q = Q_q K_j^T: four K=16 steps of 32 bytes along the 128-byte rows.
+        auto issue_s = [&](int q, int j) {
+            const uint32_t d = tmem + (uint32_t)(q * kPfKeys);
+            const uint64_t da = dq0 + kQTile * q, db = dk0 + kStage * (j % kPfStages);
+            umma_f16(d, da, db, idesc_s, 0);
+            umma_f16(d, da + 2, db + 2, idesc_s, 1);
+            umma_f16(d, da + 4, db + 4, idesc_s, 1);
+            umma_f16(d, da + 6, db + 6, idesc_s, 1);
+            umma_commit(&bars.s_full[q]);
+        };
+        // O_q += P_q V_j: f16 P in the S columns 0-63 (keys 2c, 2c+1 in column c);
+        // V_j read MN-major, 16 keys (2048 bytes) per step.
+        auto issue_pv = [&](int q, int j) {
+            const uint32_t d = tmem + kPfTmemO + (uint32_t)(q * 64);
+            const uint32_t p = tmem + (uint32_t)(q * kPfKeys);
+            const uint64_t dv = dv0 + kStage * (j % kPfStages);
+            umma_f16_ts(d, p, dv, idesc_o, j > 0 ? 1u : 0u);
 #pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    umma_f16_ts(d, p + 8 * k, dv + 128 * k, idesc_o, (j > 0 || k > 0) ? 1u : 0u);
-#pragma unroll
-                for (int k = 0; k < 8; ++k) umma_f16_ts(d, p + 64 + 8 * k, dv + 128 * k, idesc_o, 1);
-            };
-            bool ok = mbar_wait(&bars.q_full, 0) && mbar_wait(&bars.kv_full[0], 0);
-            for (int q = 0; q < kPfTiles && ok; ++q)
-                if (n_tiles(q) > 0) issue_s(q, 0);
-            int kv_ready = 0;  // highest key tile known to be in shared memory
-            for (int j = 0; j < n_kv_tiles && ok; ++j) {
-                for (int q = 0; q < kPfTiles && ok; ++q) {
-                    if (j >= n_tiles(q)) continue;
-                    if (s_err || !mbar_wait(&bars.p_full[q], j & 1)) {
-                        ok = false;
-                        break;
+            for (int k = 1; k < 8; ++k) umma_f16_ts(d, p + 8 * k, dv + 128 * k, idesc_o, 1);
+        };
+        bool ok = warp_all(mbar_wait(&bars.q_full, 0) && mbar_wait(&bars.kv_full[0], 0));
+        for (int q = 0; q < kPfTiles && ok; ++q)
+            if (n_tiles(q) > 0) issue_s(q, 0);
+        int kv_ready = 0;  // highest key tile known to be in shared memory
+        for (int j = 0; j < n_kv_tiles && ok; ++j) {
+            for (int q = 0; q < kPfTiles && ok; ++q) {
+                if (j >= n_tiles(q)) continue;
+                ok = warp_all(!s_err && mbar_wait(&bars.p_full[q], j & 1) &&
+                              (!kConvertV || mbar_wait(&bars.v_ready[j % kPfStages],
+                                                       (j / kPfStages) & 1)));
+                if (!ok) break;
+                tc_fence_after();
+                issue_pv(q, j);
+                if (j + 1 < n_tiles(q)) {
+                    if (kv_ready < j + 1) {
+                        ok = warp_all(mbar_wait(&bars.kv_full[(j + 1) % kPfStages],
+                                                ((j + 1) / kPfStages) & 1));
+                        if (!ok) break;
+                        kv_ready = j + 1;
                     }
-                    tc_fence_after();
-                    issue_pv(q, j);
-                    if (j + 1 < n_tiles(q)) {
-                        if (kv_ready < j + 1) {
-                            if (!mbar_wait(&bars.kv_full[(j + 1) % kPfStages], ((j + 1) / kPfStages) & 1)) {
-                                ok = false;
-                                break;
-                            }
-                            kv_ready = j + 1;
-                        }
-                        issue_s(q, j + 1);
-                    } else {
-                        umma_commit(&bars.o_done[q]);
+                    issue_s(q, j + 1);
+                } else {
+                    umma_commit(&bars.o_done[q]);
+                }
+            }
+            if (ok) umma_commit(&bars.kv_empty[j % kPfStages]);  // stage free once these finish
+        }
+        if (!ok && lane == 0) s_err = 1;
+        // No MMA may still be running when TMEM is released below.
+        umma_commit(&bars.mma_done);
+        mbar_wait(&bars.mma_done, 0);
+        __syncwarp();
+    } else if (warp >= kConvWarp) {
+        // ------------------------------------------------------------ V conversion
+        // Warp kConvWarp + c converts 16-byte chunks c*32 + lane + 64 i of the V
+        // tile (all 1024 chunks between the two warps) from bf16 to f16 * 2^-E.
+        if constexpr (kConvertV) {
+            const int cw = warp - kConvWarp;
+            const int ct = cw * 32 + lane;
+            int e = 0;  // E: V is stored as V * 2^-E
+            bool ok = true;
+            for (int j = 0; j < n_kv_tiles; ++j) {
+                const int st = j % kPfStages;
+                const bool here = warp_all(!s_err && mbar_wait(&bars.kv_full[st], (j / kPfStages) & 1));
+                uint4* vt = reinterpret_cast<uint4*>(skv + (2 * st + 1) * kPfKVBytes);
+                uint4 w[16];
+                // |v| >= 2^(15 + E): bf16 magnitude (127 + 15 + E) << 7
+                const uint32_t thr = (uint32_t)min(127 + 15 + e, 255) << 7;
+                const uint32_t add = 0x8000u - min(thr, 0x7f80u);
+                const uint32_t add2 = add | (add << 16);
+                uint32_t big = 0;
+                if (here) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        w[i] = vt[ct + 64 * i];
+                        big |= bf16x2_at_least(w[i].x, add2) | bf16x2_at_least(w[i].y, add2) |
+                               bf16x2_at_least(w[i].z, add2) | bf16x2_at_least(w[i].w, add2);
                     }
                 }
-                if (ok) umma_commit(&bars.kv_empty[j % kPfStages]);  // stage free once these finish
+                // Both warps must agree on failure and on E for the tile: exchange the
+                // flags (and, on the rare overflow path, the largest magnitude) through
+                // shared memory; both warps pass every named barrier of an iteration.
+                const bool any_big = __any_sync(0xffffffffu, big != 0);
+                if (lane == 0) conv_xchg[cw][0] = (any_big ? 1u : 0u) | (here ? 0u : 2u);
+                named_bar_sync(1, 64);
+                const uint32_t flags = conv_xchg[0][0] | conv_xchg[1][0];
+                if (flags & 2u) {
+                    ok = false;
+                    break;
+                }
+                if (flags & 1u) {
+                    uint32_t mag = 0;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            mag = max(mag, max(u[k] & 0x7fffu, (u[k] >> 16) & 0x7fffu));
+                    }
+                    mag = __reduce_max_sync(0xffffffffu, mag);
+                    if (lane == 0) conv_xchg[cw][1] = mag;
+                    named_bar_sync(1, 64);
+                    mag = max(conv_xchg[0][1], conv_xchg[1][1]);
+                    // largest |v| < 2^(x - 126) with x = its biased exponent: E >= x - 141
+                    e = min(max(e, (int)(mag >> 7) - 141), kMaxVShift);
+                }
+                const float sc = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-E
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float lo = __uint_as_float(u[k] << 16) * sc;
+                        const float hi = __uint_as_float(u[k] & 0xffff0000u) * sc;
+                        u[k] = pack_f16x2(lo, hi);
+                    }
+                    vt[ct + 64 * i] = make_uint4(u[0], u[1], u[2], u[3]);
+                }
+                if (ct == 0) v_shift[st] = e;
+                fence_async_smem();  // generic-proxy writes -> visible to the tensor core
+                mbar_arrive(&bars.v_ready[st]);
+                named_bar_sync(1, 64);  // conv_xchg is reused by the next tile
             }
-            if (!ok) s_err = 1;
-            // No MMA may still be running when TMEM is released below.
-            umma_commit(&bars.mma_done);
-            mbar_wait(&bars.mma_done, 0);
+            if (!ok && lane == 0) s_err = 1;
         }
     } else {
         // ------------------------------------------------------------ softmax warps
@@ -235,6 +334,7 @@ __global__ void __launch_bounds__(384, 1)
         const int diag_key = a.pos0 + q0 + q * kPfRows;  // keys above need the causal mask
         const int nt = n_tiles(q);
         float m = -INFINITY, l = 0.f;  // running max (log2 units) and row sum
+        int e_cur = 0;                 // E of the V tiles accumulated into O so far
         bool ok = true;
         for (int j = 0; j < nt; ++j) {
             ok = warp_all(!s_err && mbar_wait(&bars.s_full[q], j & 1));
@@ -272,19 +372,26 @@ __global__ void __launch_bounds__(384, 1)
                 sum4[c & 3] += s[c];
             }
             l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-            // P_j -> TMEM over the S columns: keys 2c, 2c+1 in column c (heads in 0-63,
-            // remainders in 64-127).  This thread's S loads completed above.
+            // P_j -> TMEM as f16 over the S columns 0-63: keys 2c, 2c+1 in column c.
+            // This thread's S loads completed above.
 #pragma unroll
             for (int ch = 0; ch < 4; ++ch) {
-                uint32_t hi[16], lo[16];
+                uint32_t pk[16];
 #pragma unroll
-                for (int k = 0; k < 16; ++k)
-                    split_pack<T>(s[32 * ch + 2 * k], s[32 * ch + 2 * k + 1], hi[k], lo[k]);
-                tmem_st16(t_s + 16 * ch, hi);
-                tmem_st16(t_s + 64 + 16 * ch, lo);
+                for (int k = 0; k < 16; ++k) pk[k] = pack_f16x2(s[32 * ch + 2 * k], s[32 * ch + 2 * k + 1]);
+                tmem_st16(t_s + 16 * ch, pk);
             }
-            if (__any_sync(0xffffffffu, rescale)) {  // O row *= alpha (O is idle, see above)
-                const float f = rescale ? alpha : 1.f;
+            // V_j's scale: O (in units of 2^E) follows E before P_j V_j is added.
+            int de = 0;
+            if (kConvertV) {
+                ok = warp_all(!s_err && mbar_wait(&bars.v_ready[j % kPfStages], (j / kPfStages) & 1));
+                if (!ok) break;
+                const int e_j = v_shift[j % kPfStages];
+                if (j > 0) de = e_j - e_cur;
+                e_cur = e_j;
+            }
+            if (__any_sync(0xffffffffu, rescale) || de != 0) {  // O row *= f (O is idle, see above)
+                const float f = (rescale ? alpha : 1.f) * __uint_as_float((uint32_t)(127 - de) << 23);
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     float o[32];
@@ -303,7 +410,7 @@ __global__ void __launch_bounds__(384, 1)
             ok = warp_all(!s_err && mbar_wait(&bars.o_done[q], 0));
             if (ok) {
                 tc_fence_after();
-                const float inv = 1.f / l;
+                const float inv = __uint_as_float((uint32_t)(127 + e_cur) << 23) / l;  // 2^E / l
                 const bool valid = row < (q ? rows_valid1 : rows_valid0);
                 T* orow = reinterpret_cast<T*>(a.out) +
                           ((size_t)seq * a.t + q0 + q * kPfRows + row) * a.out_row_stride +

@@ -202,6 +202,56 @@ def test_prefill_config3_shape(g):
     O.set_threads(1)
 
 
+def test_prefill_v_scale_is_exact(g):
+    """bf16 V reaches the tensor core as f16 V * 2^-E, E raised when |V| >= 2^15.
+    Scaling V by 2^17 (exact in bf16) must scale the output by 2^17 bit for bit."""
+    n_q, n_kv, hd, t = 8, 2, 64, 300
+    rng = np.random.default_rng(55)
+    stride = (n_q + 2 * n_kv) * hd
+    qkv = normal16(rng, t * stride)
+    kc, vc = normal16(rng, n_kv * t * hd), normal16(rng, n_kv * t * hd)
+    vbig = O.from_f32(O.to_f32(vc) * np.float32(2.0 ** 17))
+    assert np.abs(O.to_f32(vbig)).max() > 2.0 ** 15
+    a = torch.empty(t * n_q * hd, dtype=torch.bfloat16, device="cuda")
+    b = torch.empty_like(a)
+    g.attention(dev(qkv), dev(kc), dev(vc), a, t, 0, n_q, n_kv, hd, t)
+    g.attention(dev(qkv), dev(kc), dev(vbig), b, t, 0, n_q, n_kv, hd, t)
+    assert g.device_error() == 0
+    np.testing.assert_array_equal(host_f32(b), host_f32(a) * np.float32(2.0 ** 17))
+
+
+def test_prefill_v_magnitudes_vary_by_key_tile(g):
+    """V tiles up to 2^19 apart in magnitude: E rises twice mid-sequence and O is
+    rescaled each time.
+    Per-row bar: 2e-3 x the row's softmax-weighted mean |v| (the unit-scale bar,
+    scaled) plus one rounding of the output."""
+    n_q, n_kv, hd, t = 4, 1, 64, 600
+    rng = np.random.default_rng(56)
+    stride = (n_q + 2 * n_kv) * hd
+    qkv = normal16(rng, t * stride)
+    kc = normal16(rng, t * hd)
+    v = rng.normal(0, 1, (t, hd))
+    for tile, e in enumerate([0, 17, 3, 19, 0]):
+        v[tile * 128:(tile + 1) * 128] *= 2.0 ** e
+    vc = O.from_f32(v.astype(np.float32).ravel())
+    out = torch.empty(t * n_q * hd, dtype=torch.bfloat16, device="cuda")
+    g.attention(dev(qkv), dev(kc), dev(vc), out, t, 0, n_q, n_kv, hd, t)
+    assert g.device_error() == 0
+    got = host_f32(out).reshape(t, n_q, hd).astype(np.float64)
+    q = O.to_f32(qkv).reshape(t, n_q + 2, hd)[:, :n_q].astype(np.float64)
+    k = O.to_f32(kc).reshape(t, hd).astype(np.float64)
+    vv = O.to_f32(vc).reshape(t, hd).astype(np.float64)
+    s = np.einsum("thd,kd->htk", q, k) / 8.0
+    s = np.where(np.triu(np.ones((t, t), bool), 1)[None], -np.inf, s)
+    p = np.exp(s - s.max(-1, keepdims=True))
+    l = p.sum(-1, keepdims=True)
+    want = np.einsum("htk,kd->htd", p, vv) / l
+    scale = np.einsum("htk,kd->htd", p, np.abs(vv)) / l
+    err = np.abs(got.transpose(1, 0, 2) - want)
+    bound = 2e-3 * scale + 2.0 ** -8 * np.abs(want)
+    assert (err <= bound).all(), float((err / bound).max())
+
+
 def test_prefill_rows_are_prefix_consistent(g):
     """Size-independent property at full length: causal row i only depends on
     tokens <= i, so a prefill of the first 1000 tokens reproduces the first
