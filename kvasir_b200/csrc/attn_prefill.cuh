@@ -93,6 +93,59 @@ __device__ __forceinline__ uint32_t bf16x2_at_least(uint32_t w, uint32_t add2) {
     return ((w & 0x7fff7fffu) + add2) & 0x80008000u;
 }
 
+// ---- packed f32x2 arithmetic (one instruction for two lanes of f32 work)
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+// 2^x for a pair on the FMA pipe, to take load off the MUFU unit that ex2.approx
+// uses.  x = n + f with n = round(x) (added to the exponent field) and f in
+// [-1/2, 1/2], where a degree-3 polynomial fitted here to 2^f (weighted least
+// squares on Chebyshev nodes, max relative error 7.5e-5, below the 2^-11
+// rounding of the f16 P it feeds) supplies the mantissa.  x is clamped to
+// [-126, 2^22]: below 2^-126 the result is not a number of any consequence to
+// a softmax weight.  round(x) comes from adding 1.5 * 2^23, which leaves it in
+// the low mantissa bits of the sum.
+__device__ __forceinline__ void exp2_poly_pair(float& x0, float& x1) {
+    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+    const uint64_t x = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+    const uint64_t magic = f2_pack(kMagic, kMagic);
+    const uint64_t t = f2_add(x, magic);
+    const uint64_t f = f2_sub(x, f2_sub(t, magic));
+    uint64_t p = f2_fma(f2_pack(0.055171654f, 0.055171654f), f, f2_pack(0.24261113f, 0.24261113f));
+    p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
+    p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
+    float p0, p1, t0, t1;
+    f2_unpack(p, p0, p1);
+    f2_unpack(t, t0, t1);
+    x0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+    x1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
 template <typename T>
 // 12 warps, three per SM sub-partition (16K registers each): at most 168 registers.
 __global__ void __launch_bounds__(kPfThreads, 1)
@@ -351,35 +404,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 for (int c = 0; c < kPfKeys; ++c)
                     if (j * kPfKeys + c > my_pos) s[c] = -INFINITY;
             }
-            float mx4[4];
+            float mx8[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) mx4[i] = s[i];
+            for (int i = 0; i < 8; ++i) mx8[i] = s[i];
 #pragma unroll
-            for (int c = 4; c < kPfKeys; ++c) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+            for (int c = 8; c < kPfKeys; c += 16)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mx8[i] = max3f(mx8[i], s[c + i], s[c + 8 + i]);
             // Raw scores: the max is taken before scaling (the scale is positive).
-            const float mt = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+            const float mt = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]),
+                                   fmaxf(mx8[6], mx8[7])) *
+                             a.scale_log2;
             float alpha = 1.f;
             bool rescale = false;
             if (mt > m + kPfRescaleLog2) {  // always at j = 0 (m = -inf; row 0 of a tile sees key 0)
                 alpha = ex2_approx(m - mt);  // 0 at j = 0
                 rescale = j > 0;
                 m = mt;
-            }
-            float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int c = 0; c < kPfKeys; ++c) {
-                s[c] = ex2_approx(fmaf(s[c], a.scale_log2, -m));  // 2^(s*scale - m) <= 2^8
-                sum4[c & 3] += s[c];
-            }
-            l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-            // P_j -> TMEM as f16 over the S columns 0-63: keys 2c, 2c+1 in column c.
-            // This thread's S loads completed above.
-#pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
-                uint32_t pk[16];
-#pragma unroll
-                for (int k = 0; k < 16; ++k) pk[k] = pack_f16x2(s[32 * ch + 2 * k], s[32 * ch + 2 * k + 1]);
-                tmem_st16(t_s + 16 * ch, pk);
             }
             // V_j's scale: O (in units of 2^E) follows E before P_j V_j is added.
             int de = 0;
@@ -390,7 +431,35 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 if (j > 0) de = e_j - e_cur;
                 e_cur = e_j;
             }
-            if (__any_sync(0xffffffffu, rescale) || de != 0) {  // O row *= f (O is idle, see above)
+            // P_j = 2^(s*scale - m) <= 2^8 -> TMEM as f16 over the S columns 0-63 (keys
+            // 2c, 2c+1 in column c), 32 keys at a time so that each store is in flight
+            // while the next keys are computed.  One key pair in four takes 2^x from
+            // the FMA pipe, the others from MUFU.  This thread's S loads completed above.
+            uint64_t sum2[4] = {0, 0, 0, 0};  // four f32 pairs of partial row sums (+0.0f bits)
+#pragma unroll
+            for (int ch = 0; ch < 4; ++ch) {
+                uint32_t pk[16];
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    float p0 = fmaf(s[32 * ch + 2 * k], a.scale_log2, -m);
+                    float p1 = fmaf(s[32 * ch + 2 * k + 1], a.scale_log2, -m);
+                    if ((k & 3) == 0) {
+                        exp2_poly_pair(p0, p1);
+                    } else {
+                        p0 = ex2_approx(p0);
+                        p1 = ex2_approx(p1);
+                    }
+                    sum2[k & 3] = f2_add(sum2[k & 3], f2_pack(p0, p1));
+                    pk[k] = pack_f16x2(p0, p1);
+                }
+                tmem_st16(t_s + 16 * ch, pk);
+            }
+            float r0, r1, r2, r3, r4, r5, r6, r7;
+            f2_unpack(f2_add(sum2[0], sum2[1]), r0, r1);
+            f2_unpack(f2_add(sum2[2], sum2[3]), r2, r3);
+            (void)r4; (void)r5; (void)r6; (void)r7;
+            l = l * alpha + ((r0 + r1) + (r2 + r3));
+            if (__any_sync(0xffffffffu, rescale) || de != 0) {  // O row *= f (O is idle, see above; S is dead)
                 const float f = (rescale ? alpha : 1.f) * __uint_as_float((uint32_t)(127 - de) << 23);
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
