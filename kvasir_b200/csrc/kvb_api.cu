@@ -271,7 +271,7 @@ static int launch_prefill(kvb_stream_t stream, const void* qkv, const void* kc, 
     a.n_q = (int)n_q;
     a.n_kv = (int)n_kv;
     a.group = (int)(n_q / n_kv);
-    const size_t rows_per_block = (size_t)kPfTiles * kPfRows;
+    const size_t rows_per_block = (size_t)kPfRows;
     a.n_qblocks = (int)((t + rows_per_block - 1) / rows_per_block);
     a.scale_log2 = (1.0f / sqrtf(64.0f)) * 1.4426950408889634f;
     a.out = static_cast<uint16_t*>(out);
