@@ -2,31 +2,33 @@
 // tensor cores (tcgen05 / TMEM), head_dim 64, warp-specialised.
 //
 // One CTA computes one 128-row query tile of one head of one sequence; two
-// CTAs share an SM (256 TMEM columns and ~81 KB of shared memory each), so
+// CTAs share an SM (256 TMEM columns and ~89 KB of shared memory each), so
 // that while one CTA's softmax waits for its tensor-core work the other one's
 // runs -- two independent pipelines, nothing shared between them:
-//   warp 4   TMA producer: Q once, then 128-key K/V tiles (16 KB each) into a
-//            2-stage ring (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
+//   warp 4   TMA producer: Q once, then 96-key K/V tiles (12 KB each) into a
+//            3-stage ring (cp.async.bulk.tensor, 128-byte swizzle, no multicast)
 //   warp 5   MMA issuer (whole warp, one elected lane issues):
-//              S  = Q K_j^T       tcgen05.mma kind::f16, M=128 N=128 K=64, f32 in TMEM
+//              S  = Q K_j^T       tcgen05.mma kind::f16, M=128 N=96 K=64, f32 in
+//                                 TMEM, two S buffers (tile j in buffer j & 1)
 //              O += P_j V_j       M=128 N=64, P read from TMEM (TS form); O
 //                                 accumulated in TMEM across all key tiles
-//   warps 0-3  softmax, one thread per query row (= TMEM lane): the 128-key S
+//   warps 0-3  softmax, one thread per query row (= TMEM lane): the 96-key S
 //            row in registers, causal mask on the diagonal tiles, row max and
 //            sum in the log2 domain without any exchange between threads.
+// TMEM: S0 columns 0-95, S1 96-191, O 192-255.  96-key tiles are what lets two
+// S buffers and O fit the 256 columns of a CTA: S(j+1) is computed while the
+// softmax threads work on S(j).  Issue order P(j) V(j), S(j+2): S(j+2) reuses
+// the buffer of P(j), which P(j) V(j) has read -- MMAs issued by one thread
+// execute in issue order.
 // P goes back to TMEM over the S columns it came from.  bf16 inputs: P as a
-// bf16 head (columns 0-63) plus a bf16 remainder (64-127), two MMAs per key
-// step, so P keeps ~16 significant bits (bf16 P alone, 8 bits, puts the output
-// ~3e-3 off for unit-scale inputs, outside the 2e-3 bar).  f16 inputs: P as one
-// f16 (columns 0-63), within ~5e-4.
+// bf16 head (columns 0-47 of the buffer) plus a bf16 remainder (48-95), two
+// MMAs per key step, so P keeps ~16 significant bits (bf16 P alone, 8 bits,
+// puts the output ~3e-3 off for unit-scale inputs, outside the 2e-3 bar).
+// f16 inputs: P as one f16 (columns 0-47), within ~5e-4.
 // Lazy rescaling: the running max m is raised only when a tile's max exceeds it
 // by more than 2^8; P = 2^(s - m) then stays below 256, and O (in TMEM) and the
-// row sum are rescaled only on those rare raises.  When a softmax thread holds
-// S(j), every MMA issued before S(j) -- P(j-1) V(j-1) included -- has completed
-// (a commit tracks all earlier MMAs of the issuing thread), so the thread may
-// rescale its O row in place before it hands P(j) back.  S(j+1) overwrites the
-// TMEM columns that P(j) V(j) reads; MMAs issued by one thread execute in issue
-// order, so the read precedes the overwrite.
+// row sum are rescaled only on those rare raises, after the previous P V has
+// finished writing O.
 // Every mbarrier wait is bounded; a failed wait sets a CTA-wide flag that
 // every role checks before its next wait; TMEM is freed on every path.
 #pragma once
@@ -36,18 +38,19 @@
 namespace kvb {
 
 constexpr int kPfRows = 128;                      // query rows per CTA (MMA M)
-constexpr int kPfKeys = 128;                      // keys per K/V tile (S MMA N)
-constexpr int kPfStages = 2;                      // K/V ring depth
+constexpr int kPfKeys = 96;                       // keys per K/V tile (S MMA N)
+constexpr int kPfStages = 3;                      // K/V ring depth
 constexpr int kPfQBytes = kPfRows * 64 * 2;       // 16 KB
-constexpr int kPfKVBytes = kPfKeys * 64 * 2;      // 16 KB (K or V)
+constexpr int kPfKVBytes = kPfKeys * 64 * 2;      // 12 KB (K or V)
 constexpr int kPfSmemBytes = kPfQBytes + kPfStages * 2 * kPfKVBytes + 1024;
 constexpr int kPfSoftmaxWarps = 4;                // one thread per row
 constexpr int kTmaWarp = kPfSoftmaxWarps, kMmaWarp = kPfSoftmaxWarps + 1;
 constexpr int kPfThreads = (kPfSoftmaxWarps + 2) * 32;
 constexpr int kPfCtasPerSm = 2;
-// S (128 columns, P over them), then O (64): 192 of 256.
+// S[2] (96 columns each, P over them), then O (64): all 256.
 constexpr uint32_t kPfTmemCols = 256;
-constexpr uint32_t kPfTmemO = kPfKeys;
+constexpr uint32_t kPfTmemO = 2 * kPfKeys;
+constexpr int kPfPCols = kPfKeys / 2;             // 16-bit P: two keys per column
 constexpr float kPfRescaleLog2 = 8.0f;            // raise m only past 2^8
 
 struct PrefillArgs {
@@ -60,9 +63,15 @@ struct PrefillArgs {
 struct PrefillBars {
     uint64_t q_full;
     uint64_t kv_full[kPfStages], kv_empty[kPfStages];
-    uint64_t s_full;     // S(j) in TMEM (phase j)
-    uint64_t p_full;     // P(j) in TMEM, O row rescaled (128 arrivals, phase j)
-    uint64_t o_done;     // last P V completed: O final
+    // One S-ready and one P-ready barrier per S buffer (tile j uses buffer j & 1):
+    // a thread that runs a tile ahead arrives on the other buffer's barrier.
+    uint64_t s_full[2];
+    uint64_t p_full[2];  // 128 arrivals
+    // P(j) V(j) has completed (phase j).  A softmax thread holding S(j) knows
+    // P(j-2) V completed (S(j) was issued after it), so only P(j-1) V can be
+    // pending when it waits here: a parity wait is unambiguous there.
+    uint64_t pv_done;
+    uint64_t o_done;     // last P V completed: O final (one phase)
     uint64_t mma_done;   // every MMA of the CTA has completed (before TMEM is freed)
 };
 
@@ -162,8 +171,11 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
             mbar_init(&bars.kv_full[s], 1);
             mbar_init(&bars.kv_empty[s], 1);
         }
-        mbar_init(&bars.s_full, 1);
-        mbar_init(&bars.p_full, kPfRows);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&bars.s_full[b], 1);
+            mbar_init(&bars.p_full[b], kPfRows);
+        }
+        mbar_init(&bars.pv_done, 1);
         mbar_init(&bars.o_done, 1);
         mbar_init(&bars.mma_done, 1);
         s_err = 0;
@@ -219,39 +231,45 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
         constexpr uint64_t kStage = (2 * kPfKVBytes) >> 4;
         // S = Q K_j^T: four K=16 steps of 32 bytes along the 128-byte rows.
         auto issue_s = [&](int j) {
+            const uint32_t d = tmem + (uint32_t)((j & 1) * kPfKeys);
             const uint64_t db = dk0 + kStage * (j % kPfStages);
-            umma_f16(tmem, dq, db, idesc_s, 0);
-            umma_f16(tmem, dq + 2, db + 2, idesc_s, 1);
-            umma_f16(tmem, dq + 4, db + 4, idesc_s, 1);
-            umma_f16(tmem, dq + 6, db + 6, idesc_s, 1);
-            umma_commit(&bars.s_full);
+            umma_f16(d, dq, db, idesc_s, 0);
+            umma_f16(d, dq + 2, db + 2, idesc_s, 1);
+            umma_f16(d, dq + 4, db + 4, idesc_s, 1);
+            umma_f16(d, dq + 6, db + 6, idesc_s, 1);
+            umma_commit(&bars.s_full[j & 1]);
         };
         // O += P_j V_j: P (head, then remainder for bf16) in the S columns, two keys
         // per column; V_j read MN-major, 16 keys (2048 bytes) per step.
         auto issue_pv = [&](int j) {
             const uint32_t d = tmem + kPfTmemO;
+            const uint32_t p = tmem + (uint32_t)((j & 1) * kPfKeys);
             const uint64_t dv = dv0 + kStage * (j % kPfStages);
-            umma_f16_ts(d, tmem, dv, idesc_o, j > 0 ? 1u : 0u);
+            umma_f16_ts(d, p, dv, idesc_o, j > 0 ? 1u : 0u);
 #pragma unroll
-            for (int k = 1; k < 8; ++k) umma_f16_ts(d, tmem + 8 * k, dv + 128 * k, idesc_o, 1);
+            for (int k = 1; k < kPfKeys / 16; ++k) umma_f16_ts(d, p + 8 * k, dv + 128 * k, idesc_o, 1);
             if (kSplitP) {
 #pragma unroll
-                for (int k = 0; k < 8; ++k) umma_f16_ts(d, tmem + 64 + 8 * k, dv + 128 * k, idesc_o, 1);
+                for (int k = 0; k < kPfKeys / 16; ++k)
+                    umma_f16_ts(d, p + kPfPCols + 8 * k, dv + 128 * k, idesc_o, 1);
             }
+            umma_commit(&bars.pv_done);
         };
-        bool ok = nt > 0 && warp_all(mbar_wait(&bars.q_full, 0) && mbar_wait(&bars.kv_full[0], 0));
-        if (ok) issue_s(0);
+        bool ok = nt > 0 && warp_all(mbar_wait(&bars.q_full, 0));
+        for (int j = 0; j < 2 && j < nt && ok; ++j) {  // S for key tiles 0 and 1
+            ok = warp_all(mbar_wait(&bars.kv_full[j % kPfStages], (j / kPfStages) & 1));
+            if (ok) issue_s(j);
+        }
         for (int j = 0; j < nt && ok; ++j) {
-            ok = warp_all(!s_err && mbar_wait(&bars.p_full, j & 1));
+            ok = warp_all(!s_err && mbar_wait(&bars.p_full[j & 1], (j >> 1) & 1));
             if (!ok) break;
             tc_fence_after();
-            issue_pv(j);
-            if (j + 1 < nt) {
-                ok = warp_all(mbar_wait(&bars.kv_full[(j + 1) % kPfStages], ((j + 1) / kPfStages) & 1));
+            issue_pv(j);  // then S(j + 2) reuses buffer j & 1 (read by this P V first)
+            if (j + 1 == nt) umma_commit(&bars.o_done);
+            if (j + 2 < nt) {
+                ok = warp_all(mbar_wait(&bars.kv_full[(j + 2) % kPfStages], ((j + 2) / kPfStages) & 1));
                 if (!ok) break;
-                issue_s(j + 1);
-            } else {
-                umma_commit(&bars.o_done);
+                issue_s(j + 2);
             }
             umma_commit(&bars.kv_empty[j % kPfStages]);  // stage free once these finish
         }
@@ -266,21 +284,20 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
         // warp-uniform (tcgen05.ld / st are warp-collective).
         const int row = warp * 32 + lane;
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-        const uint32_t t_s = tmem + lane_off;             // S, then P
         const uint32_t t_o = tmem + kPfTmemO + lane_off;  // O
         const int my_pos = a.pos0 + q0 + row;
         const int diag_key = a.pos0 + q0;  // keys above need the causal mask
         float m = -INFINITY, l = 0.f;      // running max (log2 units) and row sum
         bool ok = true;
         for (int j = 0; j < nt; ++j) {
-            ok = warp_all(!s_err && mbar_wait(&bars.s_full, j & 1));
+            const int b = j & 1;
+            const uint32_t t_s = tmem + (uint32_t)(b * kPfKeys) + lane_off;  // S, then P
+            ok = warp_all(!s_err && mbar_wait(&bars.s_full[b], (j >> 1) & 1));
             if (!ok) break;
             tc_fence_after();
             float s[kPfKeys];
-            tmem_ld32(t_s, s);
-            tmem_ld32(t_s + 32, s + 32);
-            tmem_ld32(t_s + 64, s + 64);
-            tmem_ld32(t_s + 96, s + 96);
+#pragma unroll
+            for (int c = 0; c < kPfKeys; c += 32) tmem_ld32(t_s + c, s + c);
             tmem_wait_ld();
             if (j * kPfKeys + kPfKeys - 1 > diag_key) {
 #pragma unroll
@@ -291,9 +308,13 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
 #pragma unroll
             for (int i = 0; i < 8; ++i) mx8[i] = s[i];
 #pragma unroll
-            for (int c = 8; c < kPfKeys; c += 16)
+            for (int c = 8; c + 16 <= kPfKeys; c += 16)
 #pragma unroll
                 for (int i = 0; i < 8; ++i) mx8[i] = max3f(mx8[i], s[c + i], s[c + 8 + i]);
+            if ((kPfKeys - 8) % 16 != 0) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) mx8[i] = fmaxf(mx8[i], s[kPfKeys - 8 + i]);
+            }
             // Raw scores: the max is taken before scaling (the scale is positive).
             const float mt = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]),
                                    fmaxf(mx8[6], mx8[7])) *
@@ -306,12 +327,12 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
                 m = mt;
             }
             // P_j = 2^(s*scale - m) <= 2^8 -> TMEM over the S columns (keys 2c, 2c+1 in
-            // column c; bf16 remainders in columns 64 + c), 32 keys at a time.  One key
+            // column c; bf16 remainders in columns 48 + c), 32 keys at a time.  One key
             // pair in four takes 2^x from the FMA pipe, the others from MUFU.  This
             // thread's S loads completed above.
             uint64_t sum2[4] = {0, 0, 0, 0};  // four f32 pairs of partial row sums (+0.0f bits)
 #pragma unroll
-            for (int ch = 0; ch < 4; ++ch) {
+            for (int ch = 0; ch < kPfKeys / 32; ++ch) {
                 uint32_t ph[16], pl[16];
 #pragma unroll
                 for (int k = 0; k < 16; ++k) {
@@ -328,13 +349,17 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
                     else ph[k] = pack_f16x2(p0, p1);
                 }
                 tmem_st16(t_s + 16 * ch, ph);
-                if (kSplitP) tmem_st16(t_s + 64 + 16 * ch, pl);
+                if (kSplitP) tmem_st16(t_s + kPfPCols + 16 * ch, pl);
             }
             float r0, r1, r2, r3;
             f2_unpack(f2_add(sum2[0], sum2[1]), r0, r1);
             f2_unpack(f2_add(sum2[2], sum2[3]), r2, r3);
             l = l * alpha + ((r0 + r1) + (r2 + r3));
-            if (__any_sync(0xffffffffu, rescale)) {  // O row *= alpha (O is idle, see above)
+            if (__any_sync(0xffffffffu, rescale)) {
+                // O row *= alpha, once P(j-1) V(j-1) has finished writing O
+                ok = warp_all(!s_err && mbar_wait(&bars.pv_done, (j - 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
                 const float f = rescale ? alpha : 1.f;
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
@@ -348,7 +373,7 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
             }
             tmem_wait_st();
             tc_fence_before();
-            mbar_arrive(&bars.p_full);
+            mbar_arrive(&bars.p_full[b]);
         }
         if (ok && nt > 0) {
             ok = warp_all(!s_err && mbar_wait(&bars.o_done, 0));
