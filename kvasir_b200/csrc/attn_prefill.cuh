@@ -21,7 +21,8 @@
 // the buffer of P(j), which P(j) V(j) has read -- MMAs issued by one thread
 // execute in issue order.
 // P goes back to TMEM over the S columns it came from.  bf16 inputs: P as a
-// bf16 head (columns 0-47 of the buffer) plus a bf16 remainder (48-95), two
+// bf16 head (columns 0-47 of the buffer, the truncated upper half of each f32)
+// plus a bf16 remainder (48-95), two
 // MMAs per key step, so P keeps ~16 significant bits (bf16 P alone, 8 bits,
 // puts the output ~3e-3 off for unit-scale inputs, outside the 2e-3 bar).
 // f16 inputs: P as one f16 (columns 0-47), within ~5e-4.
@@ -93,11 +94,6 @@ __device__ __forceinline__ uint64_t f2_pack(float a, float b) {
 __device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
     asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
 }
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t d;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-    return d;
-}
 __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
@@ -113,28 +109,16 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
     return d;
 }
-// 2^x for a pair on the FMA pipe, to take load off the MUFU unit that ex2.approx
-// uses.  x = n + f with n = round(x) (added to the exponent field) and f in
-// [-1/2, 1/2], where a degree-3 polynomial fitted here to 2^f (weighted least
-// squares on Chebyshev nodes, max relative error 7.5e-5, below the rounding of
-// the 16-bit P it feeds) supplies the mantissa.  x is clamped to [-126, 2^22]:
-// below 2^-126 the result is not a number of any consequence to a softmax
-// weight.  round(x) comes from adding 1.5 * 2^23, which leaves it in the low
-// mantissa bits of the sum.
-__device__ __forceinline__ void exp2_poly_pair(float& x0, float& x1) {
-    constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-    const uint64_t x = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
-    const uint64_t magic = f2_pack(kMagic, kMagic);
-    const uint64_t t = f2_add(x, magic);
-    const uint64_t f = f2_sub(x, f2_sub(t, magic));
-    uint64_t p = f2_fma(f2_pack(0.055171654f, 0.055171654f), f, f2_pack(0.24261113f, 0.24261113f));
-    p = f2_fma(p, f, f2_pack(0.69326097f, 0.69326097f));
-    p = f2_fma(p, f, f2_pack(0.99992806f, 0.99992806f));
-    float p0, p1, t0, t1;
-    f2_unpack(p, p0, p1);
-    f2_unpack(t, t0, t1);
-    x0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
-    x1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+// Two f32 as a packed bf16 head (the upper halves of their bit patterns, i.e.
+// truncated) and the packed bf16 remainder (p - head, rounded): the pair keeps
+// ~16 significant bits.  prmt picks bytes 2-3 of each operand.
+__device__ __forceinline__ void split_bf16_pair(float p0, float p1, uint32_t& hi, uint32_t& lo) {
+    asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(hi) : "r"(__float_as_uint(p0)), "r"(__float_as_uint(p1)));
+    float r0, r1;
+    f2_unpack(f2_sub(f2_pack(p0, p1), f2_pack(__uint_as_float(__float_as_uint(p0) & 0xffff0000u),
+                                              __uint_as_float(__float_as_uint(p1) & 0xffff0000u))),
+              r0, r1);
+    lo = Elem<__nv_bfloat16>::pack(r0, r1);
 }
 
 template <typename T>
@@ -327,8 +311,7 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
                 m = mt;
             }
             // P_j = 2^(s*scale - m) <= 2^8 -> TMEM over the S columns (keys 2c, 2c+1 in
-            // column c; bf16 remainders in columns 48 + c), 32 keys at a time.  One key
-            // pair in four takes 2^x from the FMA pipe, the others from MUFU.  This
+            // column c; bf16 remainders in columns 48 + c), 32 keys at a time.  This
             // thread's S loads completed above.
             uint64_t sum2[4] = {0, 0, 0, 0};  // four f32 pairs of partial row sums (+0.0f bits)
 #pragma unroll
@@ -336,16 +319,10 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
                 uint32_t ph[16], pl[16];
 #pragma unroll
                 for (int k = 0; k < 16; ++k) {
-                    float p0 = fmaf(s[32 * ch + 2 * k], a.scale_log2, -m);
-                    float p1 = fmaf(s[32 * ch + 2 * k + 1], a.scale_log2, -m);
-                    if ((k & 3) == 0) {
-                        exp2_poly_pair(p0, p1);
-                    } else {
-                        p0 = ex2_approx(p0);
-                        p1 = ex2_approx(p1);
-                    }
+                    const float p0 = ex2_approx(fmaf(s[32 * ch + 2 * k], a.scale_log2, -m));
+                    const float p1 = ex2_approx(fmaf(s[32 * ch + 2 * k + 1], a.scale_log2, -m));
                     sum2[k & 3] = f2_add(sum2[k & 3], f2_pack(p0, p1));
-                    if (kSplitP) split_pack<T>(p0, p1, ph[k], pl[k]);
+                    if (kSplitP) split_bf16_pair(p0, p1, ph[k], pl[k]);
                     else ph[k] = pack_f16x2(p0, p1);
                 }
                 tmem_st16(t_s + 16 * ch, ph);
