@@ -121,7 +121,20 @@ static void set_max_smem(F* kernel, int bytes) {
 // ---------------------------------------------------------------- rope / kv append launcher
 static int launch_rope(kvb_stream_t stream, const RopeArgs& a, int rows, int dtype, bool vec) {
     if (rows == 0) return KVB_OK;
-    if (vec) {
+    if (vec && a.do_rope && (a.hd == 64 || a.hd == 128)) {  // warp per row
+        const unsigned grid = (unsigned)((rows + 3) / 4);
+        if (a.hd == 64) {
+            if (dtype == KVB_BF16)
+                rope_append_warp_kernel<__nv_bfloat16, 4><<<grid, 128, 0, stream>>>(a, rows);
+            else
+                rope_append_warp_kernel<__half, 4><<<grid, 128, 0, stream>>>(a, rows);
+        } else {
+            if (dtype == KVB_BF16)
+                rope_append_warp_kernel<__nv_bfloat16, 8><<<grid, 128, 0, stream>>>(a, rows);
+            else
+                rope_append_warp_kernel<__half, 8><<<grid, 128, 0, stream>>>(a, rows);
+        }
+    } else if (vec) {
         if (dtype == KVB_BF16)
             rope_append_vec_kernel<__nv_bfloat16><<<rows, 256, 0, stream>>>(a);
         else

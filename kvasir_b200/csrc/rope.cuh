@@ -102,6 +102,80 @@ __global__ void __launch_bounds__(256) rope_append_vec_kernel(RopeArgs a) {
     }
 }
 
+// One warp per qkv row, four rows per CTA (rotate with or without append;
+// head_dim = 16 * CPR with CPR dividing 32, 16-byte aligned rows).  Lane l
+// always handles 8-pair chunk j = l mod CPR, so its cos/sin are loaded once per
+// row; it visits heads l / CPR, + 32 / CPR, ... and issues every load of a batch
+// of up to 6 heads before the first rotation.  Same arithmetic as the kernels
+// above, bit for bit.
+template <typename T, int CPR>
+__global__ void __launch_bounds__(128) rope_append_warp_kernel(RopeArgs a, int rows) {
+    constexpr int kHeadStep = 32 / CPR;
+    constexpr int kBatch = 6;
+    const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const int seq = row / a.rows_per_seq;
+    const int p = (a.pos_arr ? a.pos_arr[seq] : a.pos0) + row % a.rows_per_seq;
+    if (p < 0 || p >= a.max_pos || (a.do_append && p >= a.max_seq)) {
+        if (lane == 0) raise_dev_error(kDevErrBadPosition);
+        return;
+    }
+    constexpr int half = CPR * 8;
+    const int j = lane % CPR;
+    const float4* c4 = reinterpret_cast<const float4*>(a.cos_t + (size_t)p * half + 8 * j);
+    const float4* s4 = reinterpret_cast<const float4*>(a.sin_t + (size_t)p * half + 8 * j);
+    const float4 c0 = c4[0], c1 = c4[1], s0 = s4[0], s1 = s4[1];
+    const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    uint16_t* rowp = a.qkv + (size_t)row * a.row_stride;
+    const size_t cache0 = (size_t)seq * a.seq_stride;
+    const int n_heads = a.n_q + a.n_kv;
+    for (int h0 = lane / CPR; h0 < n_heads; h0 += kBatch * kHeadStep) {
+        uint4 va[kBatch], vb[kBatch];
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+            const int h = h0 + k * kHeadStep;
+            if (h < n_heads) {
+                va[k] = *reinterpret_cast<const uint4*>(rowp + h * 2 * half + 8 * j);
+                vb[k] = *reinterpret_cast<const uint4*>(rowp + h * 2 * half + 8 * j + half);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < kBatch; ++k) {
+            const int h = h0 + k * kHeadStep;
+            if (h < n_heads) {
+                float x0[8], x1[8], ra[8], rb[8];
+                unpack8<T>(va[k], x0);
+                unpack8<T>(vb[k], x1);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    ra[e] = rot_a(x0[e], x1[e], c[e], sn[e]);
+                    rb[e] = rot_b(x0[e], x1[e], c[e], sn[e]);
+                }
+                const uint4 oa = pack8<T>(ra), ob = pack8<T>(rb);
+                *reinterpret_cast<uint4*>(rowp + h * 2 * half + 8 * j) = oa;
+                *reinterpret_cast<uint4*>(rowp + h * 2 * half + 8 * j + half) = ob;
+                if (a.do_append && h >= a.n_q) {
+                    const size_t dst = cache0 + ((size_t)(h - a.n_q) * a.max_seq + p) * (2 * half);
+                    *reinterpret_cast<uint4*>(a.kc + dst + 8 * j) = oa;
+                    *reinterpret_cast<uint4*>(a.kc + dst + 8 * j + half) = ob;
+                }
+            }
+        }
+    }
+    if (a.do_append) {  // raw v heads into the cache, 16 bytes per lane per step
+        const int per = (2 * half) >> 3;
+        const uint16_t* vrow = rowp + (size_t)n_heads * 2 * half;
+        for (int vi = lane; vi < a.n_kv * per; vi += 32) {
+            const int kvh = vi / per, cc = vi - kvh * per;
+            const uint4 v = *reinterpret_cast<const uint4*>(vrow + kvh * 2 * half + 8 * cc);
+            const size_t dst = cache0 + ((size_t)kvh * a.max_seq + p) * (2 * half);
+            *reinterpret_cast<uint4*>(a.vc + dst + 8 * cc) = v;
+        }
+    }
+}
+
 // Any even head_dim, any alignment.
 template <typename T>
 __global__ void __launch_bounds__(256) rope_append_scalar_kernel(RopeArgs a) {
