@@ -55,55 +55,99 @@ def load_peaks():
 
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while running."""
+    """SM clock and clock-event (throttle) reasons of this rank's GPU, sampled while
+    the timed region runs: NVML polled every 10 ms from a thread, so that even a
+    timed region of ~100 ms gets several samples (first sample at entry); the
+    nvidia-smi loop (100 ms period) when NVML cannot be loaded.  The GPU is found
+    by PCI bus id, so CUDA_VISIBLE_DEVICES renumbering does not matter."""
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, device_index: int):
         self.dev = device_index
-        self.rows = []
+        self.rows = []      # (sm_mhz, max_mhz, [reason flags in REASONS order])
+        self.source = None
         self.proc = None
         self.thread = None
+        self.stop = threading.Event()
+
+    def _nvml_handle(self, nv):
+        try:
+            import torch
+            pr = torch.cuda.get_device_properties(self.dev)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.dev)
 
     def __enter__(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._nvml_handle(nv)
+            masks = (nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                     nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap)
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+
+            def poll():
+                while True:
+                    try:
+                        sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                        r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.rows.append((sm, mx, [bool(r & m) for m in masks]))
+                    except Exception:
+                        return
+                    if self.stop.wait(0.01):
+                        return
+
+            self.source = "nvml"
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            pass
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-i", str(self.dev), "-lms", "100"], stdout=subprocess.PIPE,
                 stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.source = "nvidia-smi"
+            self.thread = threading.Thread(target=self._read_smi, daemon=True)
             self.thread.start()
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
 
-    def _read(self):
+    def _read_smi(self):
         for line in self.proc.stdout:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                self.rows.append(parts)
+            if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                mx = float(parts[2]) if parts[2].replace(".", "").isdigit() else float("nan")
+                self.rows.append((float(parts[1]), mx,
+                                  [parts[5 + i].lower().startswith("active") for i in range(4)]))
 
     def __exit__(self, *exc):
+        self.stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self.thread is not None:
             self.thread.join(timeout=5)
 
     def summary(self):
-        if not self.rows:
+        rows = list(self.rows)
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in self.rows for i in range(4)
-                          if r[5 + i].lower().startswith("active")})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(self.rows)}
+        sm = [r[0] for r in rows]
+        mx = [r[1] for r in rows if r[1] == r[1]]
+        reasons = sorted({self.REASONS[i] for r in rows for i in range(4) if r[2][i]})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows), "source": self.source}
 
 
 # ----------------------------------------------------------------------------- dist
