@@ -182,6 +182,39 @@ int kvb_attention_decode(kvb_stream_t stream, const void* q, size_t q_row_stride
 size_t kvb_attention_decode_workspace_bytes(size_t n_seq, size_t max_len, size_t n_q,
                                             size_t n_kv, size_t head_dim);
 
+/* Paged KV cache -- the reference's planned stage-3 layout (kvasir
+ * DESIGN.md:66-70: "[block, kv_head, block_size, head_dim]"; only the address
+ * computation of attention / kv_append changes).  Per layer, K and V are pools
+ * of n_blocks = pool_len / (n_kv * block_size * head_dim) blocks laid out
+ * [n_blocks][n_kv][block_size][head_dim]; block_table is a device int32 array
+ * [n_seq][max_blocks], and position p of sequence b lives in block
+ * block_table[b * max_blocks + p / block_size] at offset p % block_size.  A
+ * table entry outside [0, n_blocks) sets kvb_device_error code 4 (the row is
+ * not written / those keys read as zeros); nothing faults.
+ *
+ * RoPE + KV append into the pools: qkv rows b*t .. b*t+t-1 belong to sequence b
+ * at positions pos[b] .. pos[b]+t-1 (pos: device int32 [n_seq]); q and k heads
+ * rotated in place, rotated k and raw v written to the blocks.  Equal, bit for
+ * bit, to kvb_rope_kv_append into a contiguous cache holding the same rows. */
+int kvb_rope_kv_append_paged(kvb_stream_t stream, void* qkv, size_t n_seq, size_t t,
+                             const int32_t* pos, const float* cos_t, const float* sin_t,
+                             size_t table_len, void* k_pool, void* v_pool, size_t pool_len,
+                             const int32_t* block_table, size_t max_blocks, size_t block_size,
+                             size_t n_q, size_t n_kv, size_t head_dim, int dtype);
+
+/* kvb_attention_decode over the pools: sequence b attends keys [0, lens[b]),
+ * lens[b] <= max_len <= max_blocks * block_size.  Requires head_dim 64,
+ * block_size a multiple of 64 and n_q / n_kv <= 16 (else KVB_ERR_UNSUPPORTED);
+ * the workspace is sized by kvb_attention_decode_workspace_bytes.  Equal, bit for
+ * bit, to kvb_attention_decode on a contiguous cache holding the same keys. */
+int kvb_attention_decode_paged(kvb_stream_t stream, const void* q, size_t q_row_stride,
+                               const void* k_pool, const void* v_pool, size_t pool_len,
+                               const int32_t* block_table, size_t max_blocks, size_t block_size,
+                               const int32_t* lens, size_t n_seq, size_t max_len, size_t n_q,
+                               size_t n_kv, size_t head_dim, float scale, void* out,
+                               size_t out_row_stride, void* workspace, size_t workspace_len,
+                               int dtype);
+
 /* No counterpart in the reference: an addition for callers that cannot
  * allocate device memory.  Same arguments and result as kvb_attention_decode
  * minus the workspace: the split-KV partials go to a scratch array that the

@@ -212,6 +212,34 @@ def cfg2(args):
            "peak": f"{peaks['hbm_gbs']} GB/s ({kind})", "l2": "flushed between launches",
            "cpu_oracle_ms": cpu_s * 1e3, "cpu_threads": _cpu_threads(),
            "cpu_gbs": alg / cpu_s / 1e9})
+    # The same keys in a paged cache: 64-key blocks of every sequence scattered
+    # through one shuffled pool (kvb_attention_decode_paged); output checked equal.
+    bs = 64
+    max_blocks = max_seq // bs
+    n_blocks = n_seq * max_blocks
+    perm = torch.from_numpy(np.random.default_rng(3).permutation(n_blocks).astype(np.int64)).cuda()
+    table = perm.view(n_seq, max_blocks).to(torch.int32)
+    src = lambda c: c.view(n_seq, nkv, max_blocks, bs, hd).permute(0, 2, 1, 3, 4).reshape(
+        n_blocks, nkv, bs, hd)
+    kpool = torch.empty(n_blocks * nkv * bs * hd, dtype=torch.bfloat16, device="cuda")
+    vpool = torch.empty_like(kpool)
+    kpool.view(n_blocks, nkv, bs, hd)[perm] = src(kc)
+    vpool.view(n_blocks, nkv, bs, hd)[perm] = src(vc)
+    out_p = torch.empty_like(out)
+
+    def run_paged():
+        g.attention_decode_paged(q, nq * hd, kpool, vpool, table, max_blocks, bs, lens_t, max_seq,
+                                 nq, nkv, hd, out_p, nq * hd, scale=0.125, workspace=ws)
+
+    for _ in range(5):
+        run_paged()
+    ms_p = time_each(run_paged, 50, flush)
+    gbs_p = alg / (ms_p * 1e-3) / 1e9
+    _emit({"workload": "cfg2 paged: the same decode over a shuffled pool of 64-key blocks",
+           "metric": "attention HBM GB/s", "value": gbs_p, "unit": "GB/s", "us": ms_p * 1e3,
+           "alg_bytes": alg, "frac_of_peak": gbs_p / peaks["hbm_gbs"],
+           "peak": f"{peaks['hbm_gbs']} GB/s ({kind})", "l2": "flushed between launches",
+           "equal_to_contiguous": bool(torch.equal(out_p, out))})
 
 
 # ----------------------------------------------------------------------------- config 3

@@ -43,7 +43,30 @@ struct DecodeArgs {
     float* ws;               // split-KV partials, or nullptr when chunks == 1
     int chunk_keys;          // keys per CTA (multiple of 256)
     int max_chunks;
+    // Paged cache (block_table != nullptr): K/V pools [n_blocks][n_kv][block_size][64];
+    // key k of sequence b lives in block block_table[b * max_blocks + k / block_size].
+    const int32_t* block_table;
+    int max_blocks, block_size, n_blocks;
 };
+
+// First row (of 64 elements) of the 64-key tile starting at key kt0 (a multiple of
+// 64) of kv head kvh of sequence b.  Paged: block_size is a multiple of 64, so the
+// tile lies inside one block; an entry outside [0, n_blocks) is reported and mapped
+// past the end of the pool, where the tensor copy reads zeros.
+__device__ __forceinline__ int decode_tile_row(const DecodeArgs& a, int b, int kvh, int row_base,
+                                               int kt0, int blk) {
+    if (!a.block_table) return row_base + kt0;
+    if (blk < 0 || blk >= a.n_blocks) {
+        raise_dev_error(kDevErrBadPosition);
+        return a.n_blocks * a.n_kv * a.block_size;
+    }
+    return (blk * a.n_kv + kvh) * a.block_size + kt0 % a.block_size;
+}
+__device__ __forceinline__ int decode_block_of(const DecodeArgs& a, int b, int kt0) {
+    if (!a.block_table) return 0;
+    const int lb = kt0 / a.block_size;
+    return lb < a.max_blocks ? a.block_table[(size_t)b * a.max_blocks + lb] : -1;
+}
 
 __device__ __forceinline__ int decode_len(const DecodeArgs& a, int b) {
     int len = a.lens ? a.lens[b] : a.len_const;
@@ -112,13 +135,18 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     uint32_t phase = 0;
     bool ok = true;
 
+    // paged: lane 0 reads the block of its next tile while the current one loads
+    int blk_next = lane == 0 ? decode_block_of(a, b, key_begin + warp * kDecTileKeys) : 0;
     for (int kt0 = key_begin + warp * kDecTileKeys; kt0 < key_end && ok;
          kt0 += kDecWarps * kDecTileKeys) {
         const int nk = min(kDecTileKeys, key_end - kt0);
         if (lane == 0) {
+            const int row = decode_tile_row(a, b, kvh, row_base, kt0, blk_next);
             mbar_expect_tx(&bars[warp], 2 * kDecTileBytes);
-            tma_load_2d(ktile, &kmap, &bars[warp], 0, row_base + kt0);
-            tma_load_2d(vtile, &vmap, &bars[warp], 0, row_base + kt0);
+            tma_load_2d(ktile, &kmap, &bars[warp], 0, row);
+            tma_load_2d(vtile, &vmap, &bars[warp], 0, row);
+            const int kn = kt0 + kDecWarps * kDecTileKeys;
+            if (kn < key_end) blk_next = decode_block_of(a, b, kn);
         }
         ok = mbar_wait(&bars[warp], phase);
         phase ^= 1;

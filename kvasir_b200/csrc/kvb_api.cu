@@ -187,6 +187,9 @@ struct DecodeLaunch {
     void* ws;
     size_t ws_len;
     int dtype;
+    // paged cache: pools [n_blocks][n_kv][block_size][64]; nullptr = contiguous
+    const int32_t* block_table = nullptr;
+    size_t max_blocks = 0, block_size = 0, n_blocks = 0;
 };
 
 static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
@@ -212,6 +215,10 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
     a.scale_log2 = L.scale * 1.4426950408889634f;
     a.out = static_cast<uint16_t*>(L.out);
     a.out_row_stride = (long long)L.out_row_stride;
+    a.block_table = L.block_table;
+    a.max_blocks = (int)L.max_blocks;
+    a.block_size = (int)L.block_size;
+    a.n_blocks = (int)L.n_blocks;
     int ck = decode_chunk_keys(L.n_seq, L.n_kv, L.max_len);
     const size_t need = decode_ws_bytes(L.n_seq, L.max_len, L.n_q, L.n_kv);
     if (need == 0 || L.ws == nullptr || L.ws_len < need || !aligned(L.ws, 16)) {
@@ -600,6 +607,49 @@ int kvb_rope_kv_append_batched(kvb_stream_t stream, void* qkv, size_t n_seq, con
     return launch_rope(stream, a, (int)n_seq, dtype, vec);
 }
 
+// Paged form: sequence b's t rows (qkv rows b*t .. b*t+t-1) go to positions
+// pos[b] .. pos[b]+t-1 of its blocks (block_table row b).
+int kvb_rope_kv_append_paged(kvb_stream_t stream, void* qkv, size_t n_seq, size_t t,
+                             const int32_t* pos, const float* cos_t, const float* sin_t,
+                             size_t table_len, void* k_pool, void* v_pool, size_t pool_len,
+                             const int32_t* block_table, size_t max_blocks, size_t block_size,
+                             size_t n_q, size_t n_kv, size_t head_dim, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(head_dim > 0 && head_dim % 2 == 0, "rope: odd head_dim %zu", head_dim);
+    KVB_CHECK(pos != nullptr && block_table != nullptr,
+              "rope_kv_append_paged: null position array or block table");
+    KVB_CHECK(table_len % (head_dim / 2) == 0, "rope: bad cos/sin table sizes");
+    KVB_CHECK(block_size > 0 && n_kv > 0, "rope_kv_append_paged: block_size and n_kv must be > 0");
+    const size_t per_block = n_kv * block_size * head_dim;
+    KVB_CHECK(pool_len % per_block == 0,
+              "rope_kv_append_paged: pool of %zu elems is not a whole number of %zu-elem blocks",
+              pool_len, per_block);
+    const size_t n_blocks = pool_len / per_block;
+    const size_t max_seq = max_blocks * block_size;
+    KVB_CHECK(fits_i32(n_seq * t) && fits_i32((n_q + 2 * n_kv) * head_dim) && fits_i32(max_seq) &&
+                  fits_i32(n_blocks) && fits_i32(table_len / (head_dim / 2)),
+              "rope_kv_append_paged: a dimension does not fit in i32");
+    if (n_seq == 0 || t == 0) return KVB_OK;
+    RopeArgs a = rope_args(qkv, n_q, n_kv, head_dim);
+    a.rows_per_seq = (int)t;
+    a.pos_arr = pos;
+    a.cos_t = cos_t;
+    a.sin_t = sin_t;
+    a.max_pos = (int)(table_len / (head_dim / 2));
+    a.kc = static_cast<uint16_t*>(k_pool);
+    a.vc = static_cast<uint16_t*>(v_pool);
+    a.max_seq = (int)max_seq;
+    a.block_table = block_table;
+    a.max_blocks = (int)max_blocks;
+    a.block_size = (int)block_size;
+    a.n_blocks = (int)n_blocks;
+    a.do_rope = 1;
+    a.do_append = 1;
+    const bool vec = head_dim % 16 == 0 && aligned(qkv, 16) && aligned(cos_t, 16) &&
+                     aligned(sin_t, 16) && aligned(k_pool, 16) && aligned(v_pool, 16);
+    return launch_rope(stream, a, (int)(n_seq * t), dtype, vec);
+}
+
 // ------------------------------------------------------------------ silu_mul
 int kvb_silu_mul(kvb_stream_t stream, const void* gu, size_t gu_len, void* out, size_t out_len,
                  size_t t, size_t inter, int dtype) {
@@ -865,6 +915,68 @@ int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, 
     a.out = static_cast<uint16_t*>(out);
     a.out_row_stride = (long long)(n_q * head_dim);
     return launch_generic_attn(stream, a, n_seq * t, dtype);
+}
+
+int kvb_attention_decode_paged(kvb_stream_t stream, const void* q, size_t q_row_stride,
+                               const void* k_pool, const void* v_pool, size_t pool_len,
+                               const int32_t* block_table, size_t max_blocks, size_t block_size,
+                               const int32_t* lens, size_t n_seq, size_t max_len, size_t n_q,
+                               size_t n_kv, size_t head_dim, float scale, void* out,
+                               size_t out_row_stride, void* workspace, size_t workspace_len,
+                               int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(n_kv > 0 && n_q % n_kv == 0,
+              "attention_decode_paged: n_q %zu not a multiple of n_kv %zu", n_q, n_kv);
+    KVB_CHECK(lens != nullptr && block_table != nullptr,
+              "attention_decode_paged: null lengths array or block table");
+    KVB_CHECK(block_size > 0, "attention_decode_paged: block_size must be > 0");
+    const size_t per_block = n_kv * block_size * head_dim;
+    KVB_CHECK(head_dim > 0 && pool_len % per_block == 0,
+              "attention_decode_paged: pool of %zu elems is not a whole number of %zu-elem blocks",
+              pool_len, per_block);
+    KVB_CHECK(max_len <= max_blocks * block_size,
+              "attention_decode_paged: max_len %zu exceeds %zu blocks of %zu", max_len, max_blocks,
+              block_size);
+    KVB_CHECK(q_row_stride >= n_q * head_dim, "attention_decode_paged: q_row_stride too small");
+    KVB_CHECK(out_row_stride >= n_q * head_dim, "attention_decode_paged: out_row_stride too small");
+    const size_t n_blocks = pool_len / per_block;
+    const size_t total_rows = pool_len / 64;
+    KVB_CHECK(fits_i32(n_seq) && fits_i32(max_len) && fits_i32(max_blocks) && fits_i32(n_blocks) &&
+                  fits_i32(n_seq * max_blocks),
+              "attention_decode_paged: a dimension does not fit in i32");
+    if (n_seq == 0) return KVB_OK;
+    const size_t group = n_q / n_kv;
+    if (!(head_dim == 64 && block_size % 64 == 0 && group <= 16 && n_seq <= 65535 &&
+          n_kv <= 65535 && q_row_stride % 8 == 0 && out_row_stride % 8 == 0 && aligned(q, 16) &&
+          aligned(k_pool, 16) && aligned(v_pool, 16) && fits_i32(total_rows + 64)))
+        return fail(KVB_ERR_UNSUPPORTED,
+                    "attention_decode_paged: needs head_dim 64, block_size a multiple of 64, "
+                    "n_q/n_kv <= 16 and 16-byte aligned buffers");
+    DecodeLaunch L;
+    L.q = q;
+    L.q_row_stride = q_row_stride;
+    L.kc = k_pool;
+    L.vc = v_pool;
+    L.seq_stride = 0;
+    L.total_rows = total_rows;
+    L.lens = lens;
+    L.len_const = 0;
+    L.n_seq = n_seq;
+    L.max_len = max_len;
+    L.n_q = n_q;
+    L.n_kv = n_kv;
+    L.max_seq = max_blocks * block_size;
+    L.scale = scale;
+    L.out = out;
+    L.out_row_stride = out_row_stride;
+    L.ws = workspace;
+    L.ws_len = workspace_len;
+    L.dtype = dtype;
+    L.block_table = block_table;
+    L.max_blocks = max_blocks;
+    L.block_size = block_size;
+    L.n_blocks = n_blocks;
+    return launch_decode_mma(stream, L);
 }
 
 }  // extern "C"

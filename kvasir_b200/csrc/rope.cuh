@@ -27,9 +27,34 @@ struct RopeArgs {
     uint16_t* kc;
     uint16_t* vc;
     long long seq_stride;    // elements between consecutive sequences' caches
-    int max_seq;
+    int max_seq;             // positions per sequence (paged: max_blocks * block_size)
     int do_rope, do_append;
+    // Paged cache (block_table != nullptr): kc/vc are pools [n_blocks][n_kv][block_size][hd];
+    // position p of sequence s lives in block block_table[s * max_blocks + p / block_size].
+    const int32_t* block_table;
+    int max_blocks, block_size, n_blocks;
 };
+
+// Cache element offset of (kv head 0, position p) of sequence seq, and the stride
+// between kv heads.  Returns false (and reports) when a paged block entry lies
+// outside the pool; the caller then writes nothing for the row.
+__device__ __forceinline__ bool rope_cache_base(const RopeArgs& a, int seq, int p, size_t& kv0,
+                                                size_t& head_stride, bool report) {
+    if (!a.block_table) {
+        kv0 = (size_t)seq * a.seq_stride + (size_t)p * a.hd;
+        head_stride = (size_t)a.max_seq * a.hd;
+        return true;
+    }
+    const int lb = p / a.block_size;
+    const int blk = a.block_table[(size_t)seq * a.max_blocks + lb];  // lb < max_blocks: p < max_seq
+    if (blk < 0 || blk >= a.n_blocks) {
+        if (report) raise_dev_error(kDevErrBadPosition);
+        return false;
+    }
+    kv0 = ((size_t)blk * a.n_kv * a.block_size + (size_t)(p - lb * a.block_size)) * a.hd;
+    head_stride = (size_t)a.block_size * a.hd;
+    return true;
+}
 
 __device__ __forceinline__ float rot_a(float x0, float x1, float c, float s) {
     return __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
@@ -57,7 +82,8 @@ __global__ void __launch_bounds__(256) rope_append_vec_kernel(RopeArgs a) {
     const int n_rope = (a.n_q + a.n_kv) * cpr;
     const int n_items = n_rope + a.n_kv * (a.hd >> 3);
     uint16_t* rowp = a.qkv + (size_t)row * a.row_stride;
-    const size_t cache0 = (size_t)seq * a.seq_stride;
+    size_t kv0 = 0, hs = 0;
+    if (a.do_append && !rope_cache_base(a, seq, p, kv0, hs, threadIdx.x == 0)) return;
     for (int it = threadIdx.x; it < n_items; it += blockDim.x) {
         if (it < n_rope) {
             const int h = it / cpr, j = it - h * cpr;
@@ -86,7 +112,7 @@ __global__ void __launch_bounds__(256) rope_append_vec_kernel(RopeArgs a) {
                 *pb = vb;
             }
             if (a.do_append && h >= a.n_q) {
-                const size_t dst = cache0 + ((size_t)(h - a.n_q) * a.max_seq + p) * a.hd;
+                const size_t dst = kv0 + (size_t)(h - a.n_q) * hs;
                 *reinterpret_cast<uint4*>(a.kc + dst + 8 * j) = va;
                 *reinterpret_cast<uint4*>(a.kc + dst + 8 * j + half) = vb;
             }
@@ -96,7 +122,7 @@ __global__ void __launch_bounds__(256) rope_append_vec_kernel(RopeArgs a) {
             const int kvh = vi / per, c = vi - kvh * per;
             const uint4 v =
                 *reinterpret_cast<const uint4*>(rowp + (a.n_q + a.n_kv) * a.hd + kvh * a.hd + 8 * c);
-            const size_t dst = cache0 + ((size_t)kvh * a.max_seq + p) * a.hd;
+            const size_t dst = kv0 + (size_t)kvh * hs;
             *reinterpret_cast<uint4*>(a.vc + dst + 8 * c) = v;
         }
     }
@@ -129,7 +155,8 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(RopeArgs a, int r
     const float c[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
     const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
     uint16_t* rowp = a.qkv + (size_t)row * a.row_stride;
-    const size_t cache0 = (size_t)seq * a.seq_stride;
+    size_t kv0 = 0, hs = 0;
+    if (a.do_append && !rope_cache_base(a, seq, p, kv0, hs, lane == 0)) return;
     const int n_heads = a.n_q + a.n_kv;
     for (int h0 = lane / CPR; h0 < n_heads; h0 += kBatch * kHeadStep) {
         uint4 va[kBatch], vb[kBatch];
@@ -157,7 +184,7 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(RopeArgs a, int r
                 *reinterpret_cast<uint4*>(rowp + h * 2 * half + 8 * j) = oa;
                 *reinterpret_cast<uint4*>(rowp + h * 2 * half + 8 * j + half) = ob;
                 if (a.do_append && h >= a.n_q) {
-                    const size_t dst = cache0 + ((size_t)(h - a.n_q) * a.max_seq + p) * (2 * half);
+                    const size_t dst = kv0 + (size_t)(h - a.n_q) * hs;
                     *reinterpret_cast<uint4*>(a.kc + dst + 8 * j) = oa;
                     *reinterpret_cast<uint4*>(a.kc + dst + 8 * j + half) = ob;
                 }
@@ -170,7 +197,7 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(RopeArgs a, int r
         for (int vi = lane; vi < a.n_kv * per; vi += 32) {
             const int kvh = vi / per, cc = vi - kvh * per;
             const uint4 v = *reinterpret_cast<const uint4*>(vrow + kvh * 2 * half + 8 * cc);
-            const size_t dst = cache0 + ((size_t)kvh * a.max_seq + p) * (2 * half);
+            const size_t dst = kv0 + (size_t)kvh * hs;
             *reinterpret_cast<uint4*>(a.vc + dst + 8 * cc) = v;
         }
     }
@@ -186,13 +213,14 @@ __global__ void __launch_bounds__(256) rope_append_scalar_kernel(RopeArgs a) {
     T* rowp = reinterpret_cast<T*>(a.qkv) + (size_t)row * a.row_stride;
     T* kc = reinterpret_cast<T*>(a.kc);
     T* vc = reinterpret_cast<T*>(a.vc);
-    const size_t cache0 = (size_t)seq * a.seq_stride;
+    size_t kv0 = 0, hs = 0;
+    if (a.do_append && !rope_cache_base(a, seq, p, kv0, hs, threadIdx.x == 0)) return;
     if (!a.do_rope) {  // plain kv_append: any head_dim, element copies
         for (int it = threadIdx.x; it < 2 * a.n_kv * a.hd; it += blockDim.x) {
             const int is_v = it >= a.n_kv * a.hd;
             const int i = it - is_v * a.n_kv * a.hd;
             const int kvh = i / a.hd, d = i - kvh * a.hd;
-            const size_t dst = cache0 + ((size_t)kvh * a.max_seq + p) * a.hd + d;
+            const size_t dst = kv0 + (size_t)kvh * hs + d;
             (is_v ? vc : kc)[dst] = rowp[(a.n_q + is_v * a.n_kv) * a.hd + i];
         }
         return;
@@ -214,14 +242,14 @@ __global__ void __launch_bounds__(256) rope_append_scalar_kernel(RopeArgs a) {
                 v[j + half] = tb;
             }
             if (a.do_append && h >= a.n_q) {
-                const size_t dst = cache0 + ((size_t)(h - a.n_q) * a.max_seq + p) * a.hd;
+                const size_t dst = kv0 + (size_t)(h - a.n_q) * hs;
                 kc[dst + j] = ta;
                 kc[dst + j + half] = tb;
             }
         } else if (a.do_append) {
             const int vi = it - n_rope;
             const int kvh = vi / a.hd, d = vi - kvh * a.hd;
-            const size_t dst = cache0 + ((size_t)kvh * a.max_seq + p) * a.hd;
+            const size_t dst = kv0 + (size_t)kvh * hs;
             vc[dst + d] = rowp[(a.n_q + a.n_kv) * a.hd + kvh * a.hd + d];
         }
     }

@@ -197,6 +197,36 @@ class Gpu:
             _ptr(kc), _ptr(vc), seq_stride, kc.numel(), n_q, n_kv, head_dim, max_seq,
             dtype_tag(qkv)))
 
+    def rope_kv_append_paged(self, qkv, n_seq, t, pos, cos, sin, k_pool, v_pool, block_table,
+                             max_blocks, block_size, n_q, n_kv, head_dim):
+        """kvb_rope_kv_append_paged: rows of sequence b at positions pos[b].. into the
+        K/V block pools [n_blocks, n_kv, block_size, head_dim] via block_table
+        [n_seq, max_blocks] (int32, device)."""
+        if pos.dtype != torch.int32 or block_table.dtype != torch.int32:
+            raise ShapeError("positions and block table must be int32")
+        if cos.numel() != sin.numel() or k_pool.numel() != v_pool.numel():
+            raise ShapeError("rope_kv_append_paged: cos/sin or pool sizes differ")
+        check(self._lib.kvb_rope_kv_append_paged(
+            self._s, _ptr(qkv), n_seq, t, _ptr(pos), _ptr(cos), _ptr(sin), cos.numel(),
+            _ptr(k_pool), _ptr(v_pool), k_pool.numel(), _ptr(block_table), max_blocks, block_size,
+            n_q, n_kv, head_dim, dtype_tag(qkv)))
+
+    def attention_decode_paged(self, q, q_row_stride, k_pool, v_pool, block_table, max_blocks,
+                               block_size, lens, max_len, n_q, n_kv, head_dim, out,
+                               out_row_stride, scale=None, workspace=None):
+        """kvb_attention_decode_paged: batched decode attention over K/V block pools."""
+        if lens.dtype != torch.int32 or block_table.dtype != torch.int32:
+            raise ShapeError("lengths and block table must be int32")
+        if k_pool.numel() != v_pool.numel():
+            raise ShapeError("attention_decode_paged: pool sizes differ")
+        scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
+        ws_len = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        check(self._lib.kvb_attention_decode_paged(
+            self._s, _ptr(q), q_row_stride, _ptr(k_pool), _ptr(v_pool), k_pool.numel(),
+            _ptr(block_table), max_blocks, block_size, _ptr(lens), lens.numel(), max_len, n_q,
+            n_kv, head_dim, scale, _ptr(out), out_row_stride,
+            _ptr(workspace) if workspace is not None else None, ws_len, dtype_tag(q)))
+
     def add_rmsnorm(self, x, y, w, out, rows, hidden, eps):
         check(self._lib.kvb_add_rmsnorm(self._s, _ptr(x), x.numel(), _ptr(y), y.numel(), _ptr(w),
                                         w.numel(), _ptr(out), out.numel(), rows, hidden, eps,

@@ -59,6 +59,19 @@ def test_shape_errors_are_reported_not_launched():
     st, msg = _status(lib.kvb_rope_kv_append_prefill, None, fake, 2 * 3 * 768, fake, fake, 16 * 32,
                       fake, fake, 2 * 2 * 16 * 64, 2, 3, 14, 8, 2, 64, 16, L.KVB_BF16)
     assert st == L.KVB_ERR_SHAPE and "exceed" in msg
+    # paged cache: the pool must be whole blocks of n_kv * block_size * head_dim
+    st, msg = _status(lib.kvb_attention_decode_paged, None, fake, 32 * 64, fake, fake, 3 * 8 * 64 * 64 + 1,
+                      fake, 4, 64, fake, 2, 100, 32, 8, 64, 0.125, fake, 32 * 64, None, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "whole number" in msg
+    st, msg = _status(lib.kvb_attention_decode_paged, None, fake, 32 * 64, fake, fake, 3 * 8 * 64 * 64,
+                      fake, 4, 64, fake, 2, 300, 32, 8, 64, 0.125, fake, 32 * 64, None, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "exceeds" in msg
+    st, msg = _status(lib.kvb_attention_decode_paged, None, fake, 32 * 64, fake, fake, 3 * 8 * 32 * 64,
+                      fake, 4, 32, fake, 2, 100, 32, 8, 64, 0.125, fake, 32 * 64, None, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_UNSUPPORTED and "multiple of 64" in msg
+    st, msg = _status(lib.kvb_rope_kv_append_paged, None, fake, 2, 1, fake, fake, fake, 16 * 32,
+                      fake, fake, 5 * 8 * 64 * 64 + 3, fake, 4, 64, 32, 8, 64, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "whole number" in msg
     st, msg = _status(lib.kvb_bf16_to_f16, None, fake, 10, fake, 10, fake, 2)
     assert st == L.KVB_ERR_SHAPE and "exactly one u32" in msg
     st, msg = _status(lib.kvb_embedding_gather, None, fake, 5, fake, 301, fake, 5 * 300, 300,
