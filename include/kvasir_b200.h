@@ -202,6 +202,19 @@ int kvb_rope_kv_append_paged(kvb_stream_t stream, void* qkv, size_t n_seq, size_
                              const int32_t* block_table, size_t max_blocks, size_t block_size,
                              size_t n_q, size_t n_kv, size_t head_dim, int dtype);
 
+/* kvb_attention_prefill over the pools: causal prefill of n_seq sequences of t
+ * query rows (qkv rows as for kvb_attention_prefill) at positions pos0 .. pos0+t-1,
+ * keys 0 .. pos0+t-1 read through the block table (pos0 + t <= max_blocks *
+ * block_size).  Requires head_dim 64 and block_size a multiple of 32 (else
+ * KVB_ERR_UNSUPPORTED).  Pool slots past a sequence's last key are never used,
+ * whatever they hold.  Equal, bit for bit, to kvb_attention_prefill on a
+ * contiguous cache holding the same keys. */
+int kvb_attention_prefill_paged(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                const void* k_pool, const void* v_pool, size_t pool_len,
+                                const int32_t* block_table, size_t max_blocks, size_t block_size,
+                                void* out, size_t out_len, size_t n_seq, size_t t, size_t pos0,
+                                size_t n_q, size_t n_kv, size_t head_dim, int dtype);
+
 /* kvb_attention_decode over the pools: sequence b attends keys [0, lens[b]),
  * lens[b] <= max_len <= max_blocks * block_size.  Requires head_dim 64,
  * block_size a multiple of 64 and n_q / n_kv <= 16 (else KVB_ERR_UNSUPPORTED);

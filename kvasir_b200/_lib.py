@@ -66,6 +66,8 @@ SIGNATURES = {
                                           _sz, _sz, _sz, _sz, _int]),
     "kvb_rope_kv_append_paged": (_int, [_p, _p, _sz, _sz, _p, _p, _p, _sz, _p, _p, _sz, _p, _sz,
                                         _sz, _sz, _sz, _sz, _int]),
+    "kvb_attention_prefill_paged": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _sz, _sz, _p, _sz, _sz,
+                                           _sz, _sz, _sz, _sz, _sz, _int]),
     "kvb_attention_decode_paged": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _sz, _sz, _p, _sz, _sz,
                                           _sz, _sz, _sz, C.c_float, _p, _sz, _p, _sz, _int]),
     "kvb_add_rmsnorm": (_int, [_p, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _sz, _sz, C.c_float, _int]),

@@ -289,6 +289,24 @@ def cfg3(args):
     att()
     ms_att = time_each(att, 30, flush)
     flops = 4.0 * n_seq * nq * (T * (T + 1) / 2) * hd
+    # The same prefill over a paged cache: 64-key blocks scattered through a pool.
+    bs = 64
+    max_blocks = T // bs
+    n_blocks = n_seq * max_blocks
+    perm = torch.from_numpy(np.random.default_rng(4).permutation(n_blocks).astype(np.int64)).cuda()
+    table = perm.view(n_seq, max_blocks).to(torch.int32)
+    blocks = lambda c: c.view(n_seq, nkv, max_blocks, bs, hd).permute(0, 2, 1, 3, 4).reshape(
+        n_blocks, nkv, bs, hd)
+    kpool = torch.empty_like(kc)
+    vpool = torch.empty_like(vc)
+    kpool.view(n_blocks, nkv, bs, hd)[perm] = blocks(kc)
+    vpool.view(n_blocks, nkv, bs, hd)[perm] = blocks(vc)
+    out_p = torch.empty_like(out)
+    att_p = lambda: g.attention_prefill_paged(qkv_work, kpool, vpool, table, max_blocks, bs, out_p,
+                                              n_seq, T, 0, nq, nkv, hd)
+    att_p()
+    ms_att_p = time_each(att_p, 30, flush)
+    paged_equal = bool(torch.equal(out_p, out))
     # SiLU*mul
     gu = torch.randn(rows * 2 * I, generator=gen, device="cuda").to(torch.bfloat16)
     act = torch.empty(rows * I, dtype=torch.bfloat16, device="cuda")
@@ -318,6 +336,12 @@ def cfg3(args):
            "peak": f"{peaks['bf16_tflops']} TFLOP/s ({kind}, burst)",
            "cpu_oracle_s_scaled": cpu_s, "cpu_sample": "1 of 32 (sequence, kv head) groups, x32",
            "cpu_threads": _cpu_threads()})
+    tflops_p = flops / (ms_att_p * 1e-3) / 1e12
+    _emit({"workload": "cfg3 paged: the same prefill attention over a shuffled pool of 64-key blocks",
+           "metric": "TFLOP/s", "value": tflops_p, "unit": "TFLOP/s", "us": ms_att_p * 1e3,
+           "flops": flops, "frac_of_peak": tflops_p / peaks["bf16_tflops"],
+           "peak": f"{peaks['bf16_tflops']} TFLOP/s ({kind}, burst)",
+           "equal_to_contiguous": paged_equal})
 
 
 # ----------------------------------------------------------------------------- config 4

@@ -59,7 +59,16 @@ struct PrefillArgs {
     float scale_log2;
     uint16_t* out;
     long long out_row_stride;
+    // Paged cache (block_table != nullptr): kmap / vmap are 2-D maps over the pools'
+    // rows of 64 elements ([n_blocks][n_kv][block_size] rows, box 32 rows); key k of
+    // sequence s is row (block_table[s * max_blocks + k / block_size] * n_kv + kvh)
+    // * block_size + k % block_size, block_size a multiple of 32.
+    const int32_t* block_table;
+    int max_blocks, block_size, n_blocks;
 };
+constexpr int kPfPagedPiece = 32;                 // rows per paged tensor copy (4 KB)
+constexpr int kPfTableSmem = 1024;                // block-table entries cached in smem
+constexpr int kPfPagedPieces = kPfKeys / kPfPagedPiece;
 
 struct PrefillBars {
     uint64_t q_full;
@@ -132,6 +141,7 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
     __shared__ PrefillBars bars;
     __shared__ uint32_t tmem_slot;
     __shared__ volatile int s_err;
+    __shared__ int s_table[kPfTableSmem];  // paged: this sequence's block-table row
     // bf16: P as head + remainder (two MMAs per key step); f16: P as one f16.
     constexpr bool kSplitP = Elem<T>::kDtype == KVB_BF16;
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -174,12 +184,41 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
 
     if (warp == kTmaWarp) {
         // ------------------------------------------------------------ TMA producer
+        // Paged: the whole warp first copies the blocks this CTA visits into shared
+        // memory (one global read per block, not per tile piece on the issuing lane).
+        const int seq_len = a.pos0 + a.t;
+        const int kv_end = min(seq_len, nt * kPfKeys);
+        const bool pow2 = a.block_table && (a.block_size & (a.block_size - 1)) == 0;
+        const int bs_shift = pow2 ? __ffs(a.block_size) - 1 : 0;
+        const int n_lb = a.block_table ? (kv_end + a.block_size - 1) / a.block_size : 0;
+        const bool cached = n_lb <= kPfTableSmem;
+        if (a.block_table && cached) {
+            for (int i = lane; i < n_lb; i += 32)
+                s_table[i] = i < a.max_blocks ? a.block_table[(size_t)seq * a.max_blocks + i]
+                                              : a.n_blocks;  // reported below
+            __syncwarp();
+        }
         if (lane == 0 && nt > 0) {
             tma_prefetch_desc(&kmap);
             tma_prefetch_desc(&vmap);
             mbar_expect_tx(&bars.q_full, kPfQBytes);
             tma_load_3d(sq, &qmap, &bars.q_full, h * 64, q0, seq);
             int issued = 0;
+            // Paged: block of each 32-key piece of a tile (kPastEnd: past the sequence end);
+            // the next tile's entries are read while this one's copies are in flight.
+            constexpr int kPastEnd = -2147483647 - 1;
+            auto piece_block = [&](int k) -> int {
+                if (k >= seq_len) return kPastEnd;
+                const int lb = pow2 ? k >> bs_shift : k / a.block_size;
+                if (cached) return s_table[lb];
+                return lb < a.max_blocks ? a.block_table[(size_t)seq * a.max_blocks + lb]
+                                         : a.n_blocks;  // reported below
+            };
+            int nblk[kPfPagedPieces];
+            if (a.block_table) {
+#pragma unroll
+                for (int i = 0; i < kPfPagedPieces; ++i) nblk[i] = piece_block(i * kPfPagedPiece);
+            }
             for (int j = 0; j < nt; ++j) {
                 const int st = j % kPfStages;
                 if (j >= kPfStages && !mbar_wait(&bars.kv_empty[st], ((j - kPfStages) / kPfStages) & 1)) {
@@ -187,11 +226,48 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
                     break;
                 }
                 if (s_err) break;
-                mbar_expect_tx(&bars.kv_full[st], 2 * kPfKVBytes);
-                tma_load_3d(skv + (2 * st) * kPfKVBytes, &kmap, &bars.kv_full[st], 0, j * kPfKeys,
-                            kv_plane);
-                tma_load_3d(skv + (2 * st + 1) * kPfKVBytes, &vmap, &bars.kv_full[st], 0,
-                            j * kPfKeys, kv_plane);
+                uint8_t* kdst = skv + (2 * st) * kPfKVBytes;
+                uint8_t* vdst = kdst + kPfKVBytes;
+                if (!a.block_table) {
+                    mbar_expect_tx(&bars.kv_full[st], 2 * kPfKVBytes);
+                    tma_load_3d(kdst, &kmap, &bars.kv_full[st], 0, j * kPfKeys, kv_plane);
+                    tma_load_3d(vdst, &vmap, &bars.kv_full[st], 0, j * kPfKeys, kv_plane);
+                } else {
+                    // 32-key pieces, each inside one block; pieces past the sequence end
+                    // are not loaded (the MMA warp zeroes those V rows).  A table entry
+                    // outside the pool is reported and read as zeros (rows past the map).
+                    int rows[kPfPagedPieces];
+                    uint32_t bytes = 0;
+#pragma unroll
+                    for (int i = 0; i < kPfPagedPieces; ++i) {
+                        const int k = j * kPfKeys + i * kPfPagedPiece;
+                        const int blk = nblk[i];
+                        rows[i] = -1;
+                        if (blk == kPastEnd) continue;
+                        if (blk < 0 || blk >= a.n_blocks) {
+                            raise_dev_error(kDevErrBadPosition);
+                            rows[i] = a.n_blocks * a.n_kv * a.block_size;
+                        } else {
+                            rows[i] = (blk * a.n_kv + kvh) * a.block_size +
+                                      (pow2 ? k & (a.block_size - 1) : k % a.block_size);
+                        }
+                        bytes += 2 * kPfPagedPiece * 128;
+                    }
+                    mbar_expect_tx(&bars.kv_full[st], bytes);
+#pragma unroll
+                    for (int i = 0; i < kPfPagedPieces; ++i) {
+                        if (rows[i] < 0) continue;
+                        tma_load_2d(kdst + i * kPfPagedPiece * 128, &kmap, &bars.kv_full[st], 0,
+                                    rows[i]);
+                        tma_load_2d(vdst + i * kPfPagedPiece * 128, &vmap, &bars.kv_full[st], 0,
+                                    rows[i]);
+                    }
+                    if (j + 1 < nt) {
+#pragma unroll
+                        for (int i = 0; i < kPfPagedPieces; ++i)
+                            nblk[i] = piece_block((j + 1) * kPfKeys + i * kPfPagedPiece);
+                    }
+                }
                 issued = j + 1;
             }
             if (s_err) {
@@ -248,6 +324,15 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
             ok = warp_all(!s_err && mbar_wait(&bars.p_full[j & 1], (j >> 1) & 1));
             if (!ok) break;
             tc_fence_after();
+            if (a.block_table && (j + 1) * kPfKeys > a.pos0 + a.t) {
+                // Paged: V rows past the sequence end hold whatever the pool holds there
+                // (a contiguous map reads zeros); P is 0 on them, but 0 * NaN is not 0.
+                uint4* vt = reinterpret_cast<uint4*>(skv + (2 * (j % kPfStages) + 1) * kPfKVBytes);
+                for (int i = (a.pos0 + a.t - j * kPfKeys) * 8 + lane; i < kPfKeys * 8; i += 32)
+                    vt[i] = make_uint4(0u, 0u, 0u, 0u);
+                fence_async_smem();
+                __syncwarp();
+            }
             issue_pv(j);  // then S(j + 2) reuses buffer j & 1 (read by this P V first)
             if (j + 1 == nt) umma_commit(&bars.o_done);
             if (j + 2 < nt) {

@@ -264,9 +264,11 @@ static int launch_generic_attn(kvb_stream_t stream, const GenericAttnArgs& a, si
     return KVB_OK;
 }
 
+// Paged form when block_table != nullptr: kc / vc are pools of pool_len elements.
 static int launch_prefill(kvb_stream_t stream, const void* qkv, const void* kc, const void* vc,
                           void* out, size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
-                          size_t max_seq, int dtype) {
+                          size_t max_seq, int dtype, const int32_t* block_table = nullptr,
+                          size_t max_blocks = 0, size_t block_size = 0, size_t pool_len = 0) {
     const size_t stride = (n_q + 2 * n_kv) * 64;
     CUtensorMap qmap, kmap, vmap;
     {
@@ -276,7 +278,7 @@ static int launch_prefill(kvb_stream_t stream, const void* qkv, const void* kc, 
         int st = encode_tmap(&qmap, qkv, 3, dims, strides, box, dtype);
         if (st) return st;
     }
-    {
+    if (!block_table) {
         const uint64_t dims[3] = {64, pos0 + t, n_seq * n_kv};
         const uint64_t strides[2] = {128, max_seq * 128};
         const uint32_t box[3] = {64, (uint32_t)kPfKeys, 1};
@@ -284,8 +286,20 @@ static int launch_prefill(kvb_stream_t stream, const void* qkv, const void* kc, 
         if (st) return st;
         st = encode_tmap(&vmap, vc, 3, dims, strides, box, dtype);
         if (st) return st;
+    } else {
+        const uint64_t dims[2] = {64, pool_len / 64};
+        const uint64_t strides[1] = {128};
+        const uint32_t box[2] = {64, (uint32_t)kPfPagedPiece};
+        int st = encode_tmap(&kmap, kc, 2, dims, strides, box, dtype);
+        if (st) return st;
+        st = encode_tmap(&vmap, vc, 2, dims, strides, box, dtype);
+        if (st) return st;
     }
     PrefillArgs a;
+    a.block_table = block_table;
+    a.max_blocks = (int)max_blocks;
+    a.block_size = (int)block_size;
+    a.n_blocks = block_table ? (int)(pool_len / (n_kv * block_size * 64)) : 0;
     a.t = (int)t;
     a.pos0 = (int)pos0;
     a.n_q = (int)n_q;
@@ -915,6 +929,44 @@ int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, 
     a.out = static_cast<uint16_t*>(out);
     a.out_row_stride = (long long)(n_q * head_dim);
     return launch_generic_attn(stream, a, n_seq * t, dtype);
+}
+
+int kvb_attention_prefill_paged(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                const void* k_pool, const void* v_pool, size_t pool_len,
+                                const int32_t* block_table, size_t max_blocks, size_t block_size,
+                                void* out, size_t out_len, size_t n_seq, size_t t, size_t pos0,
+                                size_t n_q, size_t n_kv, size_t head_dim, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    KVB_CHECK(n_kv > 0 && n_q % n_kv == 0,
+              "attention_prefill_paged: n_q %zu not a multiple of n_kv %zu", n_q, n_kv);
+    KVB_CHECK(block_table != nullptr, "attention_prefill_paged: null block table");
+    KVB_CHECK(block_size > 0 && head_dim > 0, "attention_prefill_paged: block_size must be > 0");
+    KVB_CHECK(qkv_len == n_seq * t * stride,
+              "attention_prefill_paged: qkv has %zu elems, want %zux%zux%zu", qkv_len, n_seq, t,
+              stride);
+    KVB_CHECK(out_len == n_seq * t * n_q * head_dim,
+              "attention_prefill_paged: out has %zu elems, want %zux%zux%zu", out_len, n_seq, t,
+              n_q * head_dim);
+    const size_t per_block = n_kv * block_size * head_dim;
+    KVB_CHECK(pool_len % per_block == 0,
+              "attention_prefill_paged: pool of %zu elems is not a whole number of %zu-elem blocks",
+              pool_len, per_block);
+    KVB_CHECK(pos0 + t <= max_blocks * block_size,
+              "attention_prefill_paged: positions up to %zu exceed %zu blocks of %zu", pos0 + t,
+              max_blocks, block_size);
+    KVB_CHECK(fits_i32(n_seq * t) && fits_i32(pos0 + t) && fits_i32(stride) &&
+                  fits_i32(n_seq * max_blocks) && fits_i32(pool_len / 64 + 64),
+              "attention_prefill_paged: a dimension does not fit in i32");
+    if (n_seq == 0 || t == 0) return KVB_OK;
+    if (!(head_dim == 64 && block_size % 32 == 0 && n_q <= 65535 && n_seq <= 65535 &&
+          aligned(qkv, 16) && aligned(k_pool, 16) && aligned(v_pool, 16) && aligned(out, 16)))
+        return fail(KVB_ERR_UNSUPPORTED,
+                    "attention_prefill_paged: needs head_dim 64, block_size a multiple of 32 and "
+                    "16-byte aligned buffers");
+    return launch_prefill(stream, qkv, k_pool, v_pool, out, n_seq, t, pos0, n_q, n_kv,
+                          max_blocks * block_size, dtype, block_table, max_blocks, block_size,
+                          pool_len);
 }
 
 int kvb_attention_decode_paged(kvb_stream_t stream, const void* q, size_t q_row_stride,

@@ -211,6 +211,18 @@ class Gpu:
             _ptr(k_pool), _ptr(v_pool), k_pool.numel(), _ptr(block_table), max_blocks, block_size,
             n_q, n_kv, head_dim, dtype_tag(qkv)))
 
+    def attention_prefill_paged(self, qkv, k_pool, v_pool, block_table, max_blocks, block_size,
+                                out, n_seq, t, pos0, n_q, n_kv, head_dim):
+        """kvb_attention_prefill_paged: causal prefill reading K/V through block_table."""
+        if block_table.dtype != torch.int32:
+            raise ShapeError("block table must be int32")
+        if k_pool.numel() != v_pool.numel():
+            raise ShapeError("attention_prefill_paged: pool sizes differ")
+        check(self._lib.kvb_attention_prefill_paged(
+            self._s, _ptr(qkv), qkv.numel(), _ptr(k_pool), _ptr(v_pool), k_pool.numel(),
+            _ptr(block_table), max_blocks, block_size, _ptr(out), out.numel(), n_seq, t, pos0,
+            n_q, n_kv, head_dim, dtype_tag(qkv)))
+
     def attention_decode_paged(self, q, q_row_stride, k_pool, v_pool, block_table, max_blocks,
                                block_size, lens, max_len, n_q, n_kv, head_dim, out,
                                out_row_stride, scale=None, workspace=None):

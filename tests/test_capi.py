@@ -72,6 +72,10 @@ def test_shape_errors_are_reported_not_launched():
     st, msg = _status(lib.kvb_rope_kv_append_paged, None, fake, 2, 1, fake, fake, fake, 16 * 32,
                       fake, fake, 5 * 8 * 64 * 64 + 3, fake, 4, 64, 32, 8, 64, L.KVB_BF16)
     assert st == L.KVB_ERR_SHAPE and "whole number" in msg
+    st, msg = _status(lib.kvb_attention_prefill_paged, None, fake, 2 * 5 * 3072, fake, fake,
+                      4 * 8 * 64 * 64, fake, 2, 64, fake, 2 * 5 * 2048, 2, 5, 130, 32, 8, 64,
+                      L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "exceed" in msg
     st, msg = _status(lib.kvb_bf16_to_f16, None, fake, 10, fake, 10, fake, 2)
     assert st == L.KVB_ERR_SHAPE and "exactly one u32" in msg
     st, msg = _status(lib.kvb_embedding_gather, None, fake, 5, fake, 301, fake, 5 * 300, 300,

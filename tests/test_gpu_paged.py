@@ -156,3 +156,41 @@ def test_paged_bad_block_entry_is_flagged_not_fatal(g):
     x = torch.ones(16, dtype=torch.bfloat16, device="cuda")
     g.add_inplace(x, x)
     assert float(x[0]) == 2.0
+
+
+@pytest.mark.parametrize("n_seq,t,pos0,bs", [(2, 300, 17, 32), (1, 129, 0, 64), (3, 200, 100, 128),
+                                             (1, 7, 90, 32)])
+def test_paged_prefill_equals_contiguous(g, n_seq, t, pos0, bs):
+    """Causal prefill through the block table == kvb_attention_prefill on the same keys;
+    the pool slots past each sequence's last key hold NaN, which must not leak in."""
+    rng = np.random.default_rng(n_seq * 1000 + t + pos0 + bs)
+    seq_len = pos0 + t
+    max_blocks = -(-seq_len // bs)
+    max_seq = max_blocks * bs
+    stride = (N_Q + 2 * N_KV) * HD
+    qkv = normal16(rng, n_seq * t * stride)
+    per = N_KV * max_seq * HD
+    kc = normal16(rng, n_seq * per).reshape(n_seq, N_KV, max_seq, HD)
+    vc = normal16(rng, n_seq * per).reshape(n_seq, N_KV, max_seq, HD)
+    nan = np.uint16(0x7FC0)
+    kc[:, :, seq_len:] = nan  # the contiguous map never reads past seq_len
+    vc[:, :, seq_len:] = nan
+    n_blocks = n_seq * max_blocks + 2
+    perm = np.random.default_rng(bs).permutation(n_blocks)
+    table = perm[:n_seq * max_blocks].reshape(n_seq, max_blocks).astype(np.int32)
+    kpool = normal16(rng, n_blocks * N_KV * bs * HD).reshape(n_blocks, N_KV, bs, HD)
+    vpool = normal16(rng, n_blocks * N_KV * bs * HD).reshape(n_blocks, N_KV, bs, HD)
+    for b in range(n_seq):
+        for lb in range(max_blocks):
+            kpool[table[b, lb]] = kc[b, :, lb * bs:(lb + 1) * bs]
+            vpool[table[b, lb]] = vc[b, :, lb * bs:(lb + 1) * bs]
+    want = torch.empty(n_seq * t * N_Q * HD, dtype=torch.bfloat16, device="cuda")
+    got = torch.empty_like(want)
+    g.attention_prefill(dev(qkv), dev(kc.ravel()), dev(vc.ravel()), want, n_seq, t, pos0, N_Q, N_KV,
+                        HD, max_seq)
+    g.attention_prefill_paged(dev(qkv), dev(kpool.ravel()), dev(vpool.ravel()),
+                              torch.from_numpy(table).cuda(), max_blocks, bs, got, n_seq, t, pos0,
+                              N_Q, N_KV, HD)
+    assert g.device_error() == 0
+    assert not torch.isnan(got.float()).any()
+    assert torch.equal(got, want)
