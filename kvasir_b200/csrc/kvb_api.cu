@@ -121,7 +121,9 @@ static void set_max_smem(F* kernel, int bytes) {
 // ---------------------------------------------------------------- rope / kv append launcher
 static int launch_rope(kvb_stream_t stream, const RopeArgs& a, int rows, int dtype, bool vec) {
     if (rows == 0) return KVB_OK;
-    if (vec && a.do_rope && (a.hd == 64 || a.hd == 128)) {  // warp per row
+    // Many rows (prefill): a warp per row.  Few rows (decode batches): a CTA per
+    // row, which puts more loads in flight per row.
+    if (vec && a.do_rope && (a.hd == 64 || a.hd == 128) && rows >= num_sms() * 8) {
         const unsigned grid = (unsigned)((rows + 3) / 4);
         if (a.hd == 64) {
             if (dtype == KVB_BF16)

@@ -92,12 +92,13 @@ def test_paged_decode_without_workspace_equals_contiguous(g):
     assert torch.equal(got, want)
 
 
-@pytest.mark.parametrize("t", [1, 5])
+@pytest.mark.parametrize("t", [1, 5, 700])
 def test_paged_rope_append_equals_contiguous(g, t):
     """Rows rotated identically, and the blocks gathered back in table order equal
-    the contiguous cache written by kvb_rope_kv_append (unwritten slots stay zero)."""
+    the contiguous cache written by kvb_rope_kv_append (unwritten slots stay zero).
+    t = 700 (2100 rows) takes the warp-per-row kernel, the others the CTA-per-row one."""
     rng = np.random.default_rng(90 + t)
-    n_seq, max_seq, bs = 3, 384, 64
+    n_seq, max_seq, bs = 3, 1024, 64
     pos = np.array([0, 70, 200], np.int32)
     stride = (N_Q + 2 * N_KV) * HD
     qkv = normal16(rng, n_seq * t * stride)
