@@ -273,7 +273,8 @@ def run_decode(args):
     first, n_local = shard_sequences(n_total, world, rank)
     K, W = args.steps, args.warmup
     max_seq = ctx + W + 2 * K + 2
-    dec = Decoder(cfg, n_local, max_seq, device=f"cuda:{local}", seed=0)
+    bs = args.paged or None
+    dec = Decoder(cfg, n_local, max_seq, device=f"cuda:{local}", seed=0, paged_block_size=bs)
     dec.fill_kv_normal(seed=1000 + rank)
     dec.set_lengths(ctx)
     rng = np.random.default_rng(7)
@@ -325,8 +326,13 @@ def run_decode(args):
     kc0, vc0 = dec.kc[0].reshape(-1), dec.vc[0].reshape(-1)
 
     def attn():
-        g.attention_decode(q, cfg.qkv_dim, kc0, vc0, per, lens, max_seq, nq, nkv, hd, max_seq,
-                           out, cfg.q_dim, workspace=ws)
+        if bs:
+            g.attention_decode_paged(q, cfg.qkv_dim, kc0, vc0, dec.block_table,
+                                     dec.block_table.shape[1], bs, lens, max_seq, nq, nkv, hd,
+                                     out, cfg.q_dim, workspace=ws)
+        else:
+            g.attention_decode(q, cfg.qkv_dim, kc0, vc0, per, lens, max_seq, nq, nkv, hd, max_seq,
+                               out, cfg.q_dim, workspace=ws)
 
     for _ in range(3):
         attn()
@@ -372,6 +378,8 @@ def run_decode(args):
                                    "(16 layers, random init), 256 sequences x 16384-token KV",
                        "n_seq_total": n_total, "context": ctx, "n_seq_per_gpu": n_local,
                        "parallelism": f"independent sequences over {world} GPU(s)",
+                       "kv_cache": (f"paged, {bs}-token blocks scattered by a seeded table"
+                                    if bs else "contiguous per sequence"),
                        "l2": "inputs larger than L2 (KV %.1f GB per GPU, weights 2.47 GB)" %
                              (2 * cfg.num_layers * n_local * per * 2 / 1e9)},
             "e2e": {"value": n_total / (e2e_ms / 1e3), "unit": "tokens/s",
@@ -381,7 +389,8 @@ def run_decode(args):
             "roofline": {"bound": "hbm", "achieved": achieved,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                         "kernel": "kvb_attention_decode (split-KV decode + combine), layer 0",
+                         "kernel": ("kvb_attention_decode_paged" if bs else "kvb_attention_decode")
+                                   + " (split-KV decode + combine), layer 0",
                          "alg_bytes_per_launch": alg_bytes, "ms_per_launch": attn_ms,
                          "peak_source": f"{peak_kind} hbm_gbs"},
             "cpu_baseline": cpu,
@@ -431,6 +440,9 @@ def main():
     ap.add_argument("--context", type=int, default=16384, help="KV tokens per sequence (cfg5)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--paged", type=int, default=0,
+                    help="cfg5 on a paged KV cache with this block size (a multiple of 64); "
+                         "0 = contiguous")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -306,6 +306,15 @@ int kvb_decoder_create(kvb_decoder_t* out, const kvb_decoder_config* cfg,
                        const kvb_decoder_weights* w, void* kc, void* vc, const float* cos_t,
                        const float* sin_t, void* workspace, size_t workspace_len);
 int kvb_decoder_destroy(kvb_decoder_t dec);
+/* Switches the driver to a paged KV cache (see kvb_attention_decode_paged):
+ * k_pools / v_pools hold n_layers pools of pool_len elements each
+ * ([n_layers][n_blocks][n_kv][block_size][head_dim]); block_table ([n_seq]
+ * [max_blocks] int32, device) is shared by all layers and must cover max_seq
+ * positions.  The kc / vc given to kvb_decoder_create are no longer used.
+ * Requires head_dim 64 and block_size a multiple of 64.  The next step records
+ * the paged step; call it outside any stream capture. */
+int kvb_decoder_use_paged_cache(kvb_decoder_t dec, void* k_pools, void* v_pools, size_t pool_len,
+                                const int32_t* block_table, size_t max_blocks, size_t block_size);
 /* Sets the per-sequence cache fill (tokens already in the cache) from a host
  * array; the next step writes position cur_len[b]. */
 int kvb_decoder_set_lengths(kvb_decoder_t dec, kvb_stream_t stream, const int32_t* cur_len_host);

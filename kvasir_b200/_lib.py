@@ -83,6 +83,7 @@ SIGNATURES = {
     "kvb_decoder_create": (_int, [C.POINTER(_p), C.POINTER(DecoderConfig),
                                   C.POINTER(DecoderWeights), _p, _p, _p, _p, _p, _sz]),
     "kvb_decoder_destroy": (_int, [_p]),
+    "kvb_decoder_use_paged_cache": (_int, [_p, _p, _p, _sz, _p, _sz, _sz]),
     "kvb_decoder_set_lengths": (_int, [_p, _p, _p]),
     "kvb_decoder_ids_in": (_p, [_p]),
     "kvb_decoder_ids_out": (_p, [_p]),

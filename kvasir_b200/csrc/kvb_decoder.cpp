@@ -73,6 +73,12 @@ struct kvb_decoder_s {
     std::vector<const void*> attn_norm, w_qkv, w_o, mlp_norm, w_gu, w_down;
     uint8_t* kc = nullptr;
     uint8_t* vc = nullptr;
+    // paged cache (kvb_decoder_use_paged_cache): per-layer pools of pool_len
+    // elements, one block table shared by all layers
+    uint8_t* kpool = nullptr;
+    uint8_t* vpool = nullptr;
+    size_t pool_len = 0, max_blocks = 0, block_size = 0;
+    const int32_t* block_table = nullptr;
     const float* cos_t = nullptr;
     const float* sin_t = nullptr;
     kvb_blas_t blas = nullptr;
@@ -113,20 +119,35 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
     STEP(kvb_rmsnorm(s, d->at(L.x), B * H, d->attn_norm[0], H, d->at(L.h), B * H, B, H, c.eps, dt),
          false);
     for (int l = 0; l < c.n_layers; ++l) {
-        uint8_t* kl = d->kc + (size_t)l * layer_elems * 2;
-        uint8_t* vl = d->vc + (size_t)l * layer_elems * 2;
         STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->w_qkv[l], qkvd * H, d->at(L.qkv), B * qkvd,
                         B, H, qkvd, dt, 0),
              true);
-        STEP(kvb_rope_kv_append_batched(s, d->at(L.qkv), B, d->at<int32_t>(L.pos), d->cos_t,
-                                        d->sin_t, table_len, kl, vl, seq_stride, layer_elems, nq,
-                                        nkv, hd, max_seq, dt),
-             false);
-        STEP(kvb_attention_decode(s, d->at(L.qkv), qkvd, kl, vl, seq_stride, layer_elems,
-                                  d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd, max_seq,
-                                  1.0f / sqrtf((float)hd), d->at(L.attn), qd, d->at(L.attn_ws),
-                                  L.attn_ws_len, dt),
-             false);
+        if (!d->block_table) {
+            uint8_t* kl = d->kc + (size_t)l * layer_elems * 2;
+            uint8_t* vl = d->vc + (size_t)l * layer_elems * 2;
+            STEP(kvb_rope_kv_append_batched(s, d->at(L.qkv), B, d->at<int32_t>(L.pos), d->cos_t,
+                                            d->sin_t, table_len, kl, vl, seq_stride, layer_elems,
+                                            nq, nkv, hd, max_seq, dt),
+                 false);
+            STEP(kvb_attention_decode(s, d->at(L.qkv), qkvd, kl, vl, seq_stride, layer_elems,
+                                      d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd, max_seq,
+                                      1.0f / sqrtf((float)hd), d->at(L.attn), qd, d->at(L.attn_ws),
+                                      L.attn_ws_len, dt),
+                 false);
+        } else {
+            uint8_t* kl = d->kpool + (size_t)l * d->pool_len * 2;
+            uint8_t* vl = d->vpool + (size_t)l * d->pool_len * 2;
+            STEP(kvb_rope_kv_append_paged(s, d->at(L.qkv), B, 1, d->at<int32_t>(L.pos), d->cos_t,
+                                          d->sin_t, table_len, kl, vl, d->pool_len, d->block_table,
+                                          d->max_blocks, d->block_size, nq, nkv, hd, dt),
+                 false);
+            STEP(kvb_attention_decode_paged(s, d->at(L.qkv), qkvd, kl, vl, d->pool_len,
+                                            d->block_table, d->max_blocks, d->block_size,
+                                            d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd,
+                                            1.0f / sqrtf((float)hd), d->at(L.attn), qd,
+                                            d->at(L.attn_ws), L.attn_ws_len, dt),
+                 false);
+        }
         if (L.attn_ws_len > 0) ++own;  // the split-KV combine pass
         STEP(kvb_linear(d->blas, s, d->at(L.attn), B * qd, d->w_o[l], H * qd, d->at(L.o), B * H, B,
                         qd, H, dt, 0),
@@ -229,6 +250,37 @@ int kvb_decoder_destroy(kvb_decoder_t d) {
     if (d->capture_stream) cudaStreamDestroy(d->capture_stream);
     kvb_blas_destroy(d->blas);
     delete d;
+    return KVB_OK;
+}
+
+int kvb_decoder_use_paged_cache(kvb_decoder_t d, void* k_pools, void* v_pools, size_t pool_len,
+                                const int32_t* block_table, size_t max_blocks, size_t block_size) {
+    KVB_CHECK(d && k_pools && v_pools && block_table, "decoder_use_paged_cache: null argument");
+    const kvb_decoder_config& c = d->cfg;
+    const size_t per_block = (size_t)c.n_kv * block_size * (size_t)c.head_dim;
+    KVB_CHECK(block_size > 0 && pool_len > 0 && pool_len % per_block == 0,
+              "decoder_use_paged_cache: pool of %zu elems is not a whole number of %zu-elem blocks",
+              pool_len, per_block);
+    KVB_CHECK(max_blocks * block_size >= (size_t)c.max_seq,
+              "decoder_use_paged_cache: %zu blocks of %zu hold fewer than max_seq %d positions",
+              max_blocks, block_size, c.max_seq);
+    if (!(c.head_dim == 64 && block_size % 64 == 0))
+        return kvb::fail(KVB_ERR_UNSUPPORTED,
+                         "decoder_use_paged_cache: needs head_dim 64 and block_size a multiple of 64");
+    d->kpool = static_cast<uint8_t*>(k_pools);
+    d->vpool = static_cast<uint8_t*>(v_pools);
+    d->pool_len = pool_len;
+    d->block_table = block_table;
+    d->max_blocks = max_blocks;
+    d->block_size = block_size;
+    if (d->exec) {  // the next step records the paged step
+        cudaGraphExecDestroy(d->exec);
+        d->exec = nullptr;
+    }
+    if (d->graph) {
+        cudaGraphDestroy(d->graph);
+        d->graph = nullptr;
+    }
     return KVB_OK;
 }
 

@@ -54,15 +54,27 @@ def random_weights(cfg: LlamaConfig, device, dtype=torch.bfloat16, seed: int = 0
 class Decoder:
     """Greedy decoding of n_seq sequences with KV capacity max_seq each.
 
-    kc / vc: [n_layers, n_seq, n_kv, max_seq, head_dim]."""
+    kc / vc: [n_layers, n_seq, n_kv, max_seq, head_dim], or with paged_block_size
+    the block pools [n_layers, n_blocks, n_kv, paged_block_size, head_dim] that
+    self.block_table ([n_seq, max_blocks], one table for all layers) indexes."""
 
     def __init__(self, cfg: LlamaConfig, n_seq: int, max_seq: int, device="cuda",
-                 dtype=torch.bfloat16, weights: dict | None = None, seed: int = 0):
+                 dtype=torch.bfloat16, weights: dict | None = None, seed: int = 0,
+                 paged_block_size: int | None = None):
         self.cfg, self.n_seq, self.max_seq = cfg, n_seq, max_seq
         self.device = torch.device(device)
         self.dtype = dtype
         self.w = weights if weights is not None else random_weights(cfg, self.device, dtype, seed)
         shape = (cfg.num_layers, n_seq, cfg.num_kv_heads, max_seq, cfg.head_dim)
+        if paged_block_size:
+            # kc / vc are then block pools [n_layers, n_blocks, n_kv, block_size, head_dim]
+            # with every sequence's blocks scattered through them by a seeded table
+            bs = paged_block_size
+            max_blocks = -(-max_seq // bs)
+            n_blocks = n_seq * max_blocks
+            shape = (cfg.num_layers, n_blocks, cfg.num_kv_heads, bs, cfg.head_dim)
+            perm = np.random.default_rng(seed + 1).permutation(n_blocks).astype(np.int32)
+            self.block_table = torch.from_numpy(perm.reshape(n_seq, max_blocks)).to(self.device)
         self.kc = torch.empty(shape, dtype=dtype, device=self.device)
         self.vc = torch.empty(shape, dtype=dtype, device=self.device)
         cos, sin = cos_sin_table(cfg, max_seq)
@@ -99,6 +111,8 @@ class Decoder:
             esz = torch.tensor([], dtype=dt).element_size()
             return self.workspace[off:off + n * esz].view(dt)
 
+        if paged_block_size:
+            self.use_paged_cache(self.kc, self.vc, self.block_table, max_blocks, paged_block_size)
         self.ids_in = view(lib.kvb_decoder_ids_in(h), n_seq, torch.int32)
         self.ids_out = view(lib.kvb_decoder_ids_out(h), n_seq, torch.int32)
         self.logits = view(lib.kvb_decoder_logits(h), n_seq * cfg.vocab_size,
@@ -123,6 +137,18 @@ class Decoder:
         for l in range(self.cfg.num_layers):
             self.kc[l].normal_(0.0, std, generator=g)
             self.vc[l].normal_(0.0, std, generator=g)
+
+    def use_paged_cache(self, k_pools, v_pools, block_table, max_blocks: int,
+                        block_size: int) -> None:
+        """Switch to a paged KV cache (kvb_decoder_use_paged_cache).  k_pools / v_pools:
+        [n_layers, n_blocks, n_kv, block_size, head_dim]; block_table: int32
+        [n_seq, max_blocks], shared by all layers.  The tensors are kept alive here."""
+        if block_table.dtype != torch.int32:
+            raise ShapeError("block table must be int32")
+        self._paged = (k_pools, v_pools, block_table)
+        check(self._lib.kvb_decoder_use_paged_cache(self._h, k_pools.data_ptr(),
+                                                    v_pools.data_ptr(), k_pools[0].numel(),
+                                                    block_table.data_ptr(), max_blocks, block_size))
 
     def set_lengths(self, cur_len) -> None:
         """Tokens already in each sequence's cache; the next step writes there."""

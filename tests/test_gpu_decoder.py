@@ -118,3 +118,50 @@ def test_decoder_step_host_equals_device_step():
         assert torch.equal(x, y)
     a.close()
     b.close()
+
+
+def test_decoder_paged_cache_equals_contiguous():
+    """kvb_decoder_use_paged_cache: the same step over a shuffled pool of 64-key
+    blocks (one block table for all layers) gives the same logits and ids, bit for
+    bit, as the contiguous cache, step after step (the appended K/V included)."""
+    from kvasir_b200.decoder import Decoder
+    cfg = _tiny_cfg()
+    rng = np.random.default_rng(23)
+    n_seq, max_seq, bs = 3, 192, 64
+    wb = _weights_bits(rng, cfg)
+    L, nkv, hd = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim
+    kv_shape = (L, n_seq, nkv, max_seq, hd)
+    kc = dev(O.from_f32(rng.normal(0, 1, int(np.prod(kv_shape))).astype(np.float32))).view(kv_shape)
+    vc = dev(O.from_f32(rng.normal(0, 1, int(np.prod(kv_shape))).astype(np.float32))).view(kv_shape)
+    max_blocks = max_seq // bs
+    n_blocks = n_seq * max_blocks + 2
+    perm = torch.from_numpy(np.random.default_rng(5).permutation(n_blocks)[:n_seq * max_blocks]
+                            .astype(np.int64)).cuda()
+    table = perm.view(n_seq, max_blocks).to(torch.int32)
+    kp = torch.zeros(L, n_blocks, nkv, bs, hd, dtype=torch.bfloat16, device="cuda")
+    vp = torch.zeros_like(kp)
+    blocks = lambda c: c.view(n_seq, nkv, max_blocks, bs, hd).permute(0, 2, 1, 3, 4).reshape(
+        n_seq * max_blocks, nkv, bs, hd)
+    for l in range(L):
+        kp[l][perm] = blocks(kc[l])
+        vp[l][perm] = blocks(vc[l])
+    cur = np.array([5, 63, 120], np.int32)
+    ids = torch.tensor([7, 300, 999], dtype=torch.int32, device="cuda")
+    decs = []
+    for paged in (False, True):
+        d = Decoder(cfg, n_seq, max_seq, weights=_to_torch(wb, cfg))
+        d.kc.copy_(kc)
+        d.vc.copy_(vc)
+        if paged:
+            d.use_paged_cache(kp, vp, table, max_blocks, bs)
+        d.set_lengths(cur)
+        d.ids_in.copy_(ids)
+        decs.append(d)
+    for step in range(4):
+        for d in decs:
+            d.step()
+        torch.cuda.synchronize()
+        assert torch.equal(decs[0].logits, decs[1].logits), f"step {step}"
+        assert torch.equal(decs[0].ids_out, decs[1].ids_out), f"step {step}"
+    for d in decs:
+        d.close()
