@@ -264,6 +264,13 @@ def cfg3(args):
     f()
     ms = time_each(f, 30, flush)
     res["rmsnorm"] = (ms, rows * H * 2 * 2 + H * 2)
+    # the same kernel on 4x the rows (268 MB in, 268 MB out: far above L2)
+    x4 = torch.randn(4 * rows * H, generator=gen, device="cuda").to(torch.bfloat16)
+    y4 = torch.empty_like(x4)
+    f = lambda: g.rmsnorm(x4, w, y4, 4 * rows, H, 1e-5)
+    f()
+    res["rmsnorm [32768, 2048] (4x the rows)"] = (time_each(f, 30, flush), 4 * rows * H * 2 * 2 + H * 2)
+    del x4, y4
     # RoPE + KV append (each sequence into its own empty cache)
     qkv = torch.randn(rows * cfg.qkv_dim, generator=gen, device="cuda").to(torch.bfloat16)
     qkv_work = qkv.clone()
@@ -316,9 +323,19 @@ def cfg3(args):
     res["silu_mul"] = (ms, rows * I * 2 * 3)
     for name, (ms, b) in res.items():
         gbs = b / (ms * 1e-3) / 1e9
+        # A device-to-device copy moving the same bytes (b/2 read + b/2 written), timed the
+        # same way: at working sets near the L2 size the launch and ramp of any kernel
+        # are a large part of its time, and this copy is what the hardware gives there.
+        src = torch.empty(b // 2, dtype=torch.uint8, device="cuda")
+        dst = torch.empty_like(src)
+        cp = lambda: dst.copy_(src)
+        cp()
+        cp_gbs = b / (time_each(cp, 30, flush) * 1e-3) / 1e9
+        del src, dst
         _emit({"workload": f"cfg3: prefill 4 x 2048, {name}", "metric": "HBM GB/s", "value": gbs,
                "unit": "GB/s", "us": ms * 1e3, "alg_bytes": b, "frac_of_peak": gbs / peaks["hbm_gbs"],
-               "peak": f"{peaks['hbm_gbs']} GB/s ({kind})", "l2": "flushed between launches"})
+               "peak": f"{peaks['hbm_gbs']} GB/s ({kind})", "l2": "flushed between launches",
+               "same_bytes_copy_gbs": cp_gbs, "frac_of_same_bytes_copy": gbs / cp_gbs})
     tflops = flops / (ms_att * 1e-3) / 1e12
     # CPU: one (sequence, kv head) group of the causal attention, scaled to all 32
     O.set_threads(_cpu_threads())

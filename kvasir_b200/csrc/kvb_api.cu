@@ -326,6 +326,38 @@ static int launch_prefill(kvb_stream_t stream, const void* qkv, const void* kc, 
 }
 
 // ---------------------------------------------------------------- norm launcher
+// Persistent bulk-copy RMSNorm: kNormBulkPerSm CTAs per SM, fewer if the
+// instantiation's registers or shared memory do not allow that many.
+template <typename K>
+static void launch_norm_bulk(K* kernel, int smem_cap, int smem, kvb_stream_t stream, void* x,
+                             const void* y, const void* w, void* out, size_t rows, size_t chunks,
+                             float ih, float eps) {
+    set_max_smem(kernel, smem_cap);
+    static std::mutex mu;
+    static std::vector<std::pair<std::pair<int, const void*>, std::pair<int, int>>> seen;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const void* key = reinterpret_cast<const void*>(kernel);
+    int per_sm = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        for (const auto& e : seen)
+            if (e.first.first == dev && e.first.second == key && e.second.first == smem)
+                per_sm = e.second.second;
+        if (!per_sm) {
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, kNormBulkThreads,
+                                                              smem) != cudaSuccess ||
+                per_sm < 1)
+                per_sm = 1;
+            seen.push_back({{dev, key}, {smem, per_sm}});
+        }
+    }
+    const size_t cap = (size_t)num_sms() * (per_sm < kNormBulkPerSm ? per_sm : kNormBulkPerSm);
+    const unsigned grid = (unsigned)(rows < cap ? rows : cap);
+    kernel<<<grid, kNormBulkThreads, smem, stream>>>((uint4*)x, (const uint4*)y, (const uint4*)w,
+                                                      (uint4*)out, (int)rows, (int)chunks, ih, eps);
+}
+
 template <bool kAdd>
 static int launch_rmsnorm(kvb_stream_t stream, void* x, const void* y, const void* w, void* out,
                           size_t rows, size_t hidden, float eps, int dtype) {
@@ -345,19 +377,21 @@ static int launch_rmsnorm(kvb_stream_t stream, void* x, const void* y, const voi
             rmsnorm_row_kernel<__half, kAdd><<<(unsigned)rows, (unsigned)chunks, 0, stream>>>(
                 (uint4*)x, (const uint4*)y, (const uint4*)w, (uint4*)out, (int)chunks, ih, eps);
     } else if (vec) {
-        const unsigned grid = (unsigned)((rows + 3) / 4);
         const float ih = 1.0f / (float)hidden;
         const int nv = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : chunks <= 256 ? 8 : 16;
+        const int smem = norm_bulk_smem_bytes((int)chunks, kAdd);
+#define KVB_NORM_LAUNCH(T, NV, FULL)                                                               \
+    launch_norm_bulk(rmsnorm_bulk_kernel<T, NV, kAdd, FULL>, norm_bulk_smem_cap(NV, kAdd), smem,    \
+                     stream, x, y, w, out, rows, chunks, ih, eps)
 #define KVB_NORM_CASE(NV)                                                                          \
     case NV:                                                                                       \
-        if (dtype == KVB_BF16)                                                                     \
-            rmsnorm_warp_kernel<__nv_bfloat16, NV, kAdd><<<grid, 128, 0, stream>>>(               \
-                (uint4*)x, (const uint4*)y, (const uint4*)w, (uint4*)out, (int)rows, (int)chunks, ih, \
-                eps);                                                                              \
-        else                                                                                       \
-            rmsnorm_warp_kernel<__half, NV, kAdd><<<grid, 128, 0, stream>>>(                      \
-                (uint4*)x, (const uint4*)y, (const uint4*)w, (uint4*)out, (int)rows, (int)chunks, ih, \
-                eps);                                                                              \
+        if (dtype == KVB_BF16) {                                                                   \
+            if (chunks == 32 * NV) KVB_NORM_LAUNCH(__nv_bfloat16, NV, true);                       \
+            else KVB_NORM_LAUNCH(__nv_bfloat16, NV, false);                                        \
+        } else {                                                                                   \
+            if (chunks == 32 * NV) KVB_NORM_LAUNCH(__half, NV, true);                              \
+            else KVB_NORM_LAUNCH(__half, NV, false);                                               \
+        }                                                                                          \
         break;
         switch (nv) {
             KVB_NORM_CASE(1)
@@ -367,6 +401,7 @@ static int launch_rmsnorm(kvb_stream_t stream, void* x, const void* y, const voi
             KVB_NORM_CASE(16)
         }
 #undef KVB_NORM_CASE
+#undef KVB_NORM_LAUNCH
     } else {
         if (dtype == KVB_BF16)
             rmsnorm_generic_kernel<__nv_bfloat16, kAdd><<<(unsigned)rows, 256, 0, stream>>>(

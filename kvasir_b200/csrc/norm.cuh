@@ -1,59 +1,158 @@
 // norm.cuh -- RMSNorm and the fused residual-add + RMSNorm.
 //
 // Reference kernel: engine/kernels/rmsnorm.cu:3-17 (one CTA per row, two passes
-// over global x with 2-byte loads).  Here one warp owns a row: the row is read
-// once with 16-byte loads into registers, the sum of squares is reduced with
-// warp shuffles, and out = x * rsqrt(mean + eps) * w is formed in f32 and
-// rounded once -- the same arithmetic order as the reference ((x*inv)*w).
+// over global x with 2-byte loads).  Here every row is read from HBM once, in
+// 16-byte pieces, and held in registers while its sum of squares is reduced.
 #pragma once
 
-#include "kvb_common.cuh"
+#include "kvb_ptx.cuh"
 
 namespace kvb {
 
-// NV = 16-byte chunks held per lane; the row has hidden/8 <= 32*NV chunks.
-template <typename T, int NV, bool kAdd>
-__global__ void __launch_bounds__(128) rmsnorm_warp_kernel(uint4* __restrict__ x,
-                                                           const uint4* __restrict__ y,
-                                                           const uint4* __restrict__ w,
-                                                           uint4* __restrict__ out, int rows,
-                                                           int chunks, float inv_hidden,
-                                                           float eps) {
-    const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= rows) return;
-    uint4* xr = x + (size_t)row * chunks;
-    float v[NV][8];
-    float ss = 0.f;
-#pragma unroll
-    for (int k = 0; k < NV; ++k) {
-        const int c = lane + 32 * k;
-        if (c < chunks) {
-            unpack8<T>(xr[c], v[k]);
-            if (kAdd) {
-                float d[8];
-                unpack8<T>(y[(size_t)row * chunks + c], d);
-#pragma unroll
-                for (int e = 0; e < 8; ++e) d[e] += v[k][e];
-                const uint4 s = pack8<T>(d);  // residual rounded to the activation type
-                xr[c] = s;
-                unpack8<T>(s, v[k]);
-            }
-#pragma unroll
-            for (int e = 0; e < 8; ++e) ss += v[k][e] * v[k][e];
+// Many rows: persistent CTAs (kNormBulkPerSm per SM), CTA c owning the
+// contiguous rows [c*rows/grid, (c+1)*rows/grid).  One lane streams them into a
+// shared-memory ring with bulk copies, kNormBulkWarps rows per stage (x, and y
+// when the residual add is fused); consumer warp j normalises row j of each
+// stage: the row is unpacked into registers, the sum of squares reduced with
+// warp shuffles, and out = x * rsqrt(mean + eps) * w formed in f32 and rounded
+// once -- the reference's arithmetic order ((x*inv)*w).  The ring keeps ~96 KB
+// of every CTA's reads in flight whatever the per-row work, so the kernel runs
+// at the speed of a device-to-device copy of the same bytes.
+// NV = 16-byte chunks per lane (the row has chunks <= 32*NV of them).
+constexpr int kNormBulkWarps = 4;
+constexpr int kNormBulkThreads = 32 * (kNormBulkWarps + 1);
+constexpr int kNormBulkPerSm = 2;
+constexpr int kNormBulkRingBytes = 96 * 1024;
+
+__host__ __device__ constexpr int norm_bulk_stage_bytes(int chunks, bool add) {
+    return kNormBulkWarps * chunks * 16 * (add ? 2 : 1);
+}
+// Stages of the ring for a row width: as many as fit kNormBulkRingBytes, 2..12.
+__host__ __device__ constexpr int norm_bulk_stages(int chunks, bool add) {
+    return kNormBulkRingBytes / norm_bulk_stage_bytes(chunks, add) < 2 ? 2
+           : kNormBulkRingBytes / norm_bulk_stage_bytes(chunks, add) > 12
+               ? 12
+               : kNormBulkRingBytes / norm_bulk_stage_bytes(chunks, add);
+}
+// Dynamic shared memory: 24 mbarriers (256 B), the weights, then the ring.
+__host__ __device__ constexpr int norm_bulk_smem_bytes(int chunks, bool add) {
+    return 256 + ((chunks * 16 + 127) & ~127) +
+           norm_bulk_stages(chunks, add) * norm_bulk_stage_bytes(chunks, add);
+}
+// Upper bound of norm_bulk_smem_bytes over the widths one NV serves (chunks <= 32*NV).
+__host__ __device__ constexpr int norm_bulk_smem_cap(int nv, bool add) {
+    return 256 + 32 * nv * 16 +
+           (2 * norm_bulk_stage_bytes(32 * nv, add) > kNormBulkRingBytes
+                ? 2 * norm_bulk_stage_bytes(32 * nv, add)
+                : kNormBulkRingBytes);
+}
+
+// kFull: chunks == 32*NV (every lane holds NV chunks; no per-chunk guards).
+// Weights sit in registers for NV <= 8, in shared memory above that.
+template <typename T, int NV, bool kAdd, bool kFull>
+__global__ void __launch_bounds__(kNormBulkThreads) rmsnorm_bulk_kernel(
+    uint4* __restrict__ x, const uint4* __restrict__ y, const uint4* __restrict__ w,
+    uint4* __restrict__ out, int rows, int chunks_arg, float inv_hidden, float eps) {
+    constexpr bool kWReg = NV <= 8;
+    const int chunks = kFull ? 32 * NV : chunks_arg;
+    extern __shared__ __align__(128) uint8_t norm_smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(norm_smem);  // [12]
+    uint64_t* empty = full + 12;                                 // [12]
+    uint4* ws = reinterpret_cast<uint4*>(norm_smem + 256);
+    // ring after the weights, 128-byte aligned
+    uint8_t* ring = norm_smem + 256 + ((chunks * 16 + 127) & ~127);
+    const int stages = norm_bulk_stages(chunks, kAdd);
+    const int row_bytes = chunks * 16;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = (int)((long long)blockIdx.x * rows / gridDim.x);
+    const int r1 = (int)((long long)(blockIdx.x + 1) * rows / gridDim.x);
+    const int groups = (r1 - r0 + kNormBulkWarps - 1) / kNormBulkWarps;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kNormBulkWarps);
         }
+        fence_mbar_init();
     }
-    ss = warp_sum(ss);
-    const float inv = rsqrtf(ss * inv_hidden + eps);
+    __syncthreads();
+    if (warp == kNormBulkWarps) {  // producer
+        if (lane != 0) return;
+        int issued = 0;
+        for (int g = 0; g < groups; ++g) {
+            const int s = g % stages;
+            if (g >= stages && !mbar_wait(&empty[s], ((g / stages) - 1) & 1)) break;
+            const int row = r0 + g * kNormBulkWarps;
+            const uint32_t n = (uint32_t)min(kNormBulkWarps, r1 - row) * row_bytes;
+            uint8_t* dst = ring + (size_t)s * norm_bulk_stage_bytes(chunks, kAdd);
+            mbar_expect_tx(&full[s], kAdd ? 2 * n : n);
+            bulk_load(dst, x + (size_t)row * chunks, n, &full[s]);
+            if (kAdd) bulk_load(dst + kNormBulkWarps * row_bytes, y + (size_t)row * chunks, n, &full[s]);
+            ++issued;
+        }
+        // no copy may still be landing in this CTA's shared memory when it exits
+        for (int g = max(0, issued - stages); g < issued; ++g)
+            mbar_wait(&full[g % stages], (g / stages) & 1);
+        return;
+    }
+    uint4 wr[kWReg ? NV : 1];
+    if (kWReg) {
 #pragma unroll
-    for (int k = 0; k < NV; ++k) {
-        const int c = lane + 32 * k;
-        if (c < chunks) {
-            float wf[8];
-            unpack8<T>(w[c], wf);
+        for (int k = 0; k < NV; ++k) {
+            const int c = lane + 32 * k;
+            if (kFull || c < chunks) wr[k] = w[c];
+        }
+    } else {
+        for (int c = threadIdx.x; c < chunks; c += 32 * kNormBulkWarps) ws[c] = w[c];
+        named_bar_sync(1, 32 * kNormBulkWarps);  // the consumer warps only
+    }
+    for (int g = 0; g < groups; ++g) {
+        const int s = g % stages;
+        if (!mbar_wait(&full[s], (g / stages) & 1)) return;
+        const int row = r0 + g * kNormBulkWarps + warp;
+        if (row < r1) {
+            const uint8_t* st = ring + (size_t)s * norm_bulk_stage_bytes(chunks, kAdd);
+            const uint4* xs = reinterpret_cast<const uint4*>(st + warp * row_bytes);
+            const uint4* ys = reinterpret_cast<const uint4*>(st + (kNormBulkWarps + warp) * row_bytes);
+            uint4* xg = x + (size_t)row * chunks;
+            uint4* og = out + (size_t)row * chunks;
+            float v[NV][8];
+            float ss = 0.f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) v[k][e] = v[k][e] * inv * wf[e];
-            out[(size_t)row * chunks + c] = pack8<T>(v[k]);
+            for (int k = 0; k < NV; ++k) {
+                const int c = lane + 32 * k;
+                if (kFull || c < chunks) {
+                    unpack8<T>(xs[c], v[k]);
+                    if (kAdd) {
+                        float d[8];
+                        unpack8<T>(ys[c], d);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) d[e] += v[k][e];
+                        const uint4 r = pack8<T>(d);  // residual rounded to the activation type
+                        xg[c] = r;
+                        unpack8<T>(r, v[k]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) ss += v[k][e] * v[k][e];
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);  // the row is in registers now
+            ss = warp_sum(ss);
+            const float inv = rsqrtf(ss * inv_hidden + eps);
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                const int c = lane + 32 * k;
+                if (kFull || c < chunks) {
+                    float wf[8];
+                    unpack8<T>(kWReg ? wr[kWReg ? k : 0] : ws[c], wf);
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) v[k][e] = v[k][e] * inv * wf[e];
+                    og[c] = pack8<T>(v[k]);
+                }
+            }
+        } else {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
     }
 }

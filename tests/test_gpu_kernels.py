@@ -59,9 +59,13 @@ def test_embedding_prefill_rows(g):
 
 # ------------------------------------------------------------------ rmsnorm
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("rows,hidden", [(5, 2048), (3, 100), (1, 2048), (7, 4096), (2, 8)])
+@pytest.mark.parametrize("rows,hidden", [(5, 2048), (3, 100), (1, 2048), (7, 4096), (2, 8),
+                                         (1000, 2048), (700, 4096), (2000, 512), (1500, 1032),
+                                         (601, 256), (3, 136)])
 def test_rmsnorm_within_one_ulp(g, dtype, rows, hidden):
-    """reference shapes engine/tests/kernels.rs:50-82 (x ±3, w ±1.5)"""
+    """reference shapes engine/tests/kernels.rs:50-82 (x ±3, w ±1.5), plus row counts
+    above 4 per SM and widths of 1 … 16 chunks per lane, ragged ones included, for the
+    persistent bulk-copy kernel (rows split unevenly over the CTAs)"""
     rng = np.random.default_rng(2)
     x = O.uniform16(rng, rows * hidden, 3.0, dtype)
     w = O.uniform16(rng, hidden, 1.5, dtype)
@@ -84,7 +88,8 @@ def test_rmsnorm_prefill_shape(g):
     assert_within_ulp(host_bits(out), O.rmsnorm(x, w, rows, hidden, 1e-5), name="rmsnorm")
 
 
-@pytest.mark.parametrize("rows,hidden", [(4, 2048), (3, 100)])
+@pytest.mark.parametrize("rows,hidden", [(4, 2048), (3, 100), (1000, 2048), (700, 4096),
+                                         (650, 520), (5, 16)])
 def test_add_rmsnorm_equals_add_then_rmsnorm(g, rows, hidden):
     rng = np.random.default_rng(5)
     x, y = normal16(rng, rows * hidden), normal16(rng, rows * hidden)
