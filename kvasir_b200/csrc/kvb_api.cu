@@ -119,11 +119,56 @@ static void set_max_smem(F* kernel, int bytes) {
 }
 
 // ---------------------------------------------------------------- rope / kv append launcher
+// Persistent bulk-copy RoPE: 16 consumer warps when two 16-row stages fit in
+// 200 KB of shared memory, else 8 or 4; as many CTAs per SM as fit, at most 2.
+// Returns false when even 4 rows per stage do not fit (the caller falls back).
+template <typename T, int CPR>
+static bool launch_rope_bulk(kvb_stream_t stream, const RopeArgs& a, int rows) {
+    const int rb = rope_bulk_row_bytes(a);
+    int warps = 16;
+    while (warps > 4 && 2 * warps * rb > 200 * 1024) warps /= 2;
+    const int smem = rope_bulk_smem_bytes(a, warps);
+    if (smem > 227 * 1024) return false;
+    int per_sm = (228 * 1024) / (smem + 1024);
+    per_sm = per_sm < 1 ? 1 : per_sm > 2 ? 2 : per_sm;
+    if (warps == 16) per_sm = 1;
+    const int cap = num_sms() * per_sm;
+    const unsigned grid = (unsigned)(rows < cap ? rows : cap);
+    const unsigned threads = 32u * (warps + 1);
+    switch (warps) {
+        case 16:
+            set_max_smem(rope_append_bulk_kernel<T, CPR, 16>, 227 * 1024);
+            rope_append_bulk_kernel<T, CPR, 16><<<grid, threads, smem, stream>>>(a, rows);
+            break;
+        case 8:
+            set_max_smem(rope_append_bulk_kernel<T, CPR, 8>, 227 * 1024);
+            rope_append_bulk_kernel<T, CPR, 8><<<grid, threads, smem, stream>>>(a, rows);
+            break;
+        default:
+            set_max_smem(rope_append_bulk_kernel<T, CPR, 4>, 227 * 1024);
+            rope_append_bulk_kernel<T, CPR, 4><<<grid, threads, smem, stream>>>(a, rows);
+            break;
+    }
+    return true;
+}
+
 static int launch_rope(kvb_stream_t stream, const RopeArgs& a, int rows, int dtype, bool vec) {
     if (rows == 0) return KVB_OK;
-    // Many rows (prefill): a warp per row.  Few rows (decode batches): a CTA per
-    // row, which puts more loads in flight per row.
-    if (vec && a.do_rope && (a.hd == 64 || a.hd == 128) && rows >= num_sms() * 8) {
+    // Many rows (prefill): persistent bulk-copy CTAs.  Few rows (decode batches): a
+    // CTA per row, which puts more loads in flight per row.
+    const bool many = vec && a.do_rope && (a.hd == 64 || a.hd == 128) && rows >= num_sms() * 8;
+    bool done = false;
+    if (many && (a.row_stride * 2) % 16 == 0) {
+        if (a.hd == 64)
+            done = dtype == KVB_BF16 ? launch_rope_bulk<__nv_bfloat16, 4>(stream, a, rows)
+                                     : launch_rope_bulk<__half, 4>(stream, a, rows);
+        else
+            done = dtype == KVB_BF16 ? launch_rope_bulk<__nv_bfloat16, 8>(stream, a, rows)
+                                     : launch_rope_bulk<__half, 8>(stream, a, rows);
+    }
+    if (done) {
+        // launched by launch_rope_bulk
+    } else if (many) {  // rows too wide for the ring: a warp per row
         const unsigned grid = (unsigned)((rows + 3) / 4);
         if (a.hd == 64) {
             if (dtype == KVB_BF16)

@@ -11,7 +11,7 @@
 // test (engine/tests/kernels.rs:121-132), then rounded once.
 #pragma once
 
-#include "kvb_common.cuh"
+#include "kvb_ptx.cuh"
 
 namespace kvb {
 
@@ -200,6 +200,153 @@ __global__ void __launch_bounds__(128) rope_append_warp_kernel(RopeArgs a, int r
             const size_t dst = kv0 + (size_t)kvh * hs;
             *reinterpret_cast<uint4*>(a.vc + dst + 8 * cc) = v;
         }
+    }
+}
+
+// Many rows (prefill), rotate with or without append, head_dim = 16 * CPR:
+// persistent CTAs each own the contiguous rows [c*rows/grid, (c+1)*rows/grid).
+// One lane streams the rows' q, k (and v) heads into a shared-memory ring with
+// bulk copies, kWarps rows per stage; warp j rotates row j of a stage from
+// shared memory and stores q and k back in place, k and v to the cache.  A warp
+// fetches its next row's cos/sin (and block-table entry) before it waits for
+// the row's copy.  Lane l handles 8-pair chunk l mod CPR of heads l / CPR,
+// + 32 / CPR, ...: the same arithmetic as the kernels above, bit for bit.
+// The launcher takes 16 warps (one CTA per SM) when two 16-row stages fit in
+// shared memory, else 8 or 4: with fewer rows in flight per SM the per-row
+// latency of the consumer warps, not HBM, sets the pace.
+constexpr int kRopeBulkRingBytes = 96 * 1024;
+
+// Bytes of one row that the kernel copies: q and k heads, and v when appending.
+__host__ __device__ inline int rope_bulk_row_bytes(const RopeArgs& a) {
+    return (a.n_q + a.n_kv + (a.do_append ? a.n_kv : 0)) * a.hd * 2;
+}
+__host__ __device__ inline int rope_bulk_stages(const RopeArgs& a, int warps) {
+    const int st = kRopeBulkRingBytes / (warps * rope_bulk_row_bytes(a));
+    return st < 2 ? 2 : st > 12 ? 12 : st;
+}
+__host__ __device__ inline int rope_bulk_smem_bytes(const RopeArgs& a, int warps) {
+    return 256 + rope_bulk_stages(a, warps) * warps * rope_bulk_row_bytes(a);
+}
+
+template <typename T, int CPR, int kWarps, int kBatch = 1>
+__global__ void __launch_bounds__(32 * (kWarps + 1)) rope_append_bulk_kernel(RopeArgs a, int rows) {
+    constexpr int kHeadStep = 32 / CPR;
+    constexpr int half = CPR * 8;
+    extern __shared__ __align__(128) uint8_t rope_smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(rope_smem);  // [12]
+    uint64_t* empty = full + 12;                                 // [12]
+    uint8_t* ring = rope_smem + 256;
+    const int row_bytes = rope_bulk_row_bytes(a);
+    const int stage_bytes = kWarps * row_bytes;
+    const int stages = rope_bulk_stages(a, kWarps);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r0 = (int)((long long)blockIdx.x * rows / gridDim.x);
+    const int r1 = (int)((long long)(blockIdx.x + 1) * rows / gridDim.x);
+    const int groups = (r1 - r0 + kWarps - 1) / kWarps;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == kWarps) {  // producer
+        if (lane != 0) return;
+        int issued = 0;
+        for (int g = 0; g < groups; ++g) {
+            const int s = g % stages;
+            if (g >= stages && !mbar_wait(&empty[s], ((g / stages) - 1) & 1)) break;
+            const int row = r0 + g * kWarps;
+            const int n = min(kWarps, r1 - row);
+            mbar_expect_tx(&full[s], (uint32_t)(n * row_bytes));
+            for (int i = 0; i < n; ++i)
+                bulk_load(ring + (size_t)s * stage_bytes + i * row_bytes,
+                          a.qkv + (size_t)(row + i) * a.row_stride, (uint32_t)row_bytes, &full[s]);
+            ++issued;
+        }
+        for (int g = max(0, issued - stages); g < issued; ++g)
+            mbar_wait(&full[g % stages], (g / stages) & 1);
+        return;
+    }
+    const int j = lane % CPR;
+    const int n_heads = a.n_q + a.n_kv;
+    for (int g = 0; g < groups; ++g) {
+        const int s = g % stages;
+        const int row = r0 + g * kWarps + warp;
+        // row metadata and cos/sin first: their loads overlap the wait for the copy
+        bool ok = row < r1;
+        int seq = 0, p = 0;
+        float c[8], sn[8];
+        size_t kv0 = 0, hs = 0;
+        if (ok) {
+            seq = row / a.rows_per_seq;
+            p = (a.pos_arr ? a.pos_arr[seq] : a.pos0) + row % a.rows_per_seq;
+            if (p < 0 || p >= a.max_pos || (a.do_append && p >= a.max_seq)) {
+                if (lane == 0) raise_dev_error(kDevErrBadPosition);
+                ok = false;
+            }
+        }
+        if (ok) {
+            const float4* c4 = reinterpret_cast<const float4*>(a.cos_t + (size_t)p * half + 8 * j);
+            const float4* s4 = reinterpret_cast<const float4*>(a.sin_t + (size_t)p * half + 8 * j);
+            const float4 c0 = c4[0], c1 = c4[1], s0 = s4[0], s1 = s4[1];
+            c[0] = c0.x; c[1] = c0.y; c[2] = c0.z; c[3] = c0.w;
+            c[4] = c1.x; c[5] = c1.y; c[6] = c1.z; c[7] = c1.w;
+            sn[0] = s0.x; sn[1] = s0.y; sn[2] = s0.z; sn[3] = s0.w;
+            sn[4] = s1.x; sn[5] = s1.y; sn[6] = s1.z; sn[7] = s1.w;
+            if (a.do_append && !rope_cache_base(a, seq, p, kv0, hs, lane == 0)) ok = false;
+        }
+        if (!mbar_wait(&full[s], (g / stages) & 1)) return;
+        if (ok) {
+            const uint16_t* src =
+                reinterpret_cast<const uint16_t*>(ring + (size_t)s * stage_bytes + warp * row_bytes);
+            uint16_t* rowp = a.qkv + (size_t)row * a.row_stride;
+            for (int h0 = lane / CPR; h0 < n_heads; h0 += kBatch * kHeadStep) {
+                uint4 va[kBatch], vb[kBatch];
+#pragma unroll
+                for (int k = 0; k < kBatch; ++k) {
+                    const int h = h0 + k * kHeadStep;
+                    if (h < n_heads) {
+                        va[k] = *reinterpret_cast<const uint4*>(src + h * 2 * half + 8 * j);
+                        vb[k] = *reinterpret_cast<const uint4*>(src + h * 2 * half + 8 * j + half);
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < kBatch; ++k) {
+                    const int h = h0 + k * kHeadStep;
+                    if (h < n_heads) {
+                        float x0[8], x1[8], ra[8], rb[8];
+                        unpack8<T>(va[k], x0);
+                        unpack8<T>(vb[k], x1);
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            ra[e] = rot_a(x0[e], x1[e], c[e], sn[e]);
+                            rb[e] = rot_b(x0[e], x1[e], c[e], sn[e]);
+                        }
+                        const uint4 oa = pack8<T>(ra), ob = pack8<T>(rb);
+                        *reinterpret_cast<uint4*>(rowp + h * 2 * half + 8 * j) = oa;
+                        *reinterpret_cast<uint4*>(rowp + h * 2 * half + 8 * j + half) = ob;
+                        if (a.do_append && h >= a.n_q) {
+                            const size_t dst = kv0 + (size_t)(h - a.n_q) * hs;
+                            *reinterpret_cast<uint4*>(a.kc + dst + 8 * j) = oa;
+                            *reinterpret_cast<uint4*>(a.kc + dst + 8 * j + half) = ob;
+                        }
+                    }
+                }
+            }
+            if (a.do_append) {  // raw v heads into the cache, 16 bytes per lane per step
+                constexpr int per = (2 * half) >> 3;
+                const uint16_t* vrow = src + (size_t)n_heads * 2 * half;
+                for (int vi = lane; vi < a.n_kv * per; vi += 32) {
+                    const int kvh = vi / per, cc = vi - kvh * per;
+                    const uint4 v = *reinterpret_cast<const uint4*>(vrow + kvh * 2 * half + 8 * cc);
+                    *reinterpret_cast<uint4*>(a.vc + kv0 + (size_t)kvh * hs + 8 * cc) = v;
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
     }
 }
 

@@ -317,6 +317,34 @@ def test_rope_kv_append_prefill_equals_per_sequence(g, n_seq, t, pos0, max_seq):
         np.testing.assert_array_equal(host_bits(vc_a)[i * per:(i + 1) * per], wv)
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("n_q,n_kv", [(16, 4), (32, 8), (64, 8)])
+def test_rope_kv_append_prefill_head_dim_128(g, dtype, n_q, n_kv):
+    """hd 128 (eight 8-pair chunks per head), 3 x 500 rows: the persistent bulk-copy
+    kernel's wide-head form, in both 16-bit formats; rows of 6, 12 and 20 KB take
+    16, 8 and 4 rows per ring stage."""
+    rng = np.random.default_rng(23)
+    hd, n_seq, t, pos0, max_seq = 128, 3, 500, 6, 512
+    stride = (n_q + 2 * n_kv) * hd
+    qkv = O.uniform16(rng, n_seq * t * stride, 2.0, dtype)
+    cos, sin = O.cos_sin_table(hd, max_seq, **O.LLAMA3_ROPE)
+    per = n_kv * max_seq * hd
+    a = dev(qkv, dtype)
+    kc = torch.zeros(n_seq * per, dtype=a.dtype, device="cuda")
+    vc = torch.zeros_like(kc)
+    g.rope_kv_append_prefill(a, torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda(), kc, vc,
+                             n_seq, t, pos0, n_q, n_kv, hd, max_seq)
+    assert g.device_error() == 0
+    z = np.zeros(per, np.uint16)
+    for i in range(n_seq):
+        rows = qkv[i * t * stride:(i + 1) * t * stride]
+        rot = O.from_f32(O.rope(rows, cos, sin, t, pos0, n_q, n_kv, hd, dtype), dtype)
+        np.testing.assert_array_equal(host_bits(a)[i * t * stride:(i + 1) * t * stride], rot)
+        wk, wv = O.kv_append(rot, z, z, t, pos0, n_q, n_kv, hd, max_seq)
+        np.testing.assert_array_equal(host_bits(kc)[i * per:(i + 1) * per], wk)
+        np.testing.assert_array_equal(host_bits(vc)[i * per:(i + 1) * per], wv)
+
+
 def test_rope_batched_rejects_position_outside_cache(g):
     """A position beyond the cache is skipped and flagged, never written."""
     n_q, n_kv, hd, max_seq = 4, 2, 64, 8

@@ -159,6 +159,43 @@ def test_paged_bad_block_entry_is_flagged_not_fatal(g):
     assert float(x[0]) == 2.0
 
 
+def test_paged_prefill_append_bad_block_entry(g):
+    """Prefill-sized append (2 x 640 rows, the bulk-copy kernel) with one table entry
+    outside the pool: code 4 is raised, that block's rows are not written, and every
+    other row lands exactly where the contiguous append puts it."""
+    rng = np.random.default_rng(31)
+    n_seq, t, max_seq, bs = 2, 640, 640, 64
+    max_blocks = max_seq // bs
+    stride = (N_Q + 2 * N_KV) * HD
+    qkv = normal16(rng, n_seq * t * stride)
+    cos, sin = O.cos_sin_table(HD, max_seq, **O.LLAMA3_ROPE)
+    c, s = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    n_blocks = n_seq * max_blocks
+    table = np.random.default_rng(6).permutation(n_blocks).astype(np.int32).reshape(n_seq, max_blocks)
+    bad_seq, bad_lb = 1, 3
+    table[bad_seq, bad_lb] = n_blocks + 7
+    kpool = torch.zeros(n_blocks * N_KV * bs * HD, dtype=torch.bfloat16, device="cuda")
+    vpool = torch.zeros_like(kpool)
+    g.device_error()  # clear
+    g.rope_kv_append_paged(dev(qkv), n_seq, t, torch.zeros(n_seq, dtype=torch.int32, device="cuda"),
+                           c, s, kpool, vpool, torch.from_numpy(table).cuda(), max_blocks, bs, N_Q,
+                           N_KV, HD)
+    assert g.device_error() & 4
+    per = N_KV * max_seq * HD
+    kc = torch.zeros(n_seq * per, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    g.rope_kv_append_prefill(dev(qkv), c, s, kc, vc, n_seq, t, 0, N_Q, N_KV, HD, max_seq)
+    for pool, cont in ((kpool, kc), (vpool, vc)):
+        p = host_bits(pool).reshape(n_blocks, N_KV, bs, HD)
+        want = host_bits(cont).reshape(n_seq, N_KV, max_blocks, bs, HD)
+        for b in range(n_seq):
+            for lb in range(max_blocks):
+                if (b, lb) != (bad_seq, bad_lb):
+                    np.testing.assert_array_equal(p[table[b, lb]], want[b, :, lb])
+        used = set(int(x) for x in table.ravel())
+        assert not any(p[blk].any() for blk in range(n_blocks) if blk not in used)
+
+
 @pytest.mark.parametrize("n_seq,t,pos0,bs", [(2, 300, 17, 32), (1, 129, 0, 64), (3, 200, 100, 128),
                                              (1, 7, 90, 32)])
 def test_paged_prefill_equals_contiguous(g, n_seq, t, pos0, bs):
