@@ -347,18 +347,44 @@ def cfg3(args):
     O.attention(sub, kb, vb, T, 0, 4, 1, hd, T)
     cpu_s = (time.perf_counter() - t0) * (n_seq * nkv)
     O.set_threads(1)
+    lib_ref = _library_prefill_reference(n_seq, T, nq, nkv, hd, flops, flush)
     _emit({"workload": "cfg3: prefill 4 x 2048, causal GQA attention 32/8 heads hd 64 (tcgen05)",
            "metric": "TFLOP/s", "value": tflops, "unit": "TFLOP/s", "us": ms_att * 1e3,
            "flops": flops, "frac_of_peak": tflops / peaks["bf16_tflops"],
            "peak": f"{peaks['bf16_tflops']} TFLOP/s ({kind}, burst)",
            "cpu_oracle_s_scaled": cpu_s, "cpu_sample": "1 of 32 (sequence, kv head) groups, x32",
-           "cpu_threads": _cpu_threads()})
+           "cpu_threads": _cpu_threads(), "library_reference": lib_ref})
     tflops_p = flops / (ms_att_p * 1e-3) / 1e12
     _emit({"workload": "cfg3 paged: the same prefill attention over a shuffled pool of 64-key blocks",
            "metric": "TFLOP/s", "value": tflops_p, "unit": "TFLOP/s", "us": ms_att_p * 1e3,
            "flops": flops, "frac_of_peak": tflops_p / peaks["bf16_tflops"],
            "peak": f"{peaks['bf16_tflops']} TFLOP/s ({kind}, burst)",
            "equal_to_contiguous": paged_equal})
+
+
+def _library_prefill_reference(n_seq, T, nq, nkv, hd, flops, flush):
+    """torch SDPA with the cuDNN backend on the same shapes (causal, bf16), timed the
+    same way: what NVIDIA's own attention reaches on this GPU at head_dim 64.  A
+    comparison only; nothing of this library runs through it.  K and V are expanded
+    to the query heads (cuDNN's GQA support varies by version)."""
+    import torch.nn.functional as F
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        gen = torch.Generator(device="cuda").manual_seed(5)
+        q = torch.randn(n_seq, nq, T, hd, generator=gen, device="cuda").to(torch.bfloat16)
+        k = torch.randn(n_seq, nkv, T, hd, generator=gen, device="cuda").to(torch.bfloat16)
+        v = torch.randn(n_seq, nkv, T, hd, generator=gen, device="cuda").to(torch.bfloat16)
+        k = k.repeat_interleave(nq // nkv, dim=1).contiguous()
+        v = v.repeat_interleave(nq // nkv, dim=1).contiguous()
+        with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+            f = lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True)
+            for _ in range(3):
+                f()
+            ms = time_each(f, 30, flush)
+        return {"impl": "torch SDPA, cuDNN backend (K/V expanded to 32 heads)",
+                "tflops": flops / (ms * 1e-3) / 1e12, "us": ms * 1e3}
+    except Exception as e:  # a torch build without the backend
+        return {"impl": "torch SDPA, cuDNN backend", "unavailable": str(e).splitlines()[0][:200]}
 
 
 # ----------------------------------------------------------------------------- config 4
