@@ -36,7 +36,11 @@ enum kvb_status {
     KVB_ERR_SHAPE = 1,       /* a size or length check failed; nothing launched */
     KVB_ERR_CUDA = 2,        /* a CUDA runtime / driver / cuBLAS call failed */
     KVB_ERR_UNSUPPORTED = 3, /* valid request this build does not implement */
-    KVB_ERR_DEVICE = 4       /* a kernel reported a device-side error (kvb_device_error) */
+    KVB_ERR_DEVICE = 4,      /* a kernel reported a device-side error (kvb_device_error) */
+    KVB_ERR_CONFIG = 5,      /* checkpoint content: missing tensor, bad header, bad values
+                                (reference KvasirError::Config, engine/src/error.rs) */
+    KVB_ERR_IO = 6           /* a checkpoint file could not be opened or mapped
+                                (reference KvasirError::Io) */
 };
 
 enum kvb_dtype { KVB_BF16 = 0, KVB_F16 = 1 };
@@ -333,6 +337,54 @@ int kvb_decoder_step_host(kvb_decoder_t dec, kvb_stream_t stream, const int32_t*
                           int32_t* ids_host_out);
 /* Number of kernels (own + cuBLAS) one step launches. */
 int kvb_decoder_launches_per_step(kvb_decoder_t dec, int* own, int* library);
+/* Untied checkpoints (reference Weights::head, engine/src/model/weights.rs:29-32):
+ * the LM head [vocab, hidden] used instead of the embedding table.  NULL goes
+ * back to the tied head.  The next step re-records its graph. */
+int kvb_decoder_set_lm_head(kvb_decoder_t dec, const void* lm_head);
+
+/* ---------------------------------------------------------------------------
+ * Weight load path (reference Weights::load, engine/src/model/weights.rs:47-230):
+ * every *.safetensors file of a directory is memory-mapped (sorted by name; a
+ * tensor name in a later file replaces an earlier one, as the reference's map
+ * insertion does) and its header parsed.  kvb_checkpoint_load_rows copies named
+ * tensors, concatenated by rows (the reference's fused w_qkv rows q|k|v and
+ * w_gu rows gate|up, Loader::load_into), into a caller-owned device buffer in
+ * the compute type:
+ *   BF16 -> BF16, F16 -> F16: copied as they are (F16 checked finite);
+ *   BF16 -> F16: on the device by kvb_bf16_to_f16, values that are not finite
+ *                or outside the FP16 range counted in *bad (device u32), as
+ *                the reference's Loader::convert_to;
+ *   F16 -> BF16, F32 -> BF16, F32 -> F16: rounded to nearest even on the host;
+ *                a non-finite result is KVB_ERR_CONFIG (reference check_finite).
+ * Host staging is pinned and double-buffered; copies run on `stream`, and the
+ * call returns once every source byte has been staged (the last copies may
+ * still be in flight on the stream).  The loader allocates its own staging
+ * (pinned host, and device memory for BF16 -> F16); nothing else.
+ * ------------------------------------------------------------------------- */
+typedef struct kvb_checkpoint_s* kvb_checkpoint_t;
+
+enum kvb_ckpt_dtype { KVB_CKPT_BF16 = 0, KVB_CKPT_F16 = 1, KVB_CKPT_F32 = 2, KVB_CKPT_OTHER = 3 };
+
+/* Maps and indexes every *.safetensors file of dir.  KVB_ERR_CONFIG if there is
+ * none or a header is malformed, KVB_ERR_IO if a file cannot be read. */
+int kvb_checkpoint_open(kvb_checkpoint_t* out, const char* dir);
+/* Waits for the loader's copies still in flight, then unmaps and frees. */
+int kvb_checkpoint_close(kvb_checkpoint_t ck);
+/* Number of distinct tensor names. */
+size_t kvb_checkpoint_num_tensors(kvb_checkpoint_t ck);
+/* dtype (kvb_ckpt_dtype), rank and up to 8 dims of a tensor; KVB_ERR_CONFIG if
+ * the name is missing. */
+int kvb_checkpoint_tensor(kvb_checkpoint_t ck, const char* name, int* dtype, int* ndim,
+                          uint64_t* dims);
+/* Copies n_parts tensors into dst (dst_len elements of dst_dtype): part i must
+ * have shape [rows[i], cols], or [cols] when rows[i] == 0 (a vector, counted as
+ * one row).  Errors: a missing name or unsupported dtype is KVB_ERR_CONFIG, a
+ * shape other than the expected one KVB_ERR_SHAPE ("<name>: shape [..],
+ * expected [..]"), dst_len other than the parts' total KVB_ERR_SHAPE.  `bad`
+ * (device, one u32) is required when a BF16 part goes to F16. */
+int kvb_checkpoint_load_rows(kvb_checkpoint_t ck, kvb_stream_t stream, const char* const* names,
+                             const uint64_t* rows, size_t n_parts, uint64_t cols, void* dst,
+                             size_t dst_len, int dst_dtype, uint32_t* bad);
 
 /* ---------------------------------------------------------------------------
  * Self test of the bounded-wait machinery: launches one CTA that waits on an

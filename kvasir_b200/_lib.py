@@ -14,8 +14,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_lib", "libkvasir_b200.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "kvasir_b200.h")
 
-KVB_OK, KVB_ERR_SHAPE, KVB_ERR_CUDA, KVB_ERR_UNSUPPORTED, KVB_ERR_DEVICE = range(5)
+(KVB_OK, KVB_ERR_SHAPE, KVB_ERR_CUDA, KVB_ERR_UNSUPPORTED, KVB_ERR_DEVICE, KVB_ERR_CONFIG,
+ KVB_ERR_IO) = range(7)
 KVB_BF16, KVB_F16 = 0, 1
+KVB_CKPT_BF16, KVB_CKPT_F16, KVB_CKPT_F32, KVB_CKPT_OTHER = range(4)
 
 _sz = C.c_size_t
 _p = C.c_void_p
@@ -91,6 +93,14 @@ SIGNATURES = {
     "kvb_decoder_step": (_int, [_p, _p]),
     "kvb_decoder_step_host": (_int, [_p, _p, _p, _p]),
     "kvb_decoder_launches_per_step": (_int, [_p, C.POINTER(_int), C.POINTER(_int)]),
+    "kvb_decoder_set_lm_head": (_int, [_p, _p]),
+    "kvb_checkpoint_open": (_int, [C.POINTER(_p), C.c_char_p]),
+    "kvb_checkpoint_close": (_int, [_p]),
+    "kvb_checkpoint_num_tensors": (_sz, [_p]),
+    "kvb_checkpoint_tensor": (_int, [_p, C.c_char_p, C.POINTER(_int), C.POINTER(_int),
+                                     C.POINTER(C.c_uint64)]),
+    "kvb_checkpoint_load_rows": (_int, [_p, _p, C.POINTER(C.c_char_p), C.POINTER(C.c_uint64), _sz,
+                                        C.c_uint64, _p, _sz, _int, _p]),
     "kvb_selftest_wait_timeout": (_int, [_p, C.c_uint32]),
 }
 

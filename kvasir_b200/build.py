@@ -20,7 +20,7 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 LIBDIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(LIBDIR, "libkvasir_b200.so")
-SOURCES = ["kvb_api.cu", "kvb_blas.cpp", "kvb_decoder.cpp"]
+SOURCES = ["kvb_api.cu", "kvb_blas.cpp", "kvb_decoder.cpp", "kvb_checkpoint.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

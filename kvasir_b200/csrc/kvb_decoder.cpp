@@ -69,6 +69,7 @@ struct kvb_decoder_s {
     Layout lay;
     uint8_t* ws = nullptr;
     const void* embed = nullptr;
+    const void* lm_head = nullptr;  // untied checkpoints; nullptr: the embedding table
     const void* final_norm = nullptr;
     std::vector<const void*> attn_norm, w_qkv, w_o, mlp_norm, w_gu, w_down;
     uint8_t* kc = nullptr;
@@ -167,8 +168,9 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
                              B, H, c.eps, dt),
              false);
     }
-    STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->embed, (size_t)c.vocab * H,
-                    d->at<float>(L.logits), B * (size_t)c.vocab, B, H, (size_t)c.vocab, dt, 1),
+    STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->lm_head ? d->lm_head : d->embed,
+                    (size_t)c.vocab * H, d->at<float>(L.logits), B * (size_t)c.vocab, B, H,
+                    (size_t)c.vocab, dt, 1),
          true);
     STEP(kvb_argmax_f32(s, d->at<float>(L.logits), B, (size_t)c.vocab, d->at<int32_t>(L.ids_out),
                         d->at<int32_t>(L.pos), d->at<int32_t>(L.lens)),
@@ -253,6 +255,18 @@ int kvb_decoder_destroy(kvb_decoder_t d) {
     return KVB_OK;
 }
 
+// The captured step holds the old pointers: the next step records a new graph.
+static void drop_graph(kvb_decoder_t d) {
+    if (d->exec) {
+        cudaGraphExecDestroy(d->exec);
+        d->exec = nullptr;
+    }
+    if (d->graph) {
+        cudaGraphDestroy(d->graph);
+        d->graph = nullptr;
+    }
+}
+
 int kvb_decoder_use_paged_cache(kvb_decoder_t d, void* k_pools, void* v_pools, size_t pool_len,
                                 const int32_t* block_table, size_t max_blocks, size_t block_size) {
     KVB_CHECK(d && k_pools && v_pools && block_table, "decoder_use_paged_cache: null argument");
@@ -273,14 +287,14 @@ int kvb_decoder_use_paged_cache(kvb_decoder_t d, void* k_pools, void* v_pools, s
     d->block_table = block_table;
     d->max_blocks = max_blocks;
     d->block_size = block_size;
-    if (d->exec) {  // the next step records the paged step
-        cudaGraphExecDestroy(d->exec);
-        d->exec = nullptr;
-    }
-    if (d->graph) {
-        cudaGraphDestroy(d->graph);
-        d->graph = nullptr;
-    }
+    drop_graph(d);  // the next step records the paged step
+    return KVB_OK;
+}
+
+int kvb_decoder_set_lm_head(kvb_decoder_t d, const void* lm_head) {
+    KVB_CHECK(d, "decoder_set_lm_head: null decoder");
+    d->lm_head = lm_head;
+    drop_graph(d);
     return KVB_OK;
 }
 

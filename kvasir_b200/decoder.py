@@ -54,6 +54,8 @@ def random_weights(cfg: LlamaConfig, device, dtype=torch.bfloat16, seed: int = 0
 class Decoder:
     """Greedy decoding of n_seq sequences with KV capacity max_seq each.
 
+    weights: the dict of random_weights or kvasir_b200.weights.load_weights
+    ("lm_head" present for untied checkpoints).
     kc / vc: [n_layers, n_seq, n_kv, max_seq, head_dim], or with paged_block_size
     the block pools [n_layers, n_blocks, n_kv, paged_block_size, head_dim] that
     self.block_table ([n_seq, max_blocks], one table for all layers) indexes."""
@@ -111,6 +113,8 @@ class Decoder:
             esz = torch.tensor([], dtype=dt).element_size()
             return self.workspace[off:off + n * esz].view(dt)
 
+        if "lm_head" in self.w:  # untied checkpoint (kvasir_b200.weights.load_weights)
+            check(lib.kvb_decoder_set_lm_head(h, self.w["lm_head"].data_ptr()))
         if paged_block_size:
             self.use_paged_cache(self.kc, self.vc, self.block_table, max_blocks, paged_block_size)
         self.ids_in = view(lib.kvb_decoder_ids_in(h), n_seq, torch.int32)

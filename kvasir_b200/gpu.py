@@ -38,8 +38,18 @@ class DeviceError(KvasirError):
     pass
 
 
+class CheckpointError(KvasirError):
+    """Checkpoint content (reference KvasirError::Config): a missing tensor, a
+    malformed header, an unsupported dtype, values outside the target range."""
+
+
+class CheckpointIoError(KvasirError):
+    """A checkpoint file could not be opened or mapped (reference KvasirError::Io)."""
+
+
 _ERRORS = {L.KVB_ERR_SHAPE: ShapeError, L.KVB_ERR_CUDA: CudaError,
-           L.KVB_ERR_UNSUPPORTED: UnsupportedError, L.KVB_ERR_DEVICE: DeviceError}
+           L.KVB_ERR_UNSUPPORTED: UnsupportedError, L.KVB_ERR_DEVICE: DeviceError,
+           L.KVB_ERR_CONFIG: CheckpointError, L.KVB_ERR_IO: CheckpointIoError}
 
 
 def check(status: int) -> None:
