@@ -272,6 +272,24 @@ int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, 
 int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
                    int32_t* ids, int32_t* advance, int32_t* advance2);
 
+/* Temperature / top-p sampling on the device (the reference plans it on the
+ * host over copied logits: kvasir DESIGN.md:24,109, "greedy / temperature /
+ * top-p", seeded).  Per row: integer weights w_i = floor(2^32 * exp((l_i -
+ * max l) / temperature)) (0 for NaN and -inf; a +inf logit takes the row, as
+ * in the argmax); the kept set is every token whose logit is at least the
+ * largest value K* with  sum_{l_j >= K*} w_j >= ceil(top_p * sum_j w_j)  (ties
+ * at K* kept; top_p >= 1 keeps all); u24 = the top 24 bits of SplitMix64(seed +
+ * SplitMix64(counter << 32 | row)) with counter = counters[row] (0 if counters
+ * is NULL); ids[row] = the first index whose running kept weight, in
+ * vocabulary order, exceeds floor(u24 * (kept weight) / 2^24).  All sums are
+ * exact: the same seed, counter and logits give the same id.  temperature <= 0
+ * is kvb_argmax_f32.  vocab at most 327680.  advance / advance2 as for
+ * kvb_argmax_f32 (they may be the counters array: each row reads its counter
+ * before advancing it).  One 8-CTA cluster per row. */
+int kvb_sample_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
+                   float temperature, float top_p, uint64_t seed, const int32_t* counters,
+                   int32_t* ids, int32_t* advance, int32_t* advance2);
+
 /* ---------------------------------------------------------------------------
  * Decode-step driver: the reference's planned Llama forward pass
  * (reference DESIGN.md:36-74, engine/src/model/weights.rs:13-27 for the
@@ -337,6 +355,11 @@ int kvb_decoder_step_host(kvb_decoder_t dec, kvb_stream_t stream, const int32_t*
                           int32_t* ids_host_out);
 /* Number of kernels (own + cuBLAS) one step launches. */
 int kvb_decoder_launches_per_step(kvb_decoder_t dec, int* own, int* library);
+/* Sampling of the step: temperature <= 0 is greedy (the default); otherwise
+ * kvb_sample_f32 with the given top_p and seed, each sequence's counter being
+ * its position, so every step draws afresh and a rerun from the same state
+ * repeats.  The next step re-records its graph. */
+int kvb_decoder_set_sampling(kvb_decoder_t dec, float temperature, float top_p, uint64_t seed);
 /* Untied checkpoints (reference Weights::head, engine/src/model/weights.rs:29-32):
  * the LM head [vocab, hidden] used instead of the embedding table.  NULL goes
  * back to the tied head.  The next step re-records its graph. */

@@ -94,6 +94,8 @@ SIGNATURES = {
     "kvb_decoder_step_host": (_int, [_p, _p, _p, _p]),
     "kvb_decoder_launches_per_step": (_int, [_p, C.POINTER(_int), C.POINTER(_int)]),
     "kvb_decoder_set_lm_head": (_int, [_p, _p]),
+    "kvb_decoder_set_sampling": (_int, [_p, C.c_float, C.c_float, C.c_uint64]),
+    "kvb_sample_f32": (_int, [_p, _p, _sz, _sz, C.c_float, C.c_float, C.c_uint64, _p, _p, _p, _p]),
     "kvb_checkpoint_open": (_int, [C.POINTER(_p), C.c_char_p]),
     "kvb_checkpoint_close": (_int, [_p]),
     "kvb_checkpoint_num_tensors": (_sz, [_p]),

@@ -424,6 +424,34 @@ def cfg4(args):
                "metric": "tokens/s", "value": tps, "unit": "tokens/s", "ms_per_step": ms / steps,
                "bytes_per_step": step_bytes, "hbm_roofline_tokens_s": roof_tps,
                "frac_of_roofline": tps / roof_tps, "peak": f"{peaks['hbm_gbs']} GB/s ({kind})"})
+        # the same steps with device-side temperature / top-p sampling in place of argmax,
+        # and the two sampling kernels alone on this step's logits
+        dec.set_sampling(0.8, 0.95, seed=1)
+        dec.set_lengths(ctx)
+        for _ in range(3):
+            dec.step()
+        dec.set_lengths(ctx)
+        torch.cuda.synchronize()
+        a.record(s)
+        for _ in range(steps):
+            dec.step()
+        b.record(s)
+        b.synchronize()
+        ms_s = a.elapsed_time(b)
+        g = Gpu(0)
+        ids = torch.empty(B, dtype=torch.int32, device="cuda")
+        lg = dec.logits.reshape(-1)
+        us = {}
+        for name, fn in (("argmax", lambda: g.argmax(lg, B, cfg.vocab_size, ids)),
+                         ("sample", lambda: g.sample(lg, B, cfg.vocab_size, ids, 0.8, 0.95, 1))):
+            for _ in range(3):
+                fn()
+            us[name] = time_loop(fn, 50) * 1e3
+        _emit({"workload": f"cfg4: 16-layer decode, batch {B}, context 1024, 256 steps sampled "
+                           f"on the device (temperature 0.8, top-p 0.95)",
+               "metric": "tokens/s", "value": B * steps / (ms_s * 1e-3), "unit": "tokens/s",
+               "ms_per_step": ms_s / steps, "greedy_ms_per_step": ms / steps,
+               "kernel_us": {"argmax": us["argmax"], "top_p_sample": us["sample"]}})
         dec.close()
         del dec
         torch.cuda.empty_cache()

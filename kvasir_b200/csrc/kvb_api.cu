@@ -19,6 +19,7 @@
 #include "kvb_host.h"
 #include "norm.cuh"
 #include "rope.cuh"
+#include "sample.cuh"
 
 namespace kvb {
 
@@ -1185,6 +1186,29 @@ int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t
     const int vec4 = vocab % 4 == 0 && aligned(logits, 16);
     argmax_kernel<<<(unsigned)rows, 512, 0, stream>>>(logits, (int)vocab, ids, advance, advance2, vec4);
     KVB_CHECK_LAUNCH("argmax launch");
+    return KVB_OK;
+}
+
+int kvb_sample_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
+                   float temperature, float top_p, uint64_t seed, const int32_t* counters,
+                   int32_t* ids, int32_t* advance, int32_t* advance2) {
+    KVB_CHECK(vocab > 0 && vocab <= (size_t)kSampleCluster * kSampleMaxSlice,
+              "sample: vocab %zu out of range (1 .. %d)", vocab, kSampleCluster * kSampleMaxSlice);
+    KVB_CHECK(fits_i32(rows), "sample: rows %zu out of range", rows);
+    KVB_CHECK(!(temperature != temperature) && !(top_p != top_p),
+              "sample: temperature and top_p must be numbers");
+    if (rows == 0) return KVB_OK;
+    if (temperature <= 0.f)  // greedy
+        return kvb_argmax_f32(stream, logits, rows, vocab, ids, advance, advance2);
+    KVB_CHECK(rows <= 0x7fffffff / kSampleCluster, "sample: rows %zu out of range", rows);
+    const int vec4 = vocab % 4 == 0 && aligned(logits, 16);
+    // each CTA of a row's cluster stages its slice of the row in shared memory
+    const size_t slice = ((vocab + kSampleCluster - 1) / kSampleCluster + 3) & ~(size_t)3;
+    set_max_smem(sample_kernel, kSampleStageMax);
+    sample_kernel<<<(unsigned)(rows * kSampleCluster), kSampleThreads, slice * 4, stream>>>(
+        logits, (int)vocab, 1.0f / temperature, top_p, seed, counters, ids, advance, advance2,
+        vec4);
+    KVB_CHECK_LAUNCH("sample launch");
     return KVB_OK;
 }
 

@@ -70,6 +70,9 @@ struct kvb_decoder_s {
     uint8_t* ws = nullptr;
     const void* embed = nullptr;
     const void* lm_head = nullptr;  // untied checkpoints; nullptr: the embedding table
+    float temperature = 0.f;        // <= 0: greedy
+    float top_p = 1.f;
+    uint64_t seed = 0;
     const void* final_norm = nullptr;
     std::vector<const void*> attn_norm, w_qkv, w_o, mlp_norm, w_gu, w_down;
     uint8_t* kc = nullptr;
@@ -172,7 +175,9 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
                     (size_t)c.vocab * H, d->at<float>(L.logits), B * (size_t)c.vocab, B, H,
                     (size_t)c.vocab, dt, 1),
          true);
-    STEP(kvb_argmax_f32(s, d->at<float>(L.logits), B, (size_t)c.vocab, d->at<int32_t>(L.ids_out),
+    // sampling reads each sequence's position as its counter, then advances it
+    STEP(kvb_sample_f32(s, d->at<float>(L.logits), B, (size_t)c.vocab, d->temperature, d->top_p,
+                        d->seed, d->at<int32_t>(L.pos), d->at<int32_t>(L.ids_out),
                         d->at<int32_t>(L.pos), d->at<int32_t>(L.lens)),
          false);
     cudaError_t e = cudaMemcpyAsync(d->at(L.ids_in), d->at(L.ids_out), B * 4,
@@ -288,6 +293,17 @@ int kvb_decoder_use_paged_cache(kvb_decoder_t d, void* k_pools, void* v_pools, s
     d->max_blocks = max_blocks;
     d->block_size = block_size;
     drop_graph(d);  // the next step records the paged step
+    return KVB_OK;
+}
+
+int kvb_decoder_set_sampling(kvb_decoder_t d, float temperature, float top_p, uint64_t seed) {
+    KVB_CHECK(d, "decoder_set_sampling: null decoder");
+    KVB_CHECK(temperature == temperature && top_p == top_p,
+              "decoder_set_sampling: temperature and top_p must be numbers");
+    d->temperature = temperature;
+    d->top_p = top_p;
+    d->seed = seed;
+    drop_graph(d);
     return KVB_OK;
 }
 

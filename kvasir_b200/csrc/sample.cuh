@@ -1,0 +1,468 @@
+// sample.cuh -- temperature / top-p (nucleus) sampling over f32 logits, one
+// 8-CTA thread-block cluster per row, entirely on the device.
+//
+// The reference plans this on the host over the copied logits
+// (DESIGN.md:24,109 of kvasir: "greedy / temperature / top-p", seeded so that
+// the same seed and logits give the same token).  Here only the sampled id
+// leaves the GPU.  Definitions (restated by the CPU oracle):
+//   w_i   = floor(2^32 * expf((l_i - max l) * inv_temp)), an integer; 0 for NaN /
+//           -inf logits (a row holding +inf samples its first +inf, as the argmax);
+//   key_i = the logit's bits mapped to an unsigned order (monotone in l_i);
+//   K*    = the largest key with  sum_{key_j >= K*} w_j >= ceil(top_p * sum_j w_j)
+//           (every token tied at K* is kept: the nucleus without sorting);
+//   u24   = the top 24 bits of SplitMix64(seed + SplitMix64(counter << 32 | row));
+//   id    = the first index i, in vocabulary order, whose running sum of kept
+//           weights exceeds floor(u24 * sum_kept w / 2^24).
+// All sums are exact integers, so the id depends only on the weights.
+// K* is found by a mass-weighted radix select over the keys (11, 11 and 10
+// bits: three passes that histogram w by digit in shared memory), so no
+// sort is needed.  temperature <= 0 is greedy (the argmax kernel).
+//
+// Layout on the GPU: the row's vocabulary is cut into 8 contiguous slices, one
+// per CTA of a cluster, so a row streams through 8 SMs; each CTA reads its
+// slice from HBM / L2 once into shared memory and runs every pass from there.  Every cluster-wide
+// quantity (max, normaliser, digit histograms, kept mass per slice) is a
+// per-CTA partial in shared memory that each CTA reads from all 8 through
+// distributed shared memory and sums in rank order: every CTA derives the same
+// K* and draw, and the CTA whose slice holds the drawn token writes it.
+#pragma once
+
+#include "kvb_common.cuh"
+
+namespace kvb {
+
+constexpr int kSampleThreads = 512;
+constexpr int kSampleWarps = kSampleThreads / 32;
+constexpr int kSampleCluster = 8;
+constexpr int kSampleMaxSlice = 40960;          // tokens per CTA: vocabularies up to 327680
+constexpr int kSampleStageMax = kSampleMaxSlice * 4;
+
+// SplitMix64 (G. Steele, D. Lea, C. Flood, "Fast splittable pseudorandom number
+// generators", OOPSLA 2014): the finaliser of a Weyl sequence.
+__host__ __device__ inline uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+__host__ __device__ inline float sample_uniform(uint64_t seed, uint32_t row, uint32_t counter) {
+    const uint64_t z = splitmix64(seed + splitmix64(((uint64_t)counter << 32) | row));
+    return (float)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+__device__ __forceinline__ uint32_t order_key(float x) {
+    const uint32_t b = __float_as_uint(x);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float sample_weight(float x, float m, float inv_temp) {
+    return (x > -INFINITY) ? expf((x - m) * inv_temp) : 0.f;  // NaN and -inf weigh nothing
+}
+
+__device__ __forceinline__ float block_max_f(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    v = lane < kSampleWarps ? red[lane] : -INFINITY;
+    return warp_max(v);
+}
+__device__ __forceinline__ float block_sum_f(float v, float* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    v = lane < kSampleWarps ? red[lane] : 0.f;
+    return warp_sum(v);
+}
+
+// Distributed shared memory: the same variable in CTA `rank` of this cluster.
+template <typename T>
+__device__ __forceinline__ T dsmem_ld(const T* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(remote)
+                 : "r"((uint32_t)__cvta_generic_to_shared(local)), "r"(rank));
+    T v;
+    static_assert(sizeof(T) == 4, "32-bit values only");
+    uint32_t u;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(u) : "r"(remote));
+    memcpy(&v, &u, 4);
+    return v;
+}
+// Cluster-wide barrier with release / acquire semantics for shared memory.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+                 ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Weights in 32-bit fixed point (w <= 1): every histogram, mass and running
+// sum below is an exact integer, independent of the order the GPU adds in.
+// Histograms hold the high and low 16 bits of the weights in two u32 arrays
+// (native shared-memory atomics; a slice of <= 40960 tokens cannot overflow).
+constexpr float kFixScale = 4294967296.0f;  // 2^32
+__device__ __forceinline__ uint64_t fixed_weight(float x, float m, float inv_temp) {
+    return (uint64_t)(sample_weight(x, m, inv_temp) * kFixScale);
+}
+__device__ __forceinline__ uint64_t warp_sum_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ uint64_t block_sum_u64(uint64_t v, uint64_t* red64) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum_u64(v);
+    __syncthreads();
+    if (lane == 0) red64[warp] = v;
+    __syncthreads();
+    v = lane < kSampleWarps ? red64[lane] : 0ull;
+    return warp_sum_u64(v);
+}
+__device__ __forceinline__ uint64_t dsmem_ld64(const uint64_t* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(remote)
+                 : "r"((uint32_t)__cvta_generic_to_shared(local)), "r"(rank));
+    uint64_t v;
+    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(remote));
+    return v;
+}
+
+__device__ __forceinline__ void hist_add(uint32_t* hist_hi, uint32_t* hist_lo, int bucket,
+                                         uint64_t w) {
+    atomicAdd(&hist_hi[bucket], (uint32_t)(w >> 16));
+    atomicAdd(&hist_lo[bucket], (uint32_t)(w & 0xFFFFu));
+}
+
+__global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSampleThreads)
+    sample_kernel(const float* __restrict__ logits, int vocab, float inv_temp, float top_p,
+                  uint64_t seed, const int32_t* __restrict__ counters, int32_t* __restrict__ ids,
+                  int32_t* __restrict__ adv, int32_t* __restrict__ adv2, int vec4) {
+    extern __shared__ float4 slice_smem[];  // this CTA's slice of the row
+    __shared__ float red[kSampleWarps];
+    __shared__ uint64_t red64[kSampleWarps];
+    __shared__ uint32_t hist_hi[2048], hist_lo[2048];  // this CTA's digit histogram (read by
+                                                      // the cluster): high / low 16 bits
+    __shared__ float part_m;                   // this CTA's max (read by the cluster)
+    __shared__ uint64_t part_z, part_kept;     // its normaliser and kept mass (read by the cluster)
+    __shared__ int part_i;                     // its first +inf index
+    __shared__ uint64_t wmass[kSampleWarps];
+    __shared__ float s_m;
+    __shared__ uint64_t s_total, s_above, s_t, s_base;
+    __shared__ uint32_t s_digit;
+    __shared__ int s_owner, s_warp, s_cross, s_low;
+    const uint32_t rank = cluster_rank();
+    const int row = blockIdx.x / kSampleCluster;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* l = logits + (size_t)row * vocab;
+    const uint32_t counter = counters ? (uint32_t)counters[row] : 0u;
+    // this CTA's slice, a multiple of 4 elements long
+    const int slice = ((vocab + kSampleCluster - 1) / kSampleCluster + 3) & ~3;
+    const int v0 = min(vocab, (int)rank * slice), v1 = min(vocab, v0 + slice);
+    const float4* l4 = reinterpret_cast<const float4*>(l);
+    const float* sl = reinterpret_cast<const float*>(slice_smem);
+    // element i / float4 q of the row, from this CTA's staged slice
+    auto at = [&](int i) -> float { return sl[i - v0]; };
+    auto at4 = [&](int q) -> float4 { return slice_smem[q - v0 / 4]; };
+    // visits every element of the slice
+    auto for_slice = [&](auto&& f) {
+        if (vec4) {
+            for (int q = v0 / 4 + tid; q < v1 / 4; q += kSampleThreads) {
+                const float4 x = at4(q);
+                f(4 * q, x.x);
+                f(4 * q + 1, x.y);
+                f(4 * q + 2, x.z);
+                f(4 * q + 3, x.w);
+            }
+        } else {
+            for (int i = v0 + tid; i < v1; i += kSampleThreads) f(i, at(i));
+        }
+    };
+
+    // ---- the slice into shared memory (4 independent loads in flight per thread)
+    // and the max over the row
+    float m = -INFINITY;
+    {
+        float* dst = reinterpret_cast<float*>(slice_smem);
+        if (vec4) {
+            const int q0 = v0 / 4, q1 = v1 / 4;
+            for (int q = q0 + tid; q < q1; q += 4 * kSampleThreads) {
+                float4 x[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (q + k * kSampleThreads < q1) x[k] = l4[q + k * kSampleThreads];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (q + k * kSampleThreads < q1) {
+                        slice_smem[q + k * kSampleThreads - q0] = x[k];
+                        m = fmaxf(fmaxf(m, fmaxf(x[k].x, x[k].y)), fmaxf(x[k].z, x[k].w));
+                    }
+            }
+        } else {
+            for (int i = v0 + tid; i < v1; i += kSampleThreads) {
+                const float x = l[i];
+                dst[i - v0] = x;
+                m = fmaxf(m, x);
+            }
+        }
+    }
+    __syncthreads();  // the slice is in shared memory
+    m = block_max_f(m, red);
+    if (tid == 0) part_m = m;
+    cluster_sync();
+    if (tid == 0) {
+        float mm = -INFINITY;
+        for (uint32_t r = 0; r < kSampleCluster; ++r) mm = fmaxf(mm, dsmem_ld(&part_m, r));
+        s_m = mm;
+        part_i = 0x7fffffff;
+    }
+    __syncthreads();
+    m = s_m;
+    int chosen = -1;  // set by the one thread that writes the id
+    if (m == INFINITY) {  // all the mass sits on +inf: the first such index, as the argmax
+        for_slice([&](int i, float x) {
+            if (x == INFINITY) atomicMin(&part_i, i);
+        });
+        cluster_sync();
+        if (rank == 0 && tid == 0) {
+            int first = 0x7fffffff;
+            for (uint32_t r = 0; r < kSampleCluster; ++r) first = min(first, dsmem_ld(&part_i, r));
+            chosen = first;
+        }
+    } else if (m == -INFINITY) {  // nothing but NaN / -inf: index 0, as the argmax
+        if (rank == 0 && tid == 0) chosen = 0;
+    } else {
+        // ---- normaliser and the first digit histogram in one pass
+        const bool nucleus = top_p < 1.f;
+        for (int b = tid; b < 2048; b += kSampleThreads) hist_hi[b] = hist_lo[b] = 0u;
+        __syncthreads();
+        uint64_t z = 0;
+        for_slice([&](int, float x) {
+            const uint64_t w = fixed_weight(x, m, inv_temp);
+            z += w;
+            if (nucleus && w) hist_add(hist_hi, hist_lo, (int)(order_key(x) >> 21), w);
+        });
+        z = block_sum_u64(z, red64);
+        if (tid == 0) part_z = z;
+        cluster_sync();  // partials and histograms of pass 0 complete everywhere
+        if (tid == 0) {
+            uint64_t zz = 0;
+            for (uint32_t r = 0; r < kSampleCluster; ++r) zz += dsmem_ld64(&part_z, r);
+            s_total = zz;
+        }
+        __syncthreads();
+        const uint64_t total = s_total;
+        uint32_t kstar = 0;
+        if (nucleus) {
+            // the nucleus needs at least this much fixed-point mass
+            const uint64_t target = (uint64_t)ceil((double)top_p * (double)total);
+            uint64_t above = 0;
+            uint32_t prefix = 0;
+            for (int pass = 0; pass < 3; ++pass) {
+                const int bits = pass < 2 ? 11 : 10;
+                const int shift = pass == 0 ? 21 : pass == 1 ? 10 : 0;
+                const int nb = 1 << bits;
+                if (pass > 0) {
+                    for (int b = tid; b < 2048; b += kSampleThreads) hist_hi[b] = hist_lo[b] = 0u;
+                    __syncthreads();
+                    for_slice([&](int, float x) {
+                        const uint32_t k = order_key(x);
+                        if ((k >> (shift + bits)) != prefix) return;
+                        const uint64_t w = fixed_weight(x, m, inv_temp);
+                        if (w) hist_add(hist_hi, hist_lo, (int)((k >> shift) & (uint32_t)(nb - 1)), w);
+                    });
+                    cluster_sync();  // every CTA's histogram of this pass is complete
+                }
+                // thread t owns the bucket run [t*per, (t+1)*per) of the cluster's
+                // histogram; higher threads hold higher keys
+                const int per = nb / kSampleThreads;  // 4 or 2
+                uint64_t hb[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (k < per) {
+                        uint32_t vh[kSampleCluster], vl[kSampleCluster];
+#pragma unroll
+                        for (uint32_t r = 0; r < kSampleCluster; ++r) {
+                            vh[r] = dsmem_ld(&hist_hi[tid * per + k], r);
+                            vl[r] = dsmem_ld(&hist_lo[tid * per + k], r);
+                        }
+#pragma unroll
+                        for (uint32_t r = 0; r < kSampleCluster; ++r)
+                            hb[k] += ((uint64_t)vh[r] << 16) + vl[r];
+                    }
+                uint64_t own = 0;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) own += hb[k];
+                // mass of the runs above this thread's: a suffix scan over the block
+                uint64_t inc = own;  // inclusive suffix within the warp (lanes above)
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint64_t y = __shfl_down_sync(0xffffffffu, inc, o);
+                    if (lane + o < 32) inc += y;
+                }
+                if (lane == 0) red64[warp] = inc;  // the warp's total
+                __syncthreads();
+                uint64_t above_warps = 0;
+                for (int w = warp + 1; w < kSampleWarps; ++w) above_warps += red64[w];
+                const uint64_t ex = above + above_warps + (inc - own);  // everything above my run
+                const bool reach = own > 0 && ex + own >= target;
+                // the crossing run: the highest one whose cumulative mass reaches the target;
+                // if every run falls short (weights truncated to 0), keep the whole prefix
+                // down to its lowest nonempty bucket
+                if (tid == 0) {
+                    s_cross = -1;
+                    s_low = 0x7fffffff;
+                }
+                __syncthreads();
+                if (reach) atomicMax(&s_cross, tid);
+                if (own > 0) atomicMin(&s_low, tid);
+                __syncthreads();
+                const int cross = s_cross >= 0 ? s_cross : (s_low != 0x7fffffff ? s_low : -1);
+                if (cross < 0 && tid == 0) {  // no mass under the prefix: nothing to refine
+                    s_digit = 0;
+                    s_above = above;
+                }
+                if (tid == cross) {
+                    uint64_t acc = ex;
+                    int d = tid * per;
+                    if (s_cross >= 0) {
+                        for (int k = per - 1; k >= 0; --k) {
+                            if (hb[k] > 0 && acc + hb[k] >= target) {
+                                d = tid * per + k;
+                                break;
+                            }
+                            acc += hb[k];
+                        }
+                    } else {
+                        int lo = per - 1;
+                        for (int k = 0; k < per; ++k)
+                            if (hb[k] > 0) {
+                                lo = k;
+                                break;
+                            }
+                        for (int k = per - 1; k > lo; --k) acc += hb[k];
+                        d = tid * per + lo;
+                    }
+                    s_digit = (uint32_t)d;
+                    s_above = acc;
+                }
+                cluster_sync();  // the cluster has read every histogram of this pass
+                prefix = (prefix << bits) | s_digit;
+                above = s_above;
+            }
+            kstar = prefix;
+        }
+        // ---- the draw: kept mass per warp segment of this slice, then per CTA
+        const int seg = (v1 - v0 + kSampleWarps - 1) / kSampleWarps;
+        const int s0 = min(v1, v0 + warp * seg), s1 = min(v1, s0 + seg);
+        uint64_t ws = 0;
+        for (int i = s0 + lane; i < s1; i += 32) {
+            const float x = at(i);
+            if (order_key(x) >= kstar) ws += fixed_weight(x, m, inv_temp);
+        }
+        ws = warp_sum_u64(ws);
+        if (lane == 0) wmass[warp] = ws;
+        __syncthreads();
+        if (tid == 0) {
+            uint64_t cm = 0;
+            for (int w = 0; w < kSampleWarps; ++w) cm += wmass[w];
+            part_kept = cm;
+        }
+        cluster_sync();
+        if (tid == 0) {
+            uint64_t pm[kSampleCluster], sum = 0;
+            for (uint32_t r = 0; r < kSampleCluster; ++r) {
+                pm[r] = dsmem_ld64(&part_kept, r);
+                sum += pm[r];
+            }
+            // t = floor(u24 * kept / 2^24), in 128-bit integer arithmetic
+            const uint64_t u24 =
+                (uint64_t)(sample_uniform(seed, (uint32_t)row, counter) * 16777216.0f);
+            const uint64_t t = (__umul64hi(sum, u24) << 40) | ((sum * u24) >> 24);
+            int owner = -1, last = -1;
+            uint64_t base = 0, base_last = 0, acc = 0;
+            for (int r = 0; r < kSampleCluster; ++r) {
+                if (pm[r] > 0) {
+                    last = r;
+                    base_last = acc;
+                    if (owner < 0 && acc + pm[r] > t) {
+                        owner = r;
+                        base = acc;
+                    }
+                }
+                acc += pm[r];
+            }
+            if (owner < 0) {  // cannot happen with exact sums; kept for safety
+                owner = last;
+                base = base_last;
+            }
+            s_owner = owner;
+            s_t = t;
+            if (owner == (int)rank) {  // the warp of this slice that holds the draw
+                int wsel = -1, wlast = -1;
+                uint64_t wb = base, wb_last = base, a2 = base;
+                for (int w = 0; w < kSampleWarps; ++w) {
+                    if (wmass[w] > 0) {
+                        wlast = w;
+                        wb_last = a2;
+                        if (wsel < 0 && a2 + wmass[w] > t) {
+                            wsel = w;
+                            wb = a2;
+                        }
+                    }
+                    a2 += wmass[w];
+                }
+                if (wsel < 0) {
+                    wsel = wlast;
+                    wb = wb_last;
+                }
+                s_warp = wsel;
+                s_base = wb;
+            }
+        }
+        __syncthreads();
+        if (s_owner == (int)rank && warp == s_warp) {
+            const uint64_t t = s_t;
+            uint64_t base = s_base;
+            int last = -1, found = -1;
+            for (int c = s0; c < s1; c += 32) {
+                const int i = c + lane;
+                uint64_t w = 0;
+                if (i < s1) {
+                    const float x = at(i);
+                    if (order_key(x) >= kstar) w = fixed_weight(x, m, inv_temp);
+                }
+                uint64_t inc = w;  // inclusive scan over the 32 lanes, in index order
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint64_t y = __shfl_up_sync(0xffffffffu, inc, o);
+                    if (lane >= o) inc += y;
+                }
+                const uint32_t hit = __ballot_sync(0xffffffffu, w > 0 && base + inc > t);
+                const uint32_t pos = __ballot_sync(0xffffffffu, w > 0);
+                if (pos) last = c + 31 - __clz(pos);
+                if (hit) {
+                    found = c + __ffs(hit) - 1;
+                    break;
+                }
+                base += __shfl_sync(0xffffffffu, inc, 31);
+            }
+            if (lane == 0) chosen = found >= 0 ? found : last;
+        }
+    }
+    if (chosen >= 0) ids[row] = chosen;
+    cluster_sync();  // no CTA leaves while another may still read its shared memory,
+                     // and every CTA has read the row's counter
+    if (rank == 0 && tid == 0) {
+        if (adv) adv[row] += 1;
+        if (adv2) adv2[row] += 1;
+    }
+}
+
+}  // namespace kvb

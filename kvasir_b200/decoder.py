@@ -154,6 +154,12 @@ class Decoder:
                                                     v_pools.data_ptr(), k_pools[0].numel(),
                                                     block_table.data_ptr(), max_blocks, block_size))
 
+    def set_sampling(self, temperature: float, top_p: float = 1.0, seed: int = 0) -> None:
+        """Temperature / top-p sampling for the following steps (kvb_decoder_set_sampling);
+        temperature <= 0 goes back to greedy."""
+        check(self._lib.kvb_decoder_set_sampling(self._h, temperature, top_p,
+                                                 seed & 0xFFFFFFFFFFFFFFFF))
+
     def set_lengths(self, cur_len) -> None:
         """Tokens already in each sequence's cache; the next step writes there."""
         arr = np.ascontiguousarray(np.broadcast_to(np.asarray(cur_len, np.int32), (self.n_seq,)))

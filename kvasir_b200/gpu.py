@@ -284,6 +284,20 @@ class Gpu:
         check(self._lib.kvb_argmax_f32(self._s, _ptr(logits), rows, vocab, _ptr(ids),
                                        _ptr(advance), _ptr(advance2)))
 
+    def sample(self, logits, rows, vocab, ids, temperature, top_p=1.0, seed=0, counters=None,
+               advance=None, advance2=None):
+        """kvb_sample_f32: temperature / top-p sampling, one id per row (temperature
+        <= 0 is the argmax).  counters: int32 per row (None: 0)."""
+        if logits.dtype != torch.float32 or ids.dtype != torch.int32:
+            raise ShapeError("sample: f32 logits and int32 ids expected")
+        if logits.numel() != rows * vocab or ids.numel() != rows:
+            raise ShapeError("sample: bad sizes")
+        if counters is not None and (counters.dtype != torch.int32 or counters.numel() != rows):
+            raise ShapeError("sample: counters must be int32, one per row")
+        check(self._lib.kvb_sample_f32(self._s, _ptr(logits), rows, vocab, temperature, top_p,
+                                       seed & 0xFFFFFFFFFFFFFFFF, _ptr(counters), _ptr(ids),
+                                       _ptr(advance), _ptr(advance2)))
+
     def selftest_wait_timeout(self, limit_ms: int) -> int:
         """Runs the bounded-wait self test; returns the status code."""
         return int(self._lib.kvb_selftest_wait_timeout(self._s, limit_ms))

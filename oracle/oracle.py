@@ -207,6 +207,80 @@ def argmax(logits, rows, vocab):
     return out
 
 
+_M64 = (1 << 64) - 1
+
+
+def splitmix64(z: int) -> int:
+    """SplitMix64 (Steele, Lea, Flood, OOPSLA 2014) on Python integers mod 2^64."""
+    z = (z + 0x9E3779B97F4A7C15) & _M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return z ^ (z >> 31)
+
+
+def sample_uniform(seed: int, row: int, counter: int) -> float:
+    """24 random bits in [0, 1): the draw of kvb_sample_f32 for (seed, row, counter)."""
+    z = splitmix64((seed + splitmix64(((counter & 0xFFFFFFFF) << 32) | row)) & _M64)
+    return (z >> 40) / 16777216.0
+
+
+def order_keys(l32: np.ndarray) -> np.ndarray:
+    """The sampler's unsigned order of f32 values (monotone; -0.0 below +0.0)."""
+    b = np.ascontiguousarray(l32, np.float32).view(np.uint32)
+    return np.where(b & 0x80000000, ~b, b | 0x80000000).astype(np.uint32)
+
+
+def sample(logits, temperature, top_p, seed, counters=None, target_scale=1.0, u_shift=0):
+    """Restatement of kvb_sample_f32 (temperature > 0): per row the integer weights
+    w = floor(2^32 * f32(exp((l - max) * (1/temperature)))) (difference and scaling
+    in f32, as the kernel), the nucleus threshold K* over the order keys (ties
+    kept), u24 from sample_uniform and the first index, in vocabulary order, whose
+    running kept weight exceeds floor(u24 * kept / 2^24).  Sums are exact Python
+    integers.  target_scale / u_shift (in units of 2^-24) perturb the nucleus
+    target and the draw, so a test can tell a boundary case decided by the
+    device's expf from an error.  The planned host sampler this stands for is in
+    kvasir DESIGN.md:24,109."""
+    logits = np.asarray(logits, np.float32)
+    rows = logits.shape[0]
+    inv = np.float32(1.0) / np.float32(temperature)
+    out = np.zeros(rows, np.int32)
+    for r in range(rows):
+        l = logits[r]
+        valid = l > -np.inf  # False for NaN
+        if not valid.any():
+            continue
+        m = l[valid].max()
+        if m == np.inf:  # the first +inf, as the argmax
+            out[r] = int(np.nonzero(l == np.inf)[0][0])
+            continue
+        d = ((l - m).astype(np.float32) * inv).astype(np.float32)
+        w32 = np.exp(d.astype(np.float64)).astype(np.float32)
+        w = np.where(valid, np.floor(w32.astype(np.float64) * 2.0 ** 32), 0.0).astype(np.uint64)
+        keys = order_keys(l)
+        total = int(w.sum(dtype=np.uint64))
+        if top_p < 1.0:
+            target = int(np.ceil(float(np.float32(top_p)) * float(total) * target_scale))
+            pos = w > 0
+            uk, inv_idx = np.unique(keys[pos], return_inverse=True)  # ascending keys
+            mass = np.zeros(uk.size, dtype=object)
+            np.add.at(mass, inv_idx, w[pos].astype(object))
+            cum = np.cumsum(mass[::-1])  # mass at or above each key, highest first
+            hit = np.nonzero(cum >= target)[0]
+            kstar = uk[::-1][hit[0]] if hit.size else uk[0]
+            kept = keys >= kstar
+        else:
+            kept = np.ones_like(valid)
+        wk = np.where(kept, w, np.uint64(0))
+        kept_total = int(wk.sum(dtype=np.uint64))
+        u = int(sample_uniform(seed, r, 0 if counters is None else int(counters[r])) * 16777216)
+        u = min(max(u + u_shift, 0), (1 << 24) - 1)
+        t = (kept_total * u) >> 24
+        c = np.cumsum(wk.astype(object))
+        idx = np.nonzero((c > t) & (wk > 0))[0]
+        out[r] = idx[0] if idx.size else np.nonzero(wk > 0)[0][-1]
+    return out
+
+
 LLAMA3_ROPE = dict(theta=500000.0, scaled=True, factor=32.0, low=1.0, high=4.0, orig=8192.0)
 
 

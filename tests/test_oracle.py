@@ -285,3 +285,37 @@ def test_decode_step_matches_numpy_restatement():
             np.testing.assert_allclose(logits[b], want, rtol=2e-3, atol=2e-3)
             np.testing.assert_array_equal(kc[b, :, :, p], O.from_f32(kc_np[b, :, :, p]))
         ids = out_ids
+
+
+# ------------------------------------------------------------------ sampling restatement
+def test_splitmix64_known_answers():
+    """The first outputs of SplitMix64 from state 0 (the generator's published
+    reference sequence): state advances by the golden gamma, output = mix(state)."""
+    gamma, m64 = 0x9E3779B97F4A7C15, (1 << 64) - 1
+    got = [O.splitmix64((i * gamma) & m64) for i in range(3)]
+    assert got == [0xE220A8397B1DCDAF, 0x6E789E6AA1B965F4, 0x06C45D188009454F]
+
+
+def test_sample_restatement_properties():
+    rng = np.random.default_rng(5)
+    logits = rng.normal(0, 2, (6, 500)).astype(np.float32)
+    # a nucleus of ~0 mass keeps only the top token: the argmax
+    np.testing.assert_array_equal(O.sample(logits, 1.0, 1e-9, 7), O.argmax(logits, 6, 500))
+    # same seed and counters: same ids; the draw depends on the counter
+    a = O.sample(logits, 0.8, 0.9, 11, counters=[1, 2, 3, 4, 5, 6])
+    np.testing.assert_array_equal(a, O.sample(logits, 0.8, 0.9, 11, counters=[1, 2, 3, 4, 5, 6]))
+    us = {O.sample_uniform(11, 0, c) for c in range(50)}
+    assert len(us) == 50 and all(0.0 <= u < 1.0 for u in us)
+    # ids stay inside the nucleus: the kept tokens' mass reaches top_p
+    l = logits[0]
+    w = np.exp((l - l.max()).astype(np.float64))
+    order = np.argsort(-l)
+    top = set(order[: int(np.searchsorted(np.cumsum(w[order]) / w.sum(), 0.5)) + 1].tolist())
+    ids = O.sample(np.repeat(logits[:1], 200, 0), 1.0, 0.5, 3)
+    assert set(ids.tolist()) <= top
+    # NaN and -inf never win; an all -inf row gives 0
+    bad = logits[:2].copy()
+    bad[0, ::2] = np.nan
+    bad[1, :] = -np.inf
+    ids = O.sample(bad, 1.0, 1.0, 1)
+    assert ids[0] % 2 == 1 and ids[1] == 0
