@@ -14,9 +14,12 @@
 //   id    = the first index i, in vocabulary order, whose running sum of kept
 //           weights exceeds floor(u24 * sum_kept w / 2^24).
 // All sums are exact integers, so the id depends only on the weights.
-// K* is found by a mass-weighted radix select over the keys (11, 11 and 10
-// bits: three passes that histogram w by digit in shared memory), so no
-// sort is needed.  temperature <= 0 is greedy (the argmax kernel).
+// K* is found by a mass-weighted select over the keys with no sort: a first
+// histogram of w by the log-scaled key distance below the row's maximum (exact
+// below 32, then 32 buckets per power of two, so logits that differ in their
+// low bits still spread over many buckets), then radix passes of up to 11 bits
+// over the chosen bucket's exact distance range, fed only by its tokens.
+// temperature <= 0 is greedy (the argmax kernel).
 //
 // Layout on the GPU: the row's vocabulary is cut into 8 contiguous slices, one
 // per CTA of a cluster, so a row streams through 8 SMs; each CTA reads its
@@ -134,6 +137,25 @@ __device__ __forceinline__ uint64_t dsmem_ld64(const uint64_t* local, uint32_t r
     return v;
 }
 
+// Log-linear bucket of a key distance below the row's maximum: exact below 32,
+// then 32 buckets per power of two (buckets 0 .. 895, increasing with d).
+__device__ __forceinline__ int log_bucket(uint32_t d) {
+    if (d < 32) return (int)d;
+    const int e = 31 - __clz(d);  // 5 .. 31
+    return 32 + (e - 5) * 32 + (int)((d >> (e - 5)) & 31u);
+}
+// The distances [lo, lo + 2^width_log2) of a bucket.
+__device__ __forceinline__ void log_bucket_range(int b, uint32_t& lo, int& width_log2) {
+    if (b < 32) {
+        lo = (uint32_t)b;
+        width_log2 = 0;
+        return;
+    }
+    const int e = 5 + (b - 32) / 32, f = (b - 32) % 32;
+    lo = (32u + (uint32_t)f) << (e - 5);
+    width_log2 = e - 5;
+}
+
 __device__ __forceinline__ void hist_add(uint32_t* hist_hi, uint32_t* hist_lo, int bucket,
                                          uint64_t w) {
     atomicAdd(&hist_hi[bucket], (uint32_t)(w >> 16));
@@ -242,11 +264,15 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
         const bool nucleus = top_p < 1.f;
         for (int b = tid; b < 2048; b += kSampleThreads) hist_hi[b] = hist_lo[b] = 0u;
         __syncthreads();
+        // first histogram: by log-scaled key distance below the maximum, which spreads
+        // tokens of nearly equal logits over many buckets; index 1023 - bucket, so that
+        // higher indices hold higher keys
+        const uint32_t kmax = order_key(m);
         uint64_t z = 0;
         for_slice([&](int, float x) {
             const uint64_t w = fixed_weight(x, m, inv_temp);
             z += w;
-            if (nucleus && w) hist_add(hist_hi, hist_lo, (int)(order_key(x) >> 21), w);
+            if (nucleus && w) hist_add(hist_hi, hist_lo, 1023 - log_bucket(kmax - order_key(x)), w);
         });
         z = block_sum_u64(z, red64);
         if (tid == 0) part_z = z;
@@ -262,30 +288,16 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
         if (nucleus) {
             // the nucleus needs at least this much fixed-point mass
             const uint64_t target = (uint64_t)ceil((double)top_p * (double)total);
-            uint64_t above = 0;
-            uint32_t prefix = 0;
-            for (int pass = 0; pass < 3; ++pass) {
-                const int bits = pass < 2 ? 11 : 10;
-                const int shift = pass == 0 ? 21 : pass == 1 ? 10 : 0;
-                const int nb = 1 << bits;
-                if (pass > 0) {
-                    for (int b = tid; b < 2048; b += kSampleThreads) hist_hi[b] = hist_lo[b] = 0u;
-                    __syncthreads();
-                    for_slice([&](int, float x) {
-                        const uint32_t k = order_key(x);
-                        if ((k >> (shift + bits)) != prefix) return;
-                        const uint64_t w = fixed_weight(x, m, inv_temp);
-                        if (w) hist_add(hist_hi, hist_lo, (int)((k >> shift) & (uint32_t)(nb - 1)), w);
-                    });
-                    cluster_sync();  // every CTA's histogram of this pass is complete
-                }
-                // thread t owns the bucket run [t*per, (t+1)*per) of the cluster's
-                // histogram; higher threads hold higher keys
-                const int per = nb / kSampleThreads;  // 4 or 2
+            // Finds, in the cluster's histogram of nb buckets (higher index = higher keys),
+            // the bucket where the mass counted from the top first reaches the target
+            // (above = mass of the keys above all of them); returns it and the mass above it.
+            // If every bucket falls short (weights truncated to 0) the lowest nonempty one.
+            auto select = [&](int nb, uint64_t above, uint32_t& digit, uint64_t& above_out) {
+                const int per = (nb + kSampleThreads - 1) / kSampleThreads;  // 1, 2 or 4
                 uint64_t hb[4] = {0, 0, 0, 0};
 #pragma unroll
                 for (int k = 0; k < 4; ++k)
-                    if (k < per) {
+                    if (k < per && tid * per + k < nb) {
                         uint32_t vh[kSampleCluster], vl[kSampleCluster];
 #pragma unroll
                         for (uint32_t r = 0; r < kSampleCluster; ++r) {
@@ -300,31 +312,26 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
 #pragma unroll
                 for (int k = 0; k < 4; ++k) own += hb[k];
                 // mass of the runs above this thread's: a suffix scan over the block
-                uint64_t inc = own;  // inclusive suffix within the warp (lanes above)
+                uint64_t inc = own;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
                     const uint64_t y = __shfl_down_sync(0xffffffffu, inc, o);
                     if (lane + o < 32) inc += y;
                 }
-                if (lane == 0) red64[warp] = inc;  // the warp's total
-                __syncthreads();
-                uint64_t above_warps = 0;
-                for (int w = warp + 1; w < kSampleWarps; ++w) above_warps += red64[w];
-                const uint64_t ex = above + above_warps + (inc - own);  // everything above my run
-                const bool reach = own > 0 && ex + own >= target;
-                // the crossing run: the highest one whose cumulative mass reaches the target;
-                // if every run falls short (weights truncated to 0), keep the whole prefix
-                // down to its lowest nonempty bucket
+                if (lane == 0) red64[warp] = inc;
                 if (tid == 0) {
                     s_cross = -1;
                     s_low = 0x7fffffff;
                 }
                 __syncthreads();
-                if (reach) atomicMax(&s_cross, tid);
+                uint64_t above_warps = 0;
+                for (int w = warp + 1; w < kSampleWarps; ++w) above_warps += red64[w];
+                const uint64_t ex = above + above_warps + (inc - own);  // above my run
+                if (own > 0 && ex + own >= target) atomicMax(&s_cross, tid);
                 if (own > 0) atomicMin(&s_low, tid);
                 __syncthreads();
                 const int cross = s_cross >= 0 ? s_cross : (s_low != 0x7fffffff ? s_low : -1);
-                if (cross < 0 && tid == 0) {  // no mass under the prefix: nothing to refine
+                if (cross < 0 && tid == 0) {  // no mass: nothing to refine
                     s_digit = 0;
                     s_above = above;
                 }
@@ -353,10 +360,39 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
                     s_above = acc;
                 }
                 cluster_sync();  // the cluster has read every histogram of this pass
-                prefix = (prefix << bits) | s_digit;
-                above = s_above;
+                digit = s_digit;
+                above_out = s_above;
+            };
+            uint32_t d0;
+            uint64_t above;
+            select(1024, 0, d0, above);
+            // the chosen bucket is the key distances [lo, lo + 2^nbits): refine over
+            // r = (lo + 2^nbits - 1) - distance, whose higher values are higher keys
+            uint32_t lo;
+            int nbits;
+            log_bucket_range(1023 - (int)d0, lo, nbits);
+            const uint64_t hi = (uint64_t)lo + (1ull << nbits);
+            uint32_t prefix = 0;
+            for (int done = 0; done < nbits;) {
+                const int bits = min(11, nbits - done);
+                const int shift = nbits - done - bits;
+                for (int b = tid; b < 2048; b += kSampleThreads) hist_hi[b] = hist_lo[b] = 0u;
+                __syncthreads();
+                for_slice([&](int, float x) {
+                    const uint32_t dist = kmax - order_key(x);
+                    if (dist < lo || (uint64_t)dist >= hi) return;
+                    const uint32_t r = (uint32_t)(hi - 1 - dist);
+                    if ((r >> (shift + bits)) != prefix) return;
+                    const uint64_t w = fixed_weight(x, m, inv_temp);
+                    if (w) hist_add(hist_hi, hist_lo, (int)((r >> shift) & ((1u << bits) - 1)), w);
+                });
+                cluster_sync();  // every CTA's histogram of this pass is complete
+                uint32_t digit;
+                select(1 << bits, above, digit, above);
+                prefix = (prefix << bits) | digit;
+                done += bits;
             }
-            kstar = prefix;
+            kstar = kmax - (uint32_t)(hi - 1 - prefix);
         }
         // ---- the draw: kept mass per warp segment of this slice, then per CTA
         const int seg = (v1 - v0 + kSampleWarps - 1) / kSampleWarps;
