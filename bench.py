@@ -409,13 +409,15 @@ def run_reference(args):
     cfg = LlamaConfig.llama_3_2_1b()
     threads = os.cpu_count() or 1
     steps = max(1, min(args.steps, 5))
-    sample = CpuDecodeSample(cfg, args.context, steps + 1, threads)
-    sample.step()  # warm-up
+    warmup = max(1, min(args.warmup, 3))  # each CPU step takes about a second
+    sample = CpuDecodeSample(cfg, args.context, steps + warmup, threads)
+    for _ in range(warmup):
+        sample.step()
     per_step = [sample.step() for _ in range(steps)]
     sec = statistics.mean(per_step)
     v = 1.0 / sec
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
-            "n_gpus": world, "steps": steps, "warmup": 1, "ms_per_step": sec * 1e3,
+            "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": sec * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic: seeded N(0,0.02) weights, N(0,1) KV",
             "config": {"workload": "cfg5: sequence-sharded long-context decode, Llama-3.2-1B "
