@@ -302,6 +302,9 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
 }
 
 // Folds the per-chunk partials of every (sequence, kv head) with more than one chunk.
+// Up to kCombineUnroll chunks are loaded in one go (all loads in flight at once);
+// more chunks take further rounds.
+constexpr int kCombineUnroll = 8;
 template <typename T>
 __global__ void __launch_bounds__(256) attn_combine_kernel(DecodeArgs a) {
     const int kvh = blockIdx.x, b = blockIdx.y;
@@ -313,14 +316,30 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(DecodeArgs a) {
     T* outb = reinterpret_cast<T*>(a.out) + (size_t)b * a.out_row_stride + (size_t)kvh * G * 64;
     for (int i = threadIdx.x; i < G * 64; i += blockDim.x) {
         const int r = i >> 6;
-        float M = -INFINITY;
-        for (int ch = 0; ch < n_chunks; ++ch) M = fmaxf(M, base[(size_t)ch * G * 66 + G * 64 + r]);
-        float L = 0.f, O = 0.f;
-        for (int ch = 0; ch < n_chunks; ++ch) {
-            const float* p = base + (size_t)ch * G * 66;
-            const float f = exp2f(p[G * 64 + r] - M);
-            L += p[G * 65 + r] * f;
-            O += p[i] * f;
+        float M = -INFINITY, L = 0.f, O = 0.f;
+        for (int c0 = 0; c0 < n_chunks; c0 += kCombineUnroll) {
+            float mv[kCombineUnroll], lv[kCombineUnroll], ov[kCombineUnroll];
+#pragma unroll
+            for (int k = 0; k < kCombineUnroll; ++k) {
+                const float* p = base + (size_t)(c0 + k) * G * 66;
+                const bool in = c0 + k < n_chunks;
+                mv[k] = in ? p[G * 64 + r] : -INFINITY;
+                lv[k] = in ? p[G * 65 + r] : 0.f;
+                ov[k] = in ? p[i] : 0.f;
+            }
+            float Mn = M;
+#pragma unroll
+            for (int k = 0; k < kCombineUnroll; ++k) Mn = fmaxf(Mn, mv[k]);
+            const float f0 = M == -INFINITY ? 0.f : exp2f(M - Mn);  // rescale what came before
+            L *= f0;
+            O *= f0;
+#pragma unroll
+            for (int k = 0; k < kCombineUnroll; ++k) {
+                const float f = mv[k] == -INFINITY ? 0.f : exp2f(mv[k] - Mn);
+                L += lv[k] * f;
+                O += ov[k] * f;
+            }
+            M = Mn;
         }
         outb[i] = Elem<T>::from_f(O / L);
     }
