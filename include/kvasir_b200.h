@@ -123,6 +123,15 @@ int kvb_linear(kvb_blas_t blas, kvb_stream_t stream, const void* x, size_t x_len
 /* Hands cuBLAS a caller-owned device workspace (cublasSetWorkspace) so that
  * GEMMs recorded into a CUDA graph never allocate. */
 int kvb_blas_set_workspace(kvb_blas_t blas, void* workspace, size_t workspace_len);
+/* Autotuned projections (off by default; the decode-step driver turns it on).
+ * Still cuBLAS GEMMs, same f32 accumulation: the first kvb_linear call of each
+ * (device, shape, dtype, output type, workspace size) outside stream capture
+ * times cublasGemmEx against the cuBLASLt algorithms the heuristic offers
+ * within the handle's workspace (split-K included, in-place atomic reductions
+ * excluded) and the fastest serves every later call of that shape in the
+ * process.  That first call overwrites y several times and synchronises the
+ * stream.  Inside a capture an untuned shape uses cublasGemmEx. */
+int kvb_blas_set_autotune(kvb_blas_t blas, int enable);
 
 /* Host-side RoPE table (engine/src/model/rope.rs:3-39): f64 inverse
  * frequencies with optional llama3 scaling, f32 cos/sin [max_pos, head_dim/2]

@@ -57,6 +57,7 @@ SIGNATURES = {
     "kvb_blas_create": (_int, [C.POINTER(_p)]),
     "kvb_blas_destroy": (_int, [_p]),
     "kvb_blas_set_workspace": (_int, [_p, _p, _sz]),
+    "kvb_blas_set_autotune": (_int, [_p, _int]),
     "kvb_linear": (_int, [_p, _p, _p, _sz, _p, _sz, _p, _sz, _sz, _sz, _sz, _int, _int]),
     "kvb_rope_table": (_int, [_sz, C.c_double, _int, C.c_double, C.c_double, C.c_double,
                               C.c_double, _sz, _p, _p]),

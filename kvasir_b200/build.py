@@ -67,7 +67,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
             subprocess.run(cmd, check=True)
     if force or _stale(LIB, objs):
         libdir = os.path.join(_cuda_home(nvcc), "lib64")
-        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lcublas",
+        cmd = [nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-lcublas", "-lcublasLt",
                "-Xlinker", f"-rpath,{libdir}"]
         if verbose:
             print(" ".join(cmd), flush=True)

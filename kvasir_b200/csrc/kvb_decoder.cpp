@@ -18,6 +18,7 @@
 #include "kvb_host.h"
 
 extern "C" int kvb_blas_set_workspace(kvb_blas_t b, void* ws, size_t len);
+extern "C" int kvb_blas_set_autotune(kvb_blas_t b, int enable);
 
 namespace {
 
@@ -231,6 +232,7 @@ int kvb_decoder_create(kvb_decoder_t* out, const kvb_decoder_config* cfg,
     d->sin_t = sin_t;
     int st = kvb_blas_create(&d->blas);
     if (st == KVB_OK) st = kvb_blas_set_workspace(d->blas, d->at(L.blas_ws), kBlasWorkspace);
+    if (st == KVB_OK) st = kvb_blas_set_autotune(d->blas, 1);
     if (st == KVB_OK) {
         cudaError_t e = cudaStreamCreateWithFlags(&d->capture_stream, cudaStreamNonBlocking);
         if (e != cudaSuccess) st = kvb::cuda_fail(e, "decoder_create: capture stream");
@@ -336,9 +338,41 @@ int32_t* kvb_decoder_ids_in(kvb_decoder_t d) { return d ? d->at<int32_t>(d->lay.
 int32_t* kvb_decoder_ids_out(kvb_decoder_t d) { return d ? d->at<int32_t>(d->lay.ids_out) : nullptr; }
 const float* kvb_decoder_logits(kvb_decoder_t d) { return d ? d->at<float>(d->lay.logits) : nullptr; }
 
+// Runs each projection shape of the step once, eagerly on `s`, so that the
+// autotuned GEMMs are chosen before the step is captured (a capture cannot time
+// anything).  Inputs and outputs are the step's own scratch buffers, all fully
+// rewritten by every step before they are read.
+static int tune_projections(kvb_decoder_s* d, kvb_stream_t s) {
+    const kvb_decoder_config& c = d->cfg;
+    const size_t B = (size_t)c.n_seq, H = (size_t)c.hidden, I = (size_t)c.inter;
+    const size_t qd = (size_t)c.n_q * c.head_dim, qkvd = qd + 2 * (size_t)c.n_kv * c.head_dim;
+    const size_t V = (size_t)c.vocab;
+    const int dt = c.dtype;
+    const Layout& L = d->lay;
+    int st = kvb_linear(d->blas, s, d->at(L.h), B * H, d->w_qkv[0], qkvd * H, d->at(L.qkv), B * qkvd,
+                        B, H, qkvd, dt, 0);
+    if (st == KVB_OK)
+        st = kvb_linear(d->blas, s, d->at(L.attn), B * qd, d->w_o[0], H * qd, d->at(L.o), B * H, B,
+                        qd, H, dt, 0);
+    if (st == KVB_OK)
+        st = kvb_linear(d->blas, s, d->at(L.h), B * H, d->w_gu[0], 2 * I * H, d->at(L.gu), B * 2 * I,
+                        B, H, 2 * I, dt, 0);
+    if (st == KVB_OK)
+        st = kvb_linear(d->blas, s, d->at(L.act), B * I, d->w_down[0], H * I, d->at(L.o), B * H, B,
+                        I, H, dt, 0);
+    if (st == KVB_OK)
+        st = kvb_linear(d->blas, s, d->at(L.h), B * H, d->lm_head ? d->lm_head : d->embed, V * H,
+                        d->at<float>(L.logits), B * V, B, H, V, dt, 1);
+    if (st != KVB_OK) return st;
+    const cudaError_t e = cudaStreamSynchronize(s);
+    return e == cudaSuccess ? KVB_OK : kvb::cuda_fail(e, "decoder: projection tuning");
+}
+
 int kvb_decoder_step(kvb_decoder_t d, kvb_stream_t s) {
     KVB_CHECK(d != nullptr, "decoder_step: null decoder");
     if (!d->exec) {
+        const int tst = tune_projections(d, s);
+        if (tst != KVB_OK) return tst;
         // Record the step once on the private capture stream (recording runs
         // nothing); host-side work (argument checks, tensor-map encoding)
         // happens only here, every step is then one graph launch on `s`.
