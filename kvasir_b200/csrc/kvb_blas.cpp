@@ -88,10 +88,10 @@ int tune_gemm(kvb_blas_s* b, cudaStream_t s, const void* x, const void* w, void*
     if (st == CUBLAS_STATUS_SUCCESS)
         st = cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_REDUCTION_SCHEME_MASK,
                                                   &schemes, sizeof schemes);
-    cublasLtMatmulHeuristicResult_t res[16];
+    cublasLtMatmulHeuristicResult_t res[32];
     int n = 0;
     if (st == CUBLAS_STATUS_SUCCESS)
-        st = cublasLtMatmulAlgoGetHeuristic(b->lt, g.op, g.a, g.b, g.c, g.c, pref, 16, res, &n);
+        st = cublasLtMatmulAlgoGetHeuristic(b->lt, g.op, g.a, g.b, g.c, g.c, pref, 32, res, &n);
     if (pref) cublasLtMatmulPreferenceDestroy(pref);
     if (st != CUBLAS_STATUS_SUCCESS) n = 0;  // no candidates: cublasGemmEx stays
 
@@ -112,18 +112,42 @@ int tune_gemm(kvb_blas_s* b, cudaStream_t s, const void* x, const void* w, void*
     };
     float best = time_it([&] { return gemm_ex(b, x, w, y, t, in_dim, out_dim, dtype, y_f32); });
     g.use_lt = false;
-    for (int i = 0; i < n; ++i) {
-        if (res[i].state != CUBLAS_STATUS_SUCCESS || res[i].workspaceSize > b->workspace_len)
-            continue;
+    auto try_algo = [&](const cublasLtMatmulAlgo_t& algo, size_t ws) {
         TunedGemm cand = g;
-        cand.algo = res[i].algo;
-        cand.ws = res[i].workspaceSize;
+        cand.algo = algo;
+        cand.ws = ws;
         const float ms = time_it([&] { return gemm_lt(b, cand, x, w, y, s); });
         if (ms > 0.f && (best < 0.f || ms < best)) {
             best = ms;
             g.use_lt = true;
-            g.algo = res[i].algo;
-            g.ws = res[i].workspaceSize;
+            g.algo = algo;
+            g.ws = ws;
+        }
+    };
+    for (int i = 0; i < n; ++i) {
+        if (res[i].state != CUBLAS_STATUS_SUCCESS || res[i].workspaceSize > b->workspace_len)
+            continue;
+        try_algo(res[i].algo, res[i].workspaceSize);
+        // the same tile configuration with the K dimension split 2 .. 32 ways, the
+        // partial products reduced in a separate pass (no atomics)
+        if (i < 8) {
+            for (int splitk : {2, 4, 8, 16, 32}) {
+                cublasLtMatmulAlgo_t a2 = res[i].algo;
+                const int32_t sk = splitk;
+                const uint32_t scheme = CUBLASLT_REDUCTION_SCHEME_COMPUTE_TYPE;
+                if (cublasLtMatmulAlgoConfigSetAttribute(&a2, CUBLASLT_ALGO_CONFIG_SPLITK_NUM, &sk,
+                                                         sizeof sk) != CUBLAS_STATUS_SUCCESS ||
+                    cublasLtMatmulAlgoConfigSetAttribute(&a2, CUBLASLT_ALGO_CONFIG_REDUCTION_SCHEME,
+                                                         &scheme, sizeof scheme) !=
+                        CUBLAS_STATUS_SUCCESS)
+                    continue;
+                cublasLtMatmulHeuristicResult_t chk;
+                if (cublasLtMatmulAlgoCheck(b->lt, g.op, g.a, g.b, g.c, g.c, &a2, &chk) !=
+                        CUBLAS_STATUS_SUCCESS ||
+                    chk.state != CUBLAS_STATUS_SUCCESS || chk.workspaceSize > b->workspace_len)
+                    continue;
+                try_algo(a2, chk.workspaceSize);
+            }
         }
     }
     cudaEventDestroy(e0);
