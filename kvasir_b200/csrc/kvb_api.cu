@@ -199,12 +199,16 @@ static int launch_rope(kvb_stream_t stream, const RopeArgs& a, int rows, int dty
 
 // ---------------------------------------------------------------- decode attention launcher
 // Keys per CTA: aim for ~8 waves of 3 resident CTAs per SM over the worst-case
-// work (every sequence at max_len), at least one 64-key tile per warp.
+// work (every sequence at max_len), at least one 64-key tile per warp -- four
+// per warp once the (sequence, kv head) pairs alone fill every SM, where short
+// chunks only add combine work (measured: batch 32 at context 1088 and config 2
+// gain 1-3 %; one sequence, 8 pairs, needs the smaller chunks' parallelism).
 static int decode_chunk_keys(size_t n_seq, size_t n_kv, size_t max_len) {
     const size_t tiles = (max_len + 63) / 64;
     const size_t target = (size_t)num_sms() * 3 * 8;
     size_t per_cta = (n_seq * n_kv * tiles + target - 1) / target;
-    if (per_cta < 4) per_cta = 4;
+    const size_t min_tiles = n_seq * n_kv >= (size_t)num_sms() ? 16 : 4;
+    if (per_cta < min_tiles) per_cta = min_tiles;
     per_cta = (per_cta + 3) / 4 * 4;
     if (per_cta > tiles) per_cta = (tiles + 3) / 4 * 4;
     return (int)(per_cta * 64);
