@@ -274,6 +274,24 @@ int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, 
                           size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
                           size_t head_dim, size_t max_seq, int dtype);
 
+/* Decode step of the attention block in one launch: kvb_rope_kv_append_batched
+ * followed by kvb_attention_decode, bit for bit, where the new token of
+ * sequence b sits at position lens[b] - 1 (the decode convention: it is the
+ * last key attended to).  qkv [n_seq, (n_q + 2 n_kv) * head_dim] stays
+ * unrotated (the q heads are rotated in registers); the rotated k and the v
+ * of each sequence are written to its cache row lens[b] - 1.  The reference
+ * runs rope_inplace, kv_append and attention (kernels.rs:124-371) as three
+ * launches.  head_dim 64, n_q/n_kv <= 16, contiguous caches, 16-byte aligned
+ * buffers; otherwise KVB_ERR_UNSUPPORTED.  Workspace as for
+ * kvb_attention_decode. */
+int kvb_rope_attention_decode(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                              const float* cos_t, const float* sin_t, size_t table_len, void* kc,
+                              void* vc, size_t seq_stride, size_t cache_len, const int32_t* lens,
+                              size_t n_seq, size_t max_len, size_t n_q, size_t n_kv,
+                              size_t head_dim, size_t max_seq, float scale, void* out,
+                              size_t out_row_stride, void* workspace, size_t workspace_len,
+                              int dtype);
+
 /* Greedy sampling: ids[r] = first index of the maximum of logits[r, 0:vocab)
  * (NaN never wins).  If advance is non-NULL, advance[r] += 1 for every r and,
  * if advance2 is non-NULL, advance2[r] += 1 (position / length counters of

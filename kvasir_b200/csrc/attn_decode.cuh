@@ -21,6 +21,7 @@
 #pragma once
 
 #include "kvb_ptx.cuh"
+#include "rope.cuh"
 
 namespace kvb {
 
@@ -47,6 +48,17 @@ struct DecodeArgs {
     // key k of sequence b lives in block block_table[b * max_blocks + k / block_size].
     const int32_t* block_table;
     int max_blocks, block_size, n_blocks;
+    // Fused RoPE + KV append (rope_cos != nullptr; kvb_rope_attention_decode): the new
+    // token of sequence b is key lens[b] - 1; q (a.q) and the new k, v are read
+    // unrotated from the sequence's qkv row, q is rotated in registers, and the CTA of
+    // the last chunk writes the rotated k and the v to that cache row before its tensor
+    // copies read it.
+    const float* rope_cos;
+    const float* rope_sin;
+    int rope_max_pos;
+    uint16_t* kc_w;
+    uint16_t* vc_w;
+    long long cache_seq_stride;  // elements between sequences' caches
 };
 
 // First row (of 64 elements) of the 64-key tile starting at key kt0 (a multiple of
@@ -77,7 +89,7 @@ __device__ __forceinline__ int decode_len(const DecodeArgs& a, int b) {
     return len;
 }
 
-template <typename T>
+template <typename T, bool kRope>
 __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                                                              const __grid_constant__ CUtensorMap vmap,
                                                              DecodeArgs a) {
@@ -102,6 +114,35 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     const int key_begin = chunk * a.chunk_keys;
     const int key_end = min(len, key_begin + a.chunk_keys);
 
+    int rope_p = -1;  // fused RoPE: the new token's position (-1: none, or out of range)
+    if (kRope) {
+        rope_p = len - 1;
+        if (rope_p >= a.rope_max_pos) {
+            if (threadIdx.x == 0) raise_dev_error(kDevErrBadPosition);
+            rope_p = -1;
+        }
+        if (rope_p >= 0 && chunk == n_chunks - 1) {  // this CTA reads the new key
+            const T* kin = reinterpret_cast<const T*>(a.q) + (size_t)b * a.q_row_stride +
+                           (size_t)(a.n_kv * G + kvh) * 64;
+            const T* vin = kin + (size_t)a.n_kv * 64;
+            const size_t row = (size_t)b * a.cache_seq_stride + ((size_t)kvh * a.max_seq + rope_p) * 64;
+            T* kout = reinterpret_cast<T*>(a.kc_w) + row;
+            T* vout = reinterpret_cast<T*>(a.vc_w) + row;
+            const int t = threadIdx.x;
+            if (t < 32) {
+                const float x0 = Elem<T>::to_f(kin[t]), x1 = Elem<T>::to_f(kin[t + 32]);
+                const float cs = a.rope_cos[(size_t)rope_p * 32 + t];
+                const float sn = a.rope_sin[(size_t)rope_p * 32 + t];
+                kout[t] = Elem<T>::from_f(rot_a(x0, x1, cs, sn));
+                kout[t + 32] = Elem<T>::from_f(rot_b(x0, x1, cs, sn));
+            } else if (t >= 64) {
+                vout[t - 64] = vin[t - 64];
+            }
+            // the tensor copies below read this row through the async proxy
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+        }
+    }
+
     if (threadIdx.x == 0) {
         for (int i = 0; i < kDecWarps; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
@@ -125,6 +166,22 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
             qa[s][1] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * 64 + d0) : 0u;
             qa[s][2] = g < G ? *reinterpret_cast<const uint32_t*>(qb + g * 64 + d0 + 8) : 0u;
             qa[s][3] = g + 8 < G ? *reinterpret_cast<const uint32_t*>(qb + (g + 8) * 64 + d0 + 8) : 0u;
+        }
+        if (kRope && rope_p >= 0) {
+            // rotate_half in registers: dims j (s = 0, 1) pair with j + 32 (s = 2, 3);
+            // the same f32 operations and one rounding as the RoPE kernels
+            const float* cr = a.rope_cos + (size_t)rope_p * 32;
+            const float* sr = a.rope_sin + (size_t)rope_p * 32;
+#pragma unroll
+            for (int s = 0; s < 2; ++s)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int j = 16 * s + 2 * c + (r >= 2 ? 8 : 0);
+                    const float2 lo = Elem<T>::unpack(qa[s][r]), hi = Elem<T>::unpack(qa[s + 2][r]);
+                    const float c0 = cr[j], c1 = cr[j + 1], s0 = sr[j], s1 = sr[j + 1];
+                    qa[s][r] = Elem<T>::pack(rot_a(lo.x, hi.x, c0, s0), rot_a(lo.y, hi.y, c1, s1));
+                    qa[s + 2][r] = Elem<T>::pack(rot_b(lo.x, hi.x, c0, s0), rot_b(lo.y, hi.y, c1, s1));
+                }
         }
     }
 

@@ -242,6 +242,10 @@ struct DecodeLaunch {
     // paged cache: pools [n_blocks][n_kv][block_size][64]; nullptr = contiguous
     const int32_t* block_table = nullptr;
     size_t max_blocks = 0, block_size = 0, n_blocks = 0;
+    // fused RoPE + KV append (kvb_rope_attention_decode); nullptr = none
+    const float* rope_cos = nullptr;
+    const float* rope_sin = nullptr;
+    size_t rope_max_pos = 0;
 };
 
 static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
@@ -271,6 +275,12 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
     a.max_blocks = (int)L.max_blocks;
     a.block_size = (int)L.block_size;
     a.n_blocks = (int)L.n_blocks;
+    a.rope_cos = L.rope_cos;
+    a.rope_sin = L.rope_sin;
+    a.rope_max_pos = (int)L.rope_max_pos;
+    a.kc_w = static_cast<uint16_t*>(const_cast<void*>(L.kc));
+    a.vc_w = static_cast<uint16_t*>(const_cast<void*>(L.vc));
+    a.cache_seq_stride = (long long)L.seq_stride;
     int ck = decode_chunk_keys(L.n_seq, L.n_kv, L.max_len);
     const size_t need = decode_ws_bytes(L.n_seq, L.max_len, L.n_q, L.n_kv);
     if (need == 0 || L.ws == nullptr || L.ws_len < need || !aligned(L.ws, 16)) {
@@ -285,13 +295,19 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
     if (a.max_chunks < 1) a.max_chunks = 1;
 
     dim3 grid(a.max_chunks, (unsigned)L.n_kv, (unsigned)L.n_seq);
+#define KVB_DECODE_LAUNCH(T, ROPE)                                                   \
+    do {                                                                             \
+        set_max_smem(attn_decode_kernel<T, ROPE>, kDecSmemBytes);                    \
+        attn_decode_kernel<T, ROPE><<<grid, 128, kDecSmemBytes, stream>>>(kmap, vmap, a); \
+    } while (0)
     if (L.dtype == KVB_BF16) {
-        set_max_smem(attn_decode_kernel<__nv_bfloat16>, kDecSmemBytes);
-        attn_decode_kernel<__nv_bfloat16><<<grid, 128, kDecSmemBytes, stream>>>(kmap, vmap, a);
+        if (L.rope_cos) KVB_DECODE_LAUNCH(__nv_bfloat16, true);
+        else KVB_DECODE_LAUNCH(__nv_bfloat16, false);
     } else {
-        set_max_smem(attn_decode_kernel<__half>, kDecSmemBytes);
-        attn_decode_kernel<__half><<<grid, 128, kDecSmemBytes, stream>>>(kmap, vmap, a);
+        if (L.rope_cos) KVB_DECODE_LAUNCH(__half, true);
+        else KVB_DECODE_LAUNCH(__half, false);
     }
+#undef KVB_DECODE_LAUNCH
     KVB_CHECK_LAUNCH("attention decode launch");
     if (a.max_chunks > 1) {
         dim3 g2((unsigned)L.n_kv, (unsigned)L.n_seq);
@@ -972,6 +988,71 @@ int kvb_attention_decode(kvb_stream_t stream, const void* q, size_t q_row_stride
     a.out = static_cast<uint16_t*>(out);
     a.out_row_stride = (long long)out_row_stride;
     return launch_generic_attn(stream, a, n_seq, dtype);
+}
+
+int kvb_rope_attention_decode(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                              const float* cos_t, const float* sin_t, size_t table_len, void* kc,
+                              void* vc, size_t seq_stride, size_t cache_len, const int32_t* lens,
+                              size_t n_seq, size_t max_len, size_t n_q, size_t n_kv,
+                              size_t head_dim, size_t max_seq, float scale, void* out,
+                              size_t out_row_stride, void* workspace, size_t workspace_len,
+                              int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    const size_t per_seq = n_kv * max_seq * head_dim;
+    KVB_CHECK(n_kv > 0 && n_q % n_kv == 0,
+              "rope_attention_decode: n_q %zu not a multiple of n_kv %zu", n_q, n_kv);
+    KVB_CHECK(qkv_len == n_seq * stride, "rope_attention_decode: qkv has %zu elems, want %zux%zu",
+              qkv_len, n_seq, stride);
+    KVB_CHECK(cos_t != nullptr && sin_t != nullptr && lens != nullptr,
+              "rope_attention_decode: null table or lengths array");
+    KVB_CHECK(head_dim > 0 && head_dim % 2 == 0 && table_len % (head_dim / 2) == 0,
+              "rope_attention_decode: bad cos/sin table sizes");
+    KVB_CHECK(max_len <= max_seq, "rope_attention_decode: max_len %zu exceeds max_seq %zu",
+              max_len, max_seq);
+    KVB_CHECK(seq_stride >= per_seq, "rope_attention_decode: seq_stride %zu < per-sequence cache %zu",
+              seq_stride, per_seq);
+    KVB_CHECK(n_seq == 0 || cache_len >= (n_seq - 1) * seq_stride + per_seq,
+              "rope_attention_decode: cache of %zu elems is too small", cache_len);
+    KVB_CHECK(out_row_stride >= n_q * head_dim, "rope_attention_decode: out_row_stride too small");
+    KVB_CHECK(fits_i32(n_seq) && fits_i32(max_seq) && fits_i32(max_len) &&
+                  fits_i32(table_len / (head_dim / 2)),
+              "rope_attention_decode: a dimension does not fit in i32");
+    if (n_seq == 0) return KVB_OK;
+    const size_t group = n_q / n_kv;
+    const size_t total_rows = ((n_seq - 1) * seq_stride + per_seq) / 64;
+    const bool fast = head_dim == 64 && group <= 16 && n_seq <= 65535 && n_kv <= 65535 &&
+                      seq_stride % 64 == 0 && out_row_stride % 8 == 0 && aligned(qkv, 16) &&
+                      aligned(kc, 16) && aligned(vc, 16) && fits_i32(total_rows);
+    if (!fast)
+        return fail(KVB_ERR_UNSUPPORTED,
+                    "rope_attention_decode: needs head_dim 64, n_q/n_kv <= 16, 16-byte aligned "
+                    "buffers and seq_stride a multiple of 64 (use kvb_rope_kv_append_batched + "
+                    "kvb_attention_decode)");
+    DecodeLaunch L;
+    L.q = qkv;
+    L.q_row_stride = stride;
+    L.kc = kc;
+    L.vc = vc;
+    L.seq_stride = seq_stride;
+    L.total_rows = total_rows;
+    L.lens = lens;
+    L.len_const = 0;
+    L.n_seq = n_seq;
+    L.max_len = max_len;
+    L.n_q = n_q;
+    L.n_kv = n_kv;
+    L.max_seq = max_seq;
+    L.scale = scale;
+    L.out = out;
+    L.out_row_stride = out_row_stride;
+    L.ws = workspace;
+    L.ws_len = workspace_len;
+    L.dtype = dtype;
+    L.rope_cos = cos_t;
+    L.rope_sin = sin_t;
+    L.rope_max_pos = table_len / (head_dim / 2);
+    return launch_decode_mma(stream, L);
 }
 
 int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, const void* kc,

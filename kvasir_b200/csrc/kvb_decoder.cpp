@@ -7,8 +7,9 @@
 // KV append -> attention -> o projection -> residual add -> rmsnorm -> gate/up
 // projection -> SiLU*mul -> down projection -> residual add; then the final
 // norm, the tied LM head (f32 logits) and greedy argmax.  The residual add is
-// fused into the following rmsnorm (kvb_add_rmsnorm), and RoPE into the KV
-// append (kvb_rope_kv_append_batched).  All device memory is caller-owned.
+// fused into the following rmsnorm (kvb_add_rmsnorm); RoPE, the KV append and
+// decode attention are one launch (kvb_rope_attention_decode) on contiguous
+// caches at head_dim 64.  All device memory is caller-owned.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -130,15 +131,24 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
         if (!d->block_table) {
             uint8_t* kl = d->kc + (size_t)l * layer_elems * 2;
             uint8_t* vl = d->vc + (size_t)l * layer_elems * 2;
-            STEP(kvb_rope_kv_append_batched(s, d->at(L.qkv), B, d->at<int32_t>(L.pos), d->cos_t,
-                                            d->sin_t, table_len, kl, vl, seq_stride, layer_elems,
-                                            nq, nkv, hd, max_seq, dt),
-                 false);
-            STEP(kvb_attention_decode(s, d->at(L.qkv), qkvd, kl, vl, seq_stride, layer_elems,
-                                      d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd, max_seq,
-                                      1.0f / sqrtf((float)hd), d->at(L.attn), qd, d->at(L.attn_ws),
-                                      L.attn_ws_len, dt),
-                 false);
+            if (hd == 64 && nq / nkv <= 16) {  // RoPE, KV append and attention: one launch
+                STEP(kvb_rope_attention_decode(s, d->at(L.qkv), B * qkvd, d->cos_t, d->sin_t,
+                                               table_len, kl, vl, seq_stride, layer_elems,
+                                               d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd,
+                                               max_seq, 1.0f / sqrtf((float)hd), d->at(L.attn), qd,
+                                               d->at(L.attn_ws), L.attn_ws_len, dt),
+                     false);
+            } else {
+                STEP(kvb_rope_kv_append_batched(s, d->at(L.qkv), B, d->at<int32_t>(L.pos), d->cos_t,
+                                                d->sin_t, table_len, kl, vl, seq_stride,
+                                                layer_elems, nq, nkv, hd, max_seq, dt),
+                     false);
+                STEP(kvb_attention_decode(s, d->at(L.qkv), qkvd, kl, vl, seq_stride, layer_elems,
+                                          d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd, max_seq,
+                                          1.0f / sqrtf((float)hd), d->at(L.attn), qd,
+                                          d->at(L.attn_ws), L.attn_ws_len, dt),
+                     false);
+            }
         } else {
             uint8_t* kl = d->kpool + (size_t)l * d->pool_len * 2;
             uint8_t* vl = d->vpool + (size_t)l * d->pool_len * 2;

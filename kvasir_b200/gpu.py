@@ -269,6 +269,20 @@ class Gpu:
             _ptr(lens), lens.numel(), max_len, n_q, n_kv, head_dim, max_seq, scale, _ptr(out),
             out_row_stride, _ptr(workspace), ws_len, dtype_tag(q)))
 
+    def rope_attention_decode(self, qkv, cos, sin, kc, vc, seq_stride, lens, max_len, n_q, n_kv,
+                              head_dim, max_seq, out, out_row_stride, scale=None, workspace=None):
+        """kvb_rope_attention_decode: rope_kv_append_batched at positions lens - 1, then
+        attention_decode, in one launch (qkv is left unrotated)."""
+        if lens.dtype != torch.int32:
+            raise ShapeError("lengths must be int32")
+        scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
+        ws_len = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        check(self._lib.kvb_rope_attention_decode(
+            self._s, _ptr(qkv), qkv.numel(), _ptr(cos), _ptr(sin), cos.numel(), _ptr(kc),
+            _ptr(vc), seq_stride, kc.numel(), _ptr(lens), lens.numel(), max_len, n_q, n_kv,
+            head_dim, max_seq, scale, _ptr(out), out_row_stride, _ptr(workspace), ws_len,
+            dtype_tag(qkv)))
+
     def attention_prefill(self, qkv, kc, vc, out, n_seq, t, pos0, n_q, n_kv, head_dim, max_seq):
         if vc.numel() != kc.numel():
             raise ShapeError("attention_prefill: bad cache sizes")

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import assert_close, dev, host_f32, normal16
+from gpu_util import assert_close, dev, host_bits, host_f32, normal16
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -302,3 +302,66 @@ def test_bounded_wait_selftest_keeps_context_usable(g):
     x = torch.ones(16, dtype=torch.bfloat16, device="cuda")
     g.add_inplace(x, x)
     assert float(x[0]) == 2.0
+
+
+# ------------------------------------------------------------------ fused RoPE + append + decode
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("lens,n_q,n_kv,with_ws", [
+    ([1, 64, 65, 300, 1000, 2049], 32, 8, True),
+    ([7, 513], 32, 8, False),
+    ([1024] * 32, 32, 8, True),
+    ([5, 200, 4096], 8, 8, True),
+    ([130, 1], 64, 4, True),
+])
+def test_rope_attention_decode_equals_rope_then_decode(g, dtype, lens, n_q, n_kv, with_ws):
+    """kvb_rope_attention_decode == kvb_rope_kv_append_batched (positions lens - 1) +
+    kvb_attention_decode on the rotated qkv, bit for bit: the attention output and
+    both caches (the new rows written, every other row untouched)."""
+    rng = np.random.default_rng(sum(lens) + n_q)
+    hd, max_seq = 64, 4160
+    n_seq = len(lens)
+    stride = (n_q + 2 * n_kv) * hd
+    tdt = torch.bfloat16 if dtype == "bf16" else torch.float16
+    qkv = normal16(rng, n_seq * stride, dtype=dtype)
+    per = n_kv * max_seq * hd
+    kc0 = normal16(rng, n_seq * per, dtype=dtype)
+    vc0 = normal16(rng, n_seq * per, dtype=dtype)
+    cos, sin = O.cos_sin_table(hd, max_seq, **O.LLAMA3_ROPE)
+    c, s = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    lens_np = np.array(lens, np.int32)
+    ld = torch.from_numpy(lens_np).cuda()
+    pos = torch.from_numpy(lens_np - 1).cuda()
+    max_len = int(lens_np.max())
+    ws = None
+    if with_ws:
+        ws = torch.empty(max(16, g.attention_decode_workspace_bytes(n_seq, max_len, n_q, n_kv, hd)),
+                         dtype=torch.uint8, device="cuda")
+    # unfused: rotate + append, then decode over the rotated qkv
+    qa, ka, va = dev(qkv, dtype), dev(kc0, dtype), dev(vc0, dtype)
+    g.rope_kv_append_batched(qa, pos, c, s, ka, va, per, n_q, n_kv, hd, max_seq)
+    want = torch.empty(n_seq * n_q * hd, dtype=tdt, device="cuda")
+    g.attention_decode(qa, stride, ka, va, per, ld, max_len, n_q, n_kv, hd, max_seq, want, n_q * hd,
+                       workspace=ws)
+    # fused
+    qb, kb, vb = dev(qkv, dtype), dev(kc0, dtype), dev(vc0, dtype)
+    got = torch.empty_like(want)
+    g.rope_attention_decode(qb, c, s, kb, vb, per, ld, max_len, n_q, n_kv, hd, max_seq, got,
+                            n_q * hd, workspace=ws)
+    assert g.device_error() == 0
+    assert torch.equal(got, want)
+    assert torch.equal(kb, ka) and torch.equal(vb, va)
+    np.testing.assert_array_equal(host_bits(qb), qkv)  # qkv itself is not rotated
+
+
+def test_rope_attention_decode_rejects_unsupported(g):
+    from kvasir_b200.gpu import UnsupportedError
+    n_seq, n_q, n_kv, hd, max_seq = 1, 4, 1, 32, 64
+    qkv = torch.zeros(n_seq * (n_q + 2 * n_kv) * hd, dtype=torch.bfloat16, device="cuda")
+    cos, sin = O.cos_sin_table(hd, max_seq, 10000.0, False)
+    kc = torch.zeros(n_seq * n_kv * max_seq * hd, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(n_seq * n_q * hd, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(UnsupportedError, match="head_dim 64"):
+        g.rope_attention_decode(qkv, torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda(), kc,
+                                kc.clone(), n_kv * max_seq * hd,
+                                torch.ones(1, dtype=torch.int32, device="cuda"), 1, n_q, n_kv, hd,
+                                max_seq, out, n_q * hd)
