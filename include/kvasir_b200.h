@@ -292,6 +292,18 @@ int kvb_rope_attention_decode(kvb_stream_t stream, const void* qkv, size_t qkv_l
                               size_t out_row_stride, void* workspace, size_t workspace_len,
                               int dtype);
 
+/* The same on the paged cache: kvb_rope_kv_append_paged (one row per sequence,
+ * at position lens[b] - 1) followed by kvb_attention_decode_paged, bit for bit,
+ * in one launch.  Requirements and errors as kvb_attention_decode_paged. */
+int kvb_rope_attention_decode_paged(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                    const float* cos_t, const float* sin_t, size_t table_len,
+                                    void* k_pool, void* v_pool, size_t pool_len,
+                                    const int32_t* block_table, size_t max_blocks,
+                                    size_t block_size, const int32_t* lens, size_t n_seq,
+                                    size_t max_len, size_t n_q, size_t n_kv, size_t head_dim,
+                                    float scale, void* out, size_t out_row_stride, void* workspace,
+                                    size_t workspace_len, int dtype);
+
 /* Greedy sampling: ids[r] = first index of the maximum of logits[r, 0:vocab)
  * (NaN never wins).  If advance is non-NULL, advance[r] += 1 for every r and,
  * if advance2 is non-NULL, advance2[r] += 1 (position / length counters of

@@ -82,6 +82,9 @@ SIGNATURES = {
     "kvb_attention_prefill": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _sz, _sz, _sz, _sz, _sz, _sz,
                                      _sz, _sz, _int]),
     "kvb_argmax_f32": (_int, [_p, _p, _sz, _sz, _p, _p, _p]),
+    "kvb_rope_attention_decode_paged": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _p, _sz, _p, _sz, _sz,
+                                               _p, _sz, _sz, _sz, _sz, _sz, C.c_float, _p, _sz, _p,
+                                               _sz, _int]),
     "kvb_rope_attention_decode": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _p, _sz, _sz, _p, _sz, _sz,
                                          _sz, _sz, _sz, _sz, C.c_float, _p, _sz, _p, _sz, _int]),
     "kvb_decoder_workspace_bytes": (_sz, [C.POINTER(DecoderConfig)]),

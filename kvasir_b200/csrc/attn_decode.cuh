@@ -125,17 +125,27 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
             const T* kin = reinterpret_cast<const T*>(a.q) + (size_t)b * a.q_row_stride +
                            (size_t)(a.n_kv * G + kvh) * 64;
             const T* vin = kin + (size_t)a.n_kv * 64;
-            const size_t row = (size_t)b * a.cache_seq_stride + ((size_t)kvh * a.max_seq + rope_p) * 64;
+            size_t row = (size_t)b * a.cache_seq_stride + ((size_t)kvh * a.max_seq + rope_p) * 64;
+            bool write = true;
+            if (a.block_table) {  // paged: the block holding position rope_p
+                const int lb = rope_p / a.block_size;
+                const int blk = a.block_table[(size_t)b * a.max_blocks + lb];
+                if (blk < 0 || blk >= a.n_blocks) {  // reported; the tile read sees zeros there
+                    if (threadIdx.x == 0) raise_dev_error(kDevErrBadPosition);
+                    write = false;
+                }
+                row = (((size_t)blk * a.n_kv + kvh) * a.block_size + (rope_p - lb * a.block_size)) * 64;
+            }
             T* kout = reinterpret_cast<T*>(a.kc_w) + row;
             T* vout = reinterpret_cast<T*>(a.vc_w) + row;
             const int t = threadIdx.x;
-            if (t < 32) {
+            if (write && t < 32) {
                 const float x0 = Elem<T>::to_f(kin[t]), x1 = Elem<T>::to_f(kin[t + 32]);
                 const float cs = a.rope_cos[(size_t)rope_p * 32 + t];
                 const float sn = a.rope_sin[(size_t)rope_p * 32 + t];
                 kout[t] = Elem<T>::from_f(rot_a(x0, x1, cs, sn));
                 kout[t + 32] = Elem<T>::from_f(rot_b(x0, x1, cs, sn));
-            } else if (t >= 64) {
+            } else if (write && t >= 64) {
                 vout[t - 64] = vin[t - 64];
             }
             // the tensor copies below read this row through the async proxy

@@ -1137,6 +1137,78 @@ int kvb_attention_prefill_paged(kvb_stream_t stream, const void* qkv, size_t qkv
                           pool_len);
 }
 
+// kvb_rope_kv_append_paged (one row per sequence, at position lens[b] - 1) and
+// kvb_attention_decode_paged in one launch.
+int kvb_rope_attention_decode_paged(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                    const float* cos_t, const float* sin_t, size_t table_len,
+                                    void* k_pool, void* v_pool, size_t pool_len,
+                                    const int32_t* block_table, size_t max_blocks,
+                                    size_t block_size, const int32_t* lens, size_t n_seq,
+                                    size_t max_len, size_t n_q, size_t n_kv, size_t head_dim,
+                                    float scale, void* out, size_t out_row_stride, void* workspace,
+                                    size_t workspace_len, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    KVB_CHECK(n_kv > 0 && n_q % n_kv == 0,
+              "rope_attention_decode_paged: n_q %zu not a multiple of n_kv %zu", n_q, n_kv);
+    KVB_CHECK(qkv_len == n_seq * stride,
+              "rope_attention_decode_paged: qkv has %zu elems, want %zux%zu", qkv_len, n_seq, stride);
+    KVB_CHECK(cos_t != nullptr && sin_t != nullptr && lens != nullptr && block_table != nullptr,
+              "rope_attention_decode_paged: null table, lengths array or block table");
+    KVB_CHECK(head_dim > 0 && head_dim % 2 == 0 && table_len % (head_dim / 2) == 0,
+              "rope_attention_decode_paged: bad cos/sin table sizes");
+    KVB_CHECK(block_size > 0, "rope_attention_decode_paged: block_size must be > 0");
+    const size_t per_block = n_kv * block_size * head_dim;
+    KVB_CHECK(pool_len % per_block == 0,
+              "rope_attention_decode_paged: pool of %zu elems is not a whole number of %zu-elem blocks",
+              pool_len, per_block);
+    KVB_CHECK(max_len <= max_blocks * block_size,
+              "rope_attention_decode_paged: max_len %zu exceeds %zu blocks of %zu", max_len,
+              max_blocks, block_size);
+    KVB_CHECK(out_row_stride >= n_q * head_dim, "rope_attention_decode_paged: out_row_stride too small");
+    const size_t n_blocks = pool_len / per_block;
+    const size_t total_rows = pool_len / 64;
+    KVB_CHECK(fits_i32(n_seq) && fits_i32(max_len) && fits_i32(max_blocks) && fits_i32(n_blocks) &&
+                  fits_i32(n_seq * max_blocks) && fits_i32(table_len / (head_dim / 2)),
+              "rope_attention_decode_paged: a dimension does not fit in i32");
+    if (n_seq == 0) return KVB_OK;
+    const size_t group = n_q / n_kv;
+    if (!(head_dim == 64 && block_size % 64 == 0 && group <= 16 && n_seq <= 65535 &&
+          n_kv <= 65535 && out_row_stride % 8 == 0 && aligned(qkv, 16) && aligned(k_pool, 16) &&
+          aligned(v_pool, 16) && fits_i32(total_rows + 64)))
+        return fail(KVB_ERR_UNSUPPORTED,
+                    "rope_attention_decode_paged: needs head_dim 64, block_size a multiple of 64, "
+                    "n_q/n_kv <= 16 and 16-byte aligned buffers");
+    DecodeLaunch L;
+    L.q = qkv;
+    L.q_row_stride = stride;
+    L.kc = k_pool;
+    L.vc = v_pool;
+    L.seq_stride = 0;
+    L.total_rows = total_rows;
+    L.lens = lens;
+    L.len_const = 0;
+    L.n_seq = n_seq;
+    L.max_len = max_len;
+    L.n_q = n_q;
+    L.n_kv = n_kv;
+    L.max_seq = max_blocks * block_size;
+    L.scale = scale;
+    L.out = out;
+    L.out_row_stride = out_row_stride;
+    L.ws = workspace;
+    L.ws_len = workspace_len;
+    L.dtype = dtype;
+    L.block_table = block_table;
+    L.max_blocks = max_blocks;
+    L.block_size = block_size;
+    L.n_blocks = n_blocks;
+    L.rope_cos = cos_t;
+    L.rope_sin = sin_t;
+    L.rope_max_pos = table_len / (head_dim / 2);
+    return launch_decode_mma(stream, L);
+}
+
 int kvb_attention_decode_paged(kvb_stream_t stream, const void* q, size_t q_row_stride,
                                const void* k_pool, const void* v_pool, size_t pool_len,
                                const int32_t* block_table, size_t max_blocks, size_t block_size,

@@ -152,15 +152,13 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
         } else {
             uint8_t* kl = d->kpool + (size_t)l * d->pool_len * 2;
             uint8_t* vl = d->vpool + (size_t)l * d->pool_len * 2;
-            STEP(kvb_rope_kv_append_paged(s, d->at(L.qkv), B, 1, d->at<int32_t>(L.pos), d->cos_t,
-                                          d->sin_t, table_len, kl, vl, d->pool_len, d->block_table,
-                                          d->max_blocks, d->block_size, nq, nkv, hd, dt),
-                 false);
-            STEP(kvb_attention_decode_paged(s, d->at(L.qkv), qkvd, kl, vl, d->pool_len,
-                                            d->block_table, d->max_blocks, d->block_size,
-                                            d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd,
-                                            1.0f / sqrtf((float)hd), d->at(L.attn), qd,
-                                            d->at(L.attn_ws), L.attn_ws_len, dt),
+            // paged mode requires head_dim 64 and 64-key blocks: always one launch
+            STEP(kvb_rope_attention_decode_paged(s, d->at(L.qkv), B * qkvd, d->cos_t, d->sin_t,
+                                                 table_len, kl, vl, d->pool_len, d->block_table,
+                                                 d->max_blocks, d->block_size,
+                                                 d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd,
+                                                 1.0f / sqrtf((float)hd), d->at(L.attn), qd,
+                                                 d->at(L.attn_ws), L.attn_ws_len, dt),
                  false);
         }
         if (L.attn_ws_len > 0) ++own;  // the split-KV combine pass

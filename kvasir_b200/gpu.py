@@ -283,6 +283,21 @@ class Gpu:
             head_dim, max_seq, scale, _ptr(out), out_row_stride, _ptr(workspace), ws_len,
             dtype_tag(qkv)))
 
+    def rope_attention_decode_paged(self, qkv, cos, sin, k_pool, v_pool, block_table, max_blocks,
+                                    block_size, lens, max_len, n_q, n_kv, head_dim, out,
+                                    out_row_stride, scale=None, workspace=None):
+        """kvb_rope_attention_decode_paged: rope_kv_append_paged at positions lens - 1,
+        then attention_decode_paged, in one launch."""
+        if lens.dtype != torch.int32 or block_table.dtype != torch.int32:
+            raise ShapeError("lengths and block table must be int32")
+        scale = 1.0 / math.sqrt(head_dim) if scale is None else scale
+        ws_len = workspace.numel() * workspace.element_size() if workspace is not None else 0
+        check(self._lib.kvb_rope_attention_decode_paged(
+            self._s, _ptr(qkv), qkv.numel(), _ptr(cos), _ptr(sin), cos.numel(), _ptr(k_pool),
+            _ptr(v_pool), k_pool.numel(), _ptr(block_table), max_blocks, block_size, _ptr(lens),
+            lens.numel(), max_len, n_q, n_kv, head_dim, scale, _ptr(out), out_row_stride,
+            _ptr(workspace), ws_len, dtype_tag(qkv)))
+
     def attention_prefill(self, qkv, kc, vc, out, n_seq, t, pos0, n_q, n_kv, head_dim, max_seq):
         if vc.numel() != kc.numel():
             raise ShapeError("attention_prefill: bad cache sizes")

@@ -232,3 +232,40 @@ def test_paged_prefill_equals_contiguous(g, n_seq, t, pos0, bs):
     assert g.device_error() == 0
     assert not torch.isnan(got.float()).any()
     assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("bs", [64, 256])
+def test_paged_rope_attention_decode_equals_two_launches(g, bs):
+    """kvb_rope_attention_decode_paged == kvb_rope_kv_append_paged (one row per sequence at
+    lens - 1) + kvb_attention_decode_paged, bit for bit: output and both pools."""
+    rng = np.random.default_rng(100 + bs)
+    lens = np.array([1, 64, 65, 700, 2049], np.int32)
+    n_seq, max_seq = len(lens), 2560
+    max_blocks = max_seq // bs
+    n_blocks = n_seq * max_blocks + 3
+    table = np.random.default_rng(8).permutation(n_blocks)[:n_seq * max_blocks].astype(np.int32)
+    table = table.reshape(n_seq, max_blocks)
+    stride = (N_Q + 2 * N_KV) * HD
+    qkv = normal16(rng, n_seq * stride)
+    kpool0 = normal16(rng, n_blocks * N_KV * bs * HD)
+    vpool0 = normal16(rng, n_blocks * N_KV * bs * HD)
+    cos, sin = O.cos_sin_table(HD, max_seq, **O.LLAMA3_ROPE)
+    c, s = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    ld = torch.from_numpy(lens).cuda()
+    tb = torch.from_numpy(table).cuda()
+    max_len = int(lens.max())
+    ws = torch.empty(max(16, g.attention_decode_workspace_bytes(n_seq, max_len, N_Q, N_KV, HD)),
+                     dtype=torch.uint8, device="cuda")
+    qa, ka, va = dev(qkv), dev(kpool0), dev(vpool0)
+    g.rope_kv_append_paged(qa, n_seq, 1, torch.from_numpy(lens - 1).cuda(), c, s, ka, va, tb,
+                           max_blocks, bs, N_Q, N_KV, HD)
+    want = torch.empty(n_seq * N_Q * HD, dtype=torch.bfloat16, device="cuda")
+    g.attention_decode_paged(qa, stride, ka, va, tb, max_blocks, bs, ld, max_len, N_Q, N_KV, HD,
+                             want, N_Q * HD, 0.125, ws)
+    qb, kb, vb = dev(qkv), dev(kpool0), dev(vpool0)
+    got = torch.empty_like(want)
+    g.rope_attention_decode_paged(qb, c, s, kb, vb, tb, max_blocks, bs, ld, max_len, N_Q, N_KV, HD,
+                                  got, N_Q * HD, 0.125, ws)
+    assert g.device_error() == 0
+    assert torch.equal(got, want)
+    assert torch.equal(kb, ka) and torch.equal(vb, va)
