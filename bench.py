@@ -21,7 +21,7 @@ projections + the kvb kernels + greedy argmax, replayed as one CUDA graph.
 
 `--impl reference` times only that CPU path (the reference arm).
 `--workload cfg1|cfg2|cfg3|cfg4` print per-kernel lines for the other
-BASELINE configs instead.
+BASELINE configs instead; `--workload sample` times the device-side sampler.
 """
 from __future__ import annotations
 
@@ -437,7 +437,7 @@ def main():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kernel", choices=["kernel", "reference"])
-    ap.add_argument("--workload", default="cfg5", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5"])
+    ap.add_argument("--workload", default="cfg5", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "sample"])
     ap.add_argument("--seqs", type=int, default=256, help="total sequences (cfg5)")
     ap.add_argument("--context", type=int, default=16384, help="KV tokens per sequence (cfg5)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)

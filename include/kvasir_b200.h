@@ -324,7 +324,8 @@ int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t
  * exact: the same seed, counter and logits give the same id.  temperature <= 0
  * is kvb_argmax_f32.  vocab at most 327680.  advance / advance2 as for
  * kvb_argmax_f32 (they may be the counters array: each row reads its counter
- * before advancing it).  One 8-CTA cluster per row. */
+ * before advancing it).  One cluster of 8 CTAs per row, or of 16 when rows * 16
+ * CTAs fit one per SM; the ids are the same either way. */
 int kvb_sample_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
                    float temperature, float top_p, uint64_t seed, const int32_t* counters,
                    int32_t* ids, int32_t* advance, int32_t* advance2);

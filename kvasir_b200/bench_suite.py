@@ -457,5 +457,31 @@ def cfg4(args):
         torch.cuda.empty_cache()
 
 
+def sample(args):
+    """kvb_sample_f32 alone: rows of 128,256 f32 logits drawn N(0, 5^2) (peaked) or
+    N(0, 0.1^2) (flat), temperature 0.8, top_p 1.0 / 0.95 / 0.5; 1 row (16-CTA
+    clusters) and 32 rows (8-CTA clusters).  The logits stay in L2 between the
+    back-to-back calls, as the decoder's do between its LM head and the draw."""
+    g = Gpu(0)
+    vocab = 128256
+    torch.manual_seed(0)
+    for sd in (5.0, 0.1):
+        for rows in (1, 32):
+            x = (torch.randn(rows, vocab, device="cuda") * sd).reshape(-1)
+            ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+            for _ in range(5):
+                g.argmax(x, rows, vocab, ids)
+            argmax_us = time_loop(lambda: g.argmax(x, rows, vocab, ids), 200) * 1e3
+            us = {}
+            for top_p in (1.0, 0.95, 0.5):
+                fn = lambda: g.sample(x, rows, vocab, ids, 0.8, top_p, 7)
+                for _ in range(5):
+                    fn()
+                us[str(top_p)] = time_loop(fn, 200) * 1e3
+            _emit({"workload": f"sample: {rows} row(s) of {vocab} logits N(0, {sd}^2), "
+                               "temperature 0.8", "metric": "us per call", "unit": "us",
+                   "top_p_us": us, "argmax_us": argmax_us})
+
+
 def run(name, args):
-    {"cfg1": cfg1, "cfg2": cfg2, "cfg3": cfg3, "cfg4": cfg4}[name](args)
+    {"cfg1": cfg1, "cfg2": cfg2, "cfg3": cfg3, "cfg4": cfg4, "sample": sample}[name](args)

@@ -119,6 +119,73 @@ static void set_max_smem(F* kernel, int bytes) {
     done.emplace_back(dev, key);
 }
 
+// ---------------------------------------------------------------- sampler launcher
+// sample_kernel<kCluster>: one cluster of kCluster CTAs per row, each CTA staging
+// its slice of the row in shared memory.
+template <int kCluster>
+static cudaError_t launch_sample(cudaStream_t stream, const float* logits, size_t rows,
+                                 size_t vocab, float inv_temp, float top_p, uint64_t seed,
+                                 const int32_t* counters, int32_t* ids, int32_t* adv,
+                                 int32_t* adv2, int vec4) {
+    const size_t slice = ((vocab + kCluster - 1) / kCluster + 3) & ~(size_t)3;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(rows * kCluster));
+    cfg.blockDim = dim3(kSampleThreads);
+    cfg.dynamicSmemBytes = slice * 4;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr = {};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = kCluster;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, sample_kernel<kCluster>, logits, (int)vocab, inv_temp, top_p,
+                              seed, counters, ids, adv, adv2, vec4);
+}
+
+// Sets the sampler's kernel attributes once per device, and reports whether the
+// device keeps a 16-CTA cluster of it resident (16 is a non-portable cluster size:
+// the kernel must allow it, and the occupancy query must find room for one).
+static bool sample_attrs_and_wide_ok() {
+    static std::mutex mu;
+    static int state[64];  // 0 unknown, 1 wide clusters run, 2 they do not
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!state[dev]) {
+        cudaFuncSetAttribute(sample_kernel<kSampleCluster>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSampleStageMax);
+        const size_t wide_smem =
+            (((size_t)kSampleCluster * kSampleMaxSlice / kSampleClusterWide + 3) & ~(size_t)3) * 4;
+        cudaError_t e = cudaFuncSetAttribute(sample_kernel<kSampleClusterWide>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)wide_smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(sample_kernel<kSampleClusterWide>,
+                                     cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        int clusters = 0;
+        if (e == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(kSampleClusterWide);
+            cfg.blockDim = dim3(kSampleThreads);
+            cfg.dynamicSmemBytes = wide_smem;
+            cudaLaunchAttribute attr = {};
+            attr.id = cudaLaunchAttributeClusterDimension;
+            attr.val.clusterDim.x = kSampleClusterWide;
+            attr.val.clusterDim.y = 1;
+            attr.val.clusterDim.z = 1;
+            cfg.attrs = &attr;
+            cfg.numAttrs = 1;
+            e = cudaOccupancyMaxActiveClusters(&clusters, sample_kernel<kSampleClusterWide>, &cfg);
+        }
+        if (e != cudaSuccess) cudaGetLastError();  // not an error of the caller's: 8-CTA clusters
+        state[dev] = (e == cudaSuccess && clusters >= 1) ? 1 : 2;
+    }
+    return state[dev] == 1;
+}
+
 // ---------------------------------------------------------------- rope / kv append launcher
 // Persistent bulk-copy RoPE: 16 consumer warps when two 16-row stages fit in
 // 200 KB of shared memory, else 8 or 4; as many CTAs per SM as fit, at most 2.
@@ -1359,13 +1426,15 @@ int kvb_sample_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t
         return kvb_argmax_f32(stream, logits, rows, vocab, ids, advance, advance2);
     KVB_CHECK(rows <= 0x7fffffff / kSampleCluster, "sample: rows %zu out of range", rows);
     const int vec4 = vocab % 4 == 0 && aligned(logits, 16);
-    // each CTA of a row's cluster stages its slice of the row in shared memory
-    const size_t slice = ((vocab + kSampleCluster - 1) / kSampleCluster + 3) & ~(size_t)3;
-    set_max_smem(sample_kernel, kSampleStageMax);
-    sample_kernel<<<(unsigned)(rows * kSampleCluster), kSampleThreads, slice * 4, stream>>>(
-        logits, (int)vocab, 1.0f / temperature, top_p, seed, counters, ids, advance, advance2,
-        vec4);
-    KVB_CHECK_LAUNCH("sample launch");
+    // 16-CTA clusters when the rows' 16 CTAs each still get an SM of their own
+    const bool wide = sample_attrs_and_wide_ok() && rows * kSampleClusterWide <= (size_t)num_sms();
+    const cudaError_t e =
+        wide ? launch_sample<kSampleClusterWide>(stream, logits, rows, vocab, 1.0f / temperature,
+                                                 top_p, seed, counters, ids, advance, advance2,
+                                                 vec4)
+             : launch_sample<kSampleCluster>(stream, logits, rows, vocab, 1.0f / temperature,
+                                             top_p, seed, counters, ids, advance, advance2, vec4);
+    if (e != cudaSuccess) return cuda_fail(e, "sample launch");
     return KVB_OK;
 }
 

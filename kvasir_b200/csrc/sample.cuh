@@ -1,5 +1,5 @@
 // sample.cuh -- temperature / top-p (nucleus) sampling over f32 logits, one
-// 8-CTA thread-block cluster per row, entirely on the device.
+// thread-block cluster of 8 (or 16) CTAs per row, entirely on the device.
 //
 // The reference plans this on the host over the copied logits
 // (DESIGN.md:24,109 of kvasir: "greedy / temperature / top-p", seeded so that
@@ -22,10 +22,11 @@
 // temperature <= 0 is greedy (the argmax kernel).
 //
 // Layout on the GPU: the row's vocabulary is cut into 8 contiguous slices, one
-// per CTA of a cluster, so a row streams through 8 SMs; each CTA reads its
-// slice from HBM / L2 once into shared memory and runs every pass from there.  Every cluster-wide
+// per CTA of a cluster, so a row streams through 8 SMs (16 slices and SMs when
+// the rows are too few to give every SM a CTA); each CTA reads its slice from
+// HBM / L2 once into shared memory and runs every pass from there.  Every cluster-wide
 // quantity (max, normaliser, digit histograms, kept mass per slice) is a
-// per-CTA partial in shared memory that each CTA reads from all 8 through
+// per-CTA partial in shared memory that each CTA reads from all of them through
 // distributed shared memory and sums in rank order: every CTA derives the same
 // K* and draw, and the CTA whose slice holds the drawn token writes it.
 #pragma once
@@ -36,7 +37,8 @@ namespace kvb {
 
 constexpr int kSampleThreads = 512;
 constexpr int kSampleWarps = kSampleThreads / 32;
-constexpr int kSampleCluster = 8;
+constexpr int kSampleCluster = 8;              // CTAs per row's cluster; 16 (a non-portable
+constexpr int kSampleClusterWide = 16;         // cluster size) when few rows leave SMs idle
 constexpr int kSampleMaxSlice = 40960;          // tokens per CTA: vocabularies up to 327680
 constexpr int kSampleStageMax = kSampleMaxSlice * 4;
 
@@ -93,6 +95,19 @@ __device__ __forceinline__ T dsmem_ld(const T* local, uint32_t rank) {
     asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(u) : "r"(remote));
     memcpy(&v, &u, 4);
     return v;
+}
+// The address of `local` in CTA `rank` of this cluster, and a 32-bit load from such an address.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(remote)
+                 : "r"((uint32_t)__cvta_generic_to_shared(local)), "r"(rank));
+    return remote;
+}
+__device__ __forceinline__ uint32_t dsmem_ld_at(uint32_t addr) {
+    uint32_t u;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(u) : "r"(addr));
+    return u;
 }
 // Cluster-wide barrier with release / acquire semantics for shared memory.
 __device__ __forceinline__ void cluster_sync() {
@@ -162,7 +177,8 @@ __device__ __forceinline__ void hist_add(uint32_t* hist_hi, uint32_t* hist_lo, i
     atomicAdd(&hist_lo[bucket], (uint32_t)(w & 0xFFFFu));
 }
 
-__global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSampleThreads)
+template <int kCluster>
+__global__ void __launch_bounds__(kSampleThreads)
     sample_kernel(const float* __restrict__ logits, int vocab, float inv_temp, float top_p,
                   uint64_t seed, const int32_t* __restrict__ counters, int32_t* __restrict__ ids,
                   int32_t* __restrict__ adv, int32_t* __restrict__ adv2, int vec4) {
@@ -171,6 +187,8 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
     __shared__ uint64_t red64[kSampleWarps];
     __shared__ uint32_t hist_hi[2048], hist_lo[2048];  // this CTA's digit histogram (read by
                                                       // the cluster): high / low 16 bits
+    __shared__ uint64_t hist_sum[256];                 // the cluster's sums of this CTA's share
+    __shared__ uint64_t part_share;                    // and their mass (read by the cluster)
     __shared__ float part_m;                   // this CTA's max (read by the cluster)
     __shared__ uint64_t part_z, part_kept;     // its normaliser and kept mass (read by the cluster)
     __shared__ int part_i;                     // its first +inf index
@@ -178,14 +196,15 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
     __shared__ float s_m;
     __shared__ uint64_t s_total, s_above, s_t, s_base;
     __shared__ uint32_t s_digit;
-    __shared__ int s_owner, s_warp, s_cross, s_low;
+    __shared__ uint64_t s_share_above, s_kept[kCluster];
+    __shared__ int s_owner, s_warp, s_cross, s_low, s_share;
     const uint32_t rank = cluster_rank();
-    const int row = blockIdx.x / kSampleCluster;
+    const int row = blockIdx.x / kCluster;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* l = logits + (size_t)row * vocab;
     const uint32_t counter = counters ? (uint32_t)counters[row] : 0u;
     // this CTA's slice, a multiple of 4 elements long
-    const int slice = ((vocab + kSampleCluster - 1) / kSampleCluster + 3) & ~3;
+    const int slice = ((vocab + kCluster - 1) / kCluster + 3) & ~3;
     const int v0 = min(vocab, (int)rank * slice), v1 = min(vocab, v0 + slice);
     const float4* l4 = reinterpret_cast<const float4*>(l);
     const float* sl = reinterpret_cast<const float*>(slice_smem);
@@ -238,11 +257,12 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
     m = block_max_f(m, red);
     if (tid == 0) part_m = m;
     cluster_sync();
-    if (tid == 0) {
-        float mm = -INFINITY;
-        for (uint32_t r = 0; r < kSampleCluster; ++r) mm = fmaxf(mm, dsmem_ld(&part_m, r));
-        s_m = mm;
-        part_i = 0x7fffffff;
+    if (warp == 0) {  // one lane per CTA of the cluster
+        const float mm = warp_max(lane < kCluster ? dsmem_ld(&part_m, (uint32_t)lane) : -INFINITY);
+        if (lane == 0) {
+            s_m = mm;
+            part_i = 0x7fffffff;
+        }
     }
     __syncthreads();
     m = s_m;
@@ -254,7 +274,7 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
         cluster_sync();
         if (rank == 0 && tid == 0) {
             int first = 0x7fffffff;
-            for (uint32_t r = 0; r < kSampleCluster; ++r) first = min(first, dsmem_ld(&part_i, r));
+            for (uint32_t r = 0; r < kCluster; ++r) first = min(first, dsmem_ld(&part_i, r));
             chosen = first;
         }
     } else if (m == -INFINITY) {  // nothing but NaN / -inf: index 0, as the argmax
@@ -277,10 +297,10 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
         z = block_sum_u64(z, red64);
         if (tid == 0) part_z = z;
         cluster_sync();  // partials and histograms of pass 0 complete everywhere
-        if (tid == 0) {
-            uint64_t zz = 0;
-            for (uint32_t r = 0; r < kSampleCluster; ++r) zz += dsmem_ld64(&part_z, r);
-            s_total = zz;
+        if (warp == 0) {  // one lane per CTA of the cluster
+            const uint64_t zz =
+                warp_sum_u64(lane < kCluster ? dsmem_ld64(&part_z, (uint32_t)lane) : 0ull);
+            if (lane == 0) s_total = zz;
         }
         __syncthreads();
         const uint64_t total = s_total;
@@ -293,25 +313,64 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
             // (above = mass of the keys above all of them); returns it and the mass above it.
             // If every bucket falls short (weights truncated to 0) the lowest nonempty one.
             auto select = [&](int nb, uint64_t above, uint32_t& digit, uint64_t& above_out) {
-                const int per = (nb + kSampleThreads - 1) / kSampleThreads;  // 1, 2 or 4
-                uint64_t hb[4] = {0, 0, 0, 0};
+                // 1. CTA `rank` owns the buckets [b0, b1): it sums them over the cluster
+                //    (consecutive threads read consecutive buckets of every CTA: whole
+                //    128-byte lines) into hist_sum, and publishes their mass
+                const int share = (nb + kCluster - 1) / kCluster;  // <= 256
+                const int b0 = min(nb, (int)rank * share), b1 = min(nb, b0 + share);
+                uint64_t part = 0;
+                if (b0 + tid < b1) {
+                    const int b = b0 + tid;
+                    uint32_t vh[kCluster], vl[kCluster];
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    if (k < per && tid * per + k < nb) {
-                        uint32_t vh[kSampleCluster], vl[kSampleCluster];
-#pragma unroll
-                        for (uint32_t r = 0; r < kSampleCluster; ++r) {
-                            vh[r] = dsmem_ld(&hist_hi[tid * per + k], r);
-                            vl[r] = dsmem_ld(&hist_lo[tid * per + k], r);
-                        }
-#pragma unroll
-                        for (uint32_t r = 0; r < kSampleCluster; ++r)
-                            hb[k] += ((uint64_t)vh[r] << 16) + vl[r];
+                    for (uint32_t r = 0; r < kCluster; ++r) {
+                        vh[r] = dsmem_ld_at(dsmem_addr(&hist_hi[b], r));
+                        vl[r] = dsmem_ld_at(dsmem_addr(&hist_lo[b], r));
                     }
-                uint64_t own = 0;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) own += hb[k];
-                // mass of the runs above this thread's: a suffix scan over the block
+                    for (uint32_t r = 0; r < kCluster; ++r)
+                        part += ((uint64_t)vh[r] << 16) + vl[r];
+                    hist_sum[tid] = part;
+                }
+                part = block_sum_u64(part, red64);
+                if (tid == 0) part_share = part;
+                cluster_sync();  // every share is summed; no CTA reads hist_hi / hist_lo again
+                // 2. the share where the mass counted from the top first reaches the target,
+                //    else the lowest nonempty share (all CTAs decide alike from the 8 masses)
+                if (warp == 0) {  // one lane per CTA's share
+                    const uint64_t mr =
+                        lane < kCluster ? dsmem_ld64(&part_share, (uint32_t)lane) : 0ull;
+                    uint64_t suf = mr;  // mass of the shares from this one up
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const uint64_t y = __shfl_down_sync(0xffffffffu, suf, o);
+                        if (lane + o < 32) suf += y;
+                    }
+                    const uint32_t crosses =
+                        __ballot_sync(0xffffffffu, mr > 0 && above + suf >= target);
+                    const uint32_t nonempty = __ballot_sync(0xffffffffu, mr > 0);
+                    const int cr = crosses ? 31 - __clz((int)crosses)
+                                           : (nonempty ? __ffs((int)nonempty) - 1 : -1);
+                    const uint64_t cr_above =
+                        __shfl_sync(0xffffffffu, above + suf - mr, cr < 0 ? 0 : cr);
+                    if (lane == 0) {
+                        s_share = cr;
+                        s_share_above = cr_above;
+                        s_cross = -1;
+                        s_low = 0x7fffffff;
+                    }
+                }
+                __syncthreads();
+                const int cr = s_share;
+                if (cr < 0) {  // no mass at all: nothing to refine
+                    digit = 0;
+                    above_out = above;
+                    return;
+                }
+                // 3. that share's buckets, one per thread, from the CTA that summed them
+                const int c0 = min(nb, cr * share), n = min(nb, c0 + share) - c0;
+                const uint64_t own = tid < n ? dsmem_ld64(&hist_sum[tid], (uint32_t)cr) : 0ull;
+                // mass of the buckets above this thread's: a suffix scan over the block
                 uint64_t inc = own;
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
@@ -319,47 +378,20 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
                     if (lane + o < 32) inc += y;
                 }
                 if (lane == 0) red64[warp] = inc;
-                if (tid == 0) {
-                    s_cross = -1;
-                    s_low = 0x7fffffff;
-                }
                 __syncthreads();
                 uint64_t above_warps = 0;
                 for (int w = warp + 1; w < kSampleWarps; ++w) above_warps += red64[w];
-                const uint64_t ex = above + above_warps + (inc - own);  // above my run
+                const uint64_t ex = s_share_above + above_warps + (inc - own);  // above mine
                 if (own > 0 && ex + own >= target) atomicMax(&s_cross, tid);
                 if (own > 0) atomicMin(&s_low, tid);
                 __syncthreads();
-                const int cross = s_cross >= 0 ? s_cross : (s_low != 0x7fffffff ? s_low : -1);
-                if (cross < 0 && tid == 0) {  // no mass: nothing to refine
-                    s_digit = 0;
-                    s_above = above;
+                // the crossing bucket, else (every bucket short) the lowest nonempty one
+                const int pick = s_cross >= 0 ? s_cross : s_low;
+                if (tid == pick) {
+                    s_digit = (uint32_t)(c0 + tid);
+                    s_above = ex;
                 }
-                if (tid == cross) {
-                    uint64_t acc = ex;
-                    int d = tid * per;
-                    if (s_cross >= 0) {
-                        for (int k = per - 1; k >= 0; --k) {
-                            if (hb[k] > 0 && acc + hb[k] >= target) {
-                                d = tid * per + k;
-                                break;
-                            }
-                            acc += hb[k];
-                        }
-                    } else {
-                        int lo = per - 1;
-                        for (int k = 0; k < per; ++k)
-                            if (hb[k] > 0) {
-                                lo = k;
-                                break;
-                            }
-                        for (int k = per - 1; k > lo; --k) acc += hb[k];
-                        d = tid * per + lo;
-                    }
-                    s_digit = (uint32_t)d;
-                    s_above = acc;
-                }
-                cluster_sync();  // the cluster has read every histogram of this pass
+                __syncthreads();
                 digit = s_digit;
                 above_out = s_above;
             };
@@ -411,10 +443,15 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
             part_kept = cm;
         }
         cluster_sync();
+        if (warp == 0) {  // one lane per CTA of the cluster
+            const uint64_t v = lane < kCluster ? dsmem_ld64(&part_kept, (uint32_t)lane) : 0ull;
+            if (lane < kCluster) s_kept[lane] = v;
+        }
+        __syncthreads();
         if (tid == 0) {
-            uint64_t pm[kSampleCluster], sum = 0;
-            for (uint32_t r = 0; r < kSampleCluster; ++r) {
-                pm[r] = dsmem_ld64(&part_kept, r);
+            uint64_t pm[kCluster], sum = 0;
+            for (int r = 0; r < kCluster; ++r) {
+                pm[r] = s_kept[r];
                 sum += pm[r];
             }
             // t = floor(u24 * kept / 2^24), in 128-bit integer arithmetic
@@ -423,7 +460,7 @@ __global__ void __cluster_dims__(kSampleCluster, 1, 1) __launch_bounds__(kSample
             const uint64_t t = (__umul64hi(sum, u24) << 40) | ((sum * u24) >> 24);
             int owner = -1, last = -1;
             uint64_t base = 0, base_last = 0, acc = 0;
-            for (int r = 0; r < kSampleCluster; ++r) {
+            for (int r = 0; r < kCluster; ++r) {
                 if (pm[r] > 0) {
                     last = r;
                     base_last = acc;

@@ -51,6 +51,23 @@ def test_sample_matches_oracle(g, vocab, temperature, top_p):
     _check(logits, got, temperature, top_p, 1234, counters)
 
 
+@pytest.mark.parametrize("vocab,sd", [(128256, 0.1), (128256, 5.0), (1001, 1.0)])
+def test_wide_and_narrow_clusters_agree(g, vocab, sd):
+    """Up to 9 rows run on 16-CTA clusters (148 SMs), more rows on 8-CTA clusters:
+    the same rows draw the same ids either way, equal to the oracle's.  Flat logits
+    (sd 0.1) take the most refinement passes; 1001 is not a multiple of 4 (the
+    scalar loads)."""
+    rng = np.random.default_rng(vocab + int(10 * sd))
+    logits = rng.normal(0, sd, (16, vocab)).astype(np.float32)
+    counters = rng.integers(0, 1 << 20, 16).tolist()
+    for temperature, top_p in ((0.8, 0.95), (1.0, 0.5), (0.6, 1.0)):
+        narrow = _run(g, logits, temperature, top_p, 5, counters)
+        for rows in (1, 9):
+            wide = _run(g, logits[:rows], temperature, top_p, 5, counters[:rows])
+            np.testing.assert_array_equal(wide, narrow[:rows])
+        _check(logits, narrow, temperature, top_p, 5, counters)
+
+
 def test_greedy_when_temperature_is_zero(g):
     rng = np.random.default_rng(1)
     logits = rng.normal(0, 1, (5, 3000)).astype(np.float32)
