@@ -288,6 +288,8 @@ def run_decode(args):
 
     # ---- device-resident throughput
     barrier(dist, torch)
+    if args.ncu_window:
+        torch.cuda.profiler.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
         ev0.record(stream)
@@ -442,6 +444,9 @@ def main():
     ap.add_argument("--context", type=int, default=16384, help="KV tokens per sequence (cfg5)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-window", action="store_true",
+                    help="call cudaProfilerStart just before the first timed decode steps, so that "
+                         "`ncu --profile-from-start off` lists only step launches (cfg4, cfg5)")
     ap.add_argument("--paged", type=int, default=0,
                     help="cfg5 on a paged KV cache with this block size (a multiple of 64); "
                          "0 = contiguous")

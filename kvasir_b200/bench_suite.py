@@ -408,6 +408,8 @@ def cfg4(args):
         dec.set_lengths(ctx)
         torch.cuda.synchronize()
         s = torch.cuda.current_stream()
+        if getattr(args, "ncu_window", False) and B == 1:
+            torch.cuda.profiler.start()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(s)
         for _ in range(steps):
