@@ -16,8 +16,8 @@
 // All sums are exact integers, so the id depends only on the weights.
 // K* is found by a mass-weighted select over the keys with no sort: a first
 // histogram of w by the log-scaled key distance below the row's maximum (exact
-// below 32, then 32 buckets per power of two, so logits that differ in their
-// low bits still spread over many buckets), then radix passes of up to 11 bits
+// below 128, then 128 buckets per power of two, so logits that differ in their
+// low bits still spread over many buckets), then radix passes of up to 12 bits
 // over the chosen bucket's exact distance range, fed only by its tokens.
 // temperature <= 0 is greedy (the argmax kernel).
 //
@@ -152,23 +152,31 @@ __device__ __forceinline__ uint64_t dsmem_ld64(const uint64_t* local, uint32_t r
     return v;
 }
 
-// Log-linear bucket of a key distance below the row's maximum: exact below 32,
-// then 32 buckets per power of two (buckets 0 .. 895, increasing with d).
+// Log-linear bucket of a key distance below the row's maximum: exact below 128,
+// then 128 buckets per power of two (buckets 0 .. kLogBuckets - 1, increasing
+// with d).  A bucket spans at most 2^24 distances: two 12-bit refinement passes.
+constexpr int kLogSubBits = 7;
+constexpr int kLogSub = 1 << kLogSubBits;
+constexpr int kLogBuckets = kLogSub + (32 - kLogSubBits) * kLogSub;  // 3328
+constexpr int kRadixBits = 12;                                        // refinement digits
+constexpr int kHistBuckets = 1 << kRadixBits;                         // >= kLogBuckets
+static_assert(kLogBuckets <= kHistBuckets, "first-pass buckets exceed the histogram");
 __device__ __forceinline__ int log_bucket(uint32_t d) {
-    if (d < 32) return (int)d;
-    const int e = 31 - __clz(d);  // 5 .. 31
-    return 32 + (e - 5) * 32 + (int)((d >> (e - 5)) & 31u);
+    if (d < (uint32_t)kLogSub) return (int)d;
+    const int e = 31 - __clz(d);  // kLogSubBits .. 31
+    return kLogSub + (e - kLogSubBits) * kLogSub +
+           (int)((d >> (e - kLogSubBits)) & (uint32_t)(kLogSub - 1));
 }
 // The distances [lo, lo + 2^width_log2) of a bucket.
 __device__ __forceinline__ void log_bucket_range(int b, uint32_t& lo, int& width_log2) {
-    if (b < 32) {
+    if (b < kLogSub) {
         lo = (uint32_t)b;
         width_log2 = 0;
         return;
     }
-    const int e = 5 + (b - 32) / 32, f = (b - 32) % 32;
-    lo = (32u + (uint32_t)f) << (e - 5);
-    width_log2 = e - 5;
+    const int e = kLogSubBits + (b - kLogSub) / kLogSub, f = (b - kLogSub) % kLogSub;
+    lo = ((uint32_t)kLogSub + (uint32_t)f) << (e - kLogSubBits);
+    width_log2 = e - kLogSubBits;
 }
 
 __device__ __forceinline__ void hist_add(uint32_t* hist_hi, uint32_t* hist_lo, int bucket,
@@ -182,12 +190,13 @@ __global__ void __launch_bounds__(kSampleThreads)
     sample_kernel(const float* __restrict__ logits, int vocab, float inv_temp, float top_p,
                   uint64_t seed, const int32_t* __restrict__ counters, int32_t* __restrict__ ids,
                   int32_t* __restrict__ adv, int32_t* __restrict__ adv2, int vec4) {
+    static_assert(kHistBuckets / kCluster <= kSampleThreads, "a share is one bucket per thread");
     extern __shared__ float4 slice_smem[];  // this CTA's slice of the row
     __shared__ float red[kSampleWarps];
     __shared__ uint64_t red64[kSampleWarps];
-    __shared__ uint32_t hist_hi[2048], hist_lo[2048];  // this CTA's digit histogram (read by
+    __shared__ uint32_t hist_hi[kHistBuckets], hist_lo[kHistBuckets];  // this CTA's histogram (read by
                                                       // the cluster): high / low 16 bits
-    __shared__ uint64_t hist_sum[256];                 // the cluster's sums of this CTA's share
+    __shared__ uint64_t hist_sum[kHistBuckets / kCluster];  // the cluster's sums of this CTA's share
     __shared__ uint64_t part_share;                    // and their mass (read by the cluster)
     __shared__ float part_m;                   // this CTA's max (read by the cluster)
     __shared__ uint64_t part_z, part_kept;     // its normaliser and kept mass (read by the cluster)
@@ -282,17 +291,18 @@ __global__ void __launch_bounds__(kSampleThreads)
     } else {
         // ---- normaliser and the first digit histogram in one pass
         const bool nucleus = top_p < 1.f;
-        for (int b = tid; b < 2048; b += kSampleThreads) hist_hi[b] = hist_lo[b] = 0u;
+        for (int b = tid; b < kLogBuckets; b += kSampleThreads) hist_hi[b] = hist_lo[b] = 0u;
         __syncthreads();
         // first histogram: by log-scaled key distance below the maximum, which spreads
-        // tokens of nearly equal logits over many buckets; index 1023 - bucket, so that
+        // tokens of nearly equal logits over many buckets; index kLogBuckets - 1 - bucket, so that
         // higher indices hold higher keys
         const uint32_t kmax = order_key(m);
         uint64_t z = 0;
         for_slice([&](int, float x) {
             const uint64_t w = fixed_weight(x, m, inv_temp);
             z += w;
-            if (nucleus && w) hist_add(hist_hi, hist_lo, 1023 - log_bucket(kmax - order_key(x)), w);
+            if (nucleus && w)
+                hist_add(hist_hi, hist_lo, kLogBuckets - 1 - log_bucket(kmax - order_key(x)), w);
         });
         z = block_sum_u64(z, red64);
         if (tid == 0) part_z = z;
@@ -316,7 +326,7 @@ __global__ void __launch_bounds__(kSampleThreads)
                 // 1. CTA `rank` owns the buckets [b0, b1): it sums them over the cluster
                 //    (consecutive threads read consecutive buckets of every CTA: whole
                 //    128-byte lines) into hist_sum, and publishes their mass
-                const int share = (nb + kCluster - 1) / kCluster;  // <= 256
+                const int share = (nb + kCluster - 1) / kCluster;  // <= kSampleThreads
                 const int b0 = min(nb, (int)rank * share), b1 = min(nb, b0 + share);
                 uint64_t part = 0;
                 if (b0 + tid < b1) {
@@ -397,18 +407,21 @@ __global__ void __launch_bounds__(kSampleThreads)
             };
             uint32_t d0;
             uint64_t above;
-            select(1024, 0, d0, above);
+            select(kLogBuckets, 0, d0, above);
             // the chosen bucket is the key distances [lo, lo + 2^nbits): refine over
             // r = (lo + 2^nbits - 1) - distance, whose higher values are higher keys
             uint32_t lo;
             int nbits;
-            log_bucket_range(1023 - (int)d0, lo, nbits);
+            log_bucket_range(kLogBuckets - 1 - (int)d0, lo, nbits);
             const uint64_t hi = (uint64_t)lo + (1ull << nbits);
             uint32_t prefix = 0;
-            for (int done = 0; done < nbits;) {
-                const int bits = min(11, nbits - done);
+            // as few passes of at most kRadixBits as the range needs, their digits balanced
+            // (13 bits: 7 + 6), so that each histogram and select is as small as it can be
+            const int passes = (nbits + kRadixBits - 1) / kRadixBits;
+            for (int done = 0, pass = 0; done < nbits; ++pass) {
+                const int bits = (nbits - done + passes - pass - 1) / (passes - pass);
                 const int shift = nbits - done - bits;
-                for (int b = tid; b < 2048; b += kSampleThreads) hist_hi[b] = hist_lo[b] = 0u;
+                for (int b = tid; b < (1 << bits); b += kSampleThreads) hist_hi[b] = hist_lo[b] = 0u;
                 __syncthreads();
                 for_slice([&](int, float x) {
                     const uint32_t dist = kmax - order_key(x);
