@@ -147,13 +147,21 @@ static cudaError_t launch_sample(cudaStream_t stream, const float* logits, size_
 // Sets the sampler's kernel attributes once per device, and reports whether the
 // device keeps a 16-CTA cluster of it resident (16 is a non-portable cluster size:
 // the kernel must allow it, and the occupancy query must find room for one).
-static bool sample_attrs_and_wide_ok() {
+// While `stream` is being captured the query is not made: 8-CTA clusters, and the
+// answer is left for a later call (the decode-step driver asks before it captures).
+static bool sample_attrs_and_wide_ok(cudaStream_t stream) {
     static std::mutex mu;
     static int state[64];  // 0 unknown, 1 wide clusters run, 2 they do not
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return false;
     std::lock_guard<std::mutex> lock(mu);
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (!state[dev] && stream != nullptr && cudaStreamIsCapturing(stream, &cap) == cudaSuccess &&
+        cap != cudaStreamCaptureStatusNone) {
+        set_max_smem(sample_kernel<kSampleCluster>, kSampleStageMax);
+        return false;
+    }
     if (!state[dev]) {
         cudaFuncSetAttribute(sample_kernel<kSampleCluster>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSampleStageMax);
@@ -185,6 +193,8 @@ static bool sample_attrs_and_wide_ok() {
     }
     return state[dev] == 1;
 }
+
+void sample_prepare() { sample_attrs_and_wide_ok(nullptr); }
 
 // ---------------------------------------------------------------- rope / kv append launcher
 // Persistent bulk-copy RoPE: 16 consumer warps when two 16-row stages fit in
@@ -1427,7 +1437,8 @@ int kvb_sample_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t
     KVB_CHECK(rows <= 0x7fffffff / kSampleCluster, "sample: rows %zu out of range", rows);
     const int vec4 = vocab % 4 == 0 && aligned(logits, 16);
     // 16-CTA clusters when the rows' 16 CTAs each still get an SM of their own
-    const bool wide = sample_attrs_and_wide_ok() && rows * kSampleClusterWide <= (size_t)num_sms();
+    const bool wide =
+        sample_attrs_and_wide_ok(stream) && rows * kSampleClusterWide <= (size_t)num_sms();
     const cudaError_t e =
         wide ? launch_sample<kSampleClusterWide>(stream, logits, rows, vocab, 1.0f / temperature,
                                                  top_p, seed, counters, ids, advance, advance2,

@@ -381,6 +381,7 @@ int kvb_decoder_step(kvb_decoder_t d, kvb_stream_t s) {
     if (!d->exec) {
         const int tst = tune_projections(d, s);
         if (tst != KVB_OK) return tst;
+        kvb::sample_prepare();
         // Record the step once on the private capture stream (recording runs
         // nothing); host-side work (argument checks, tensor-map encoding)
         // happens only here, every step is then one graph launch on `s`.

@@ -29,6 +29,11 @@ int num_sms();
 int encode_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* dims,
                 const uint64_t* strides_bytes, const uint32_t* box, int dtype);
 
+// Sets the sampler's kernel attributes and decides its cluster size for the
+// current device, outside any stream capture (kvb_sample_f32 then makes no
+// attribute or occupancy call while a step is being recorded).
+void sample_prepare();
+
 }  // namespace kvb
 
 #define KVB_CHECK(cond, ...)                                         \

@@ -130,6 +130,45 @@ def test_counters_advance_after_they_are_read(g):
     _check(logits, ids.cpu().numpy(), 0.9, 0.9, 21, pos0)
 
 
+_FRESH = r"""
+import json, sys
+import torch
+sys.path.insert(0, sys.argv[1])
+from kvasir_b200.config import LlamaConfig
+from kvasir_b200.decoder import Decoder
+cfg = LlamaConfig(hidden_size=256, intermediate_size=512, num_layers=2, num_heads=4,
+                  num_kv_heads=1, head_dim=64, vocab_size=1000, rms_norm_eps=1e-5,
+                  rope_theta=500000.0, max_position_embeddings=4096)
+dec = Decoder(cfg, 2, 64, seed=5)
+dec.fill_kv_normal(seed=6)
+dec.set_lengths([4, 20])
+dec.ids_in.copy_(torch.tensor([1, 2], dtype=torch.int32, device="cuda"))
+dec.set_sampling(0.9, 0.8, seed=11)
+dec.step()
+torch.cuda.synchronize()
+print(json.dumps({"logits": dec.logits.cpu().numpy().tolist(),
+                  "ids": dec.ids_out.cpu().numpy().tolist()}))
+dec.close()
+"""
+
+
+def test_decoder_sampling_first_use_in_a_fresh_process():
+    """The decoder's first sampled step is recorded into its CUDA graph; in a process
+    that has not sampled before, the sampler's one-time set-up (kernel attributes,
+    cluster-size check) must happen before that capture.  The ids are the oracle's."""
+    import json
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    out = subprocess.run([sys.executable, "-c", _FRESH, root], capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    d = json.loads(out.stdout.strip().splitlines()[-1])
+    logits = np.asarray(d["logits"], np.float32).reshape(2, 1000)
+    _check(logits, np.asarray(d["ids"]), 0.9, 0.8, 11, [4, 20])
+
+
 def test_decoder_sampling_mode():
     """Decoder steps with sampling: each step's ids are the oracle's draw from that
     step's logits with the positions as counters; set_sampling(0) is greedy again."""
