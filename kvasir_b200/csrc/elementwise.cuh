@@ -111,41 +111,73 @@ __global__ void silu_mul_scalar_kernel(const T* __restrict__ gu, T* __restrict__
 }
 
 // ---------------------------------------------------------------- greedy argmax
-// One CTA per row; first index of the maximum, NaN never wins.
+// First index of the row's maximum; NaN and -inf never win, so a row with no
+// value above -inf gives 0 (the CPU reference's scan: strict > from -inf, index 0).
+// The merge is a maximum over (value descending, index ascending), so the order in
+// which partials meet does not change the result.
 __device__ __forceinline__ void argmax_merge(float& v, int& i, float v2, int i2) {
-    if (v2 > v || (v2 == v && i2 < i)) {
+    if (v2 > v || (v2 == v && i2 < i && v2 > -INFINITY)) {
         v = v2;
         i = i2;
     }
 }
-__global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ logits, int vocab,
-                                                     int32_t* __restrict__ ids,
-                                                     int32_t* __restrict__ adv,
-                                                     int32_t* __restrict__ adv2, int vec4) {
-    const int row = blockIdx.x;
-    const float* l = logits + (size_t)row * vocab;
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    if (vec4) {
-        const float4* l4 = reinterpret_cast<const float4*>(l);
-        for (int c = threadIdx.x; c < vocab / 4; c += blockDim.x) {
-            const float4 v = l4[c];
-            argmax_merge(best, bi, v.x, 4 * c);
-            argmax_merge(best, bi, v.y, 4 * c + 1);
-            argmax_merge(best, bi, v.z, 4 * c + 2);
-            argmax_merge(best, bi, v.w, 4 * c + 3);
-        }
-    } else {
-        for (int c = threadIdx.x; c < vocab; c += blockDim.x) argmax_merge(best, bi, l[c], c);
-    }
+__device__ __forceinline__ void argmax_warp(float& v, int& i) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-        const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
-        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-        argmax_merge(best, bi, v2, i2);
+        const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+        argmax_merge(v, i, v2, i2);
     }
-    __shared__ float sv[16];
-    __shared__ int si[16];
+}
+
+// One 8-CTA cluster per row: CTA r scans the row's r-th contiguous slice (`slice`
+// elements, a multiple of 4) with kArgmaxUnroll independent loads in flight per
+// thread, and CTA 0 merges the eight partials through distributed shared memory.
+// A 128,256-token row is 64 KB per SM, one round of loads (one CTA per row kept a
+// single SM's loads waiting on L2 latency ~60 times in a row).
+constexpr int kArgmaxCluster = 8;
+constexpr int kArgmaxThreads = 512;
+constexpr int kArgmaxUnroll = 8;
+__global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmaxThreads)
+    argmax_kernel(const float* __restrict__ logits, int vocab, int slice,
+                  int32_t* __restrict__ ids, int32_t* __restrict__ adv,
+                  int32_t* __restrict__ adv2, int vec4) {
+    const uint32_t rank = cluster_rank();
+    const size_t row = blockIdx.x / kArgmaxCluster;
+    const float* l = logits + row * (size_t)vocab;
+    const int lo = (int)min((int64_t)vocab, (int64_t)rank * slice);
+    const int hi = (int)min((int64_t)vocab, (int64_t)lo + slice);
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    if (vec4) {  // vocab and slice are multiples of 4, the row 16-byte aligned
+        const float4* l4 = reinterpret_cast<const float4*>(l);
+        const int hi4 = hi / 4;
+        for (int c0 = lo / 4 + (int)threadIdx.x; c0 < hi4; c0 += kArgmaxThreads * kArgmaxUnroll) {
+            float4 v[kArgmaxUnroll];
+#pragma unroll
+            for (int u = 0; u < kArgmaxUnroll; ++u) {
+                const int c = c0 + u * kArgmaxThreads;
+                if (c < hi4) v[u] = l4[c];
+            }
+#pragma unroll
+            for (int u = 0; u < kArgmaxUnroll; ++u) {
+                const int c = c0 + u * kArgmaxThreads;
+                if (c < hi4) {
+                    argmax_merge(best, bi, v[u].x, 4 * c);
+                    argmax_merge(best, bi, v[u].y, 4 * c + 1);
+                    argmax_merge(best, bi, v[u].z, 4 * c + 2);
+                    argmax_merge(best, bi, v[u].w, 4 * c + 3);
+                }
+            }
+        }
+    } else {
+        for (int c = lo + (int)threadIdx.x; c < hi; c += kArgmaxThreads) argmax_merge(best, bi, l[c], c);
+    }
+    argmax_warp(best, bi);
+    __shared__ float sv[kArgmaxThreads / 32];
+    __shared__ int si[kArgmaxThreads / 32];
+    __shared__ float part_v;  // this CTA's partial, read by CTA 0 of the cluster
+    __shared__ int part_i;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) {
         sv[warp] = best;
@@ -153,21 +185,26 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ l
     }
     __syncthreads();
     if (warp == 0) {
-        const int nw = blockDim.x >> 5;
-        best = lane < nw ? sv[lane] : -INFINITY;
-        bi = lane < nw ? si[lane] : 0x7fffffff;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
-            const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-            argmax_merge(best, bi, v2, i2);
+        best = lane < kArgmaxThreads / 32 ? sv[lane] : -INFINITY;
+        bi = lane < kArgmaxThreads / 32 ? si[lane] : 0x7fffffff;
+        argmax_warp(best, bi);
+        if (lane == 0) {
+            part_v = best;
+            part_i = bi;
         }
+    }
+    cluster_sync();  // every CTA's partial is written
+    if (rank == 0 && warp == 0) {
+        best = lane < kArgmaxCluster ? dsmem_ld(&part_v, lane) : -INFINITY;
+        bi = lane < kArgmaxCluster ? dsmem_ld(&part_i, lane) : 0x7fffffff;
+        argmax_warp(best, bi);
         if (lane == 0) {
             ids[row] = bi == 0x7fffffff ? 0 : bi;  // all -inf / NaN rows give index 0
             if (adv) adv[row] += 1;
             if (adv2) adv2[row] += 1;
         }
     }
+    cluster_sync();  // no CTA leaves while CTA 0 may still read its partial
 }
 
 }  // namespace kvb

@@ -1415,10 +1415,12 @@ int kvb_attention_decode_noalloc(kvb_stream_t stream, const void* q, size_t q_ro
 int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
                    int32_t* ids, int32_t* advance, int32_t* advance2) {
     KVB_CHECK(vocab > 0 && fits_i32(vocab), "argmax: vocab %zu out of range", vocab);
-    KVB_CHECK(fits_i32(rows), "argmax: rows %zu out of range", rows);
+    KVB_CHECK(rows <= 0x7fffffff / kArgmaxCluster, "argmax: rows %zu out of range", rows);
     if (rows == 0) return KVB_OK;
     const int vec4 = vocab % 4 == 0 && aligned(logits, 16);
-    argmax_kernel<<<(unsigned)rows, 512, 0, stream>>>(logits, (int)vocab, ids, advance, advance2, vec4);
+    const size_t slice = ((vocab + kArgmaxCluster - 1) / kArgmaxCluster + 3) & ~(size_t)3;
+    argmax_kernel<<<(unsigned)(rows * kArgmaxCluster), kArgmaxThreads, 0, stream>>>(
+        logits, (int)vocab, (int)slice, ids, advance, advance2, vec4);
     KVB_CHECK_LAUNCH("argmax launch");
     return KVB_OK;
 }

@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "kvasir_b200.h"  // include/ (on the compiler's include path)
 
@@ -117,6 +118,45 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// ---------------------------------------------------------------- thread-block clusters
+// Distributed shared memory: the same variable in CTA `rank` of this cluster.
+template <typename T>
+__device__ __forceinline__ T dsmem_ld(const T* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(remote)
+                 : "r"((uint32_t)__cvta_generic_to_shared(local)), "r"(rank));
+    T v;
+    static_assert(sizeof(T) == 4, "32-bit values only");
+    uint32_t u;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(u) : "r"(remote));
+    memcpy(&v, &u, 4);
+    return v;
+}
+// The address of `local` in CTA `rank` of this cluster, and a 32-bit load from such an address.
+__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(remote)
+                 : "r"((uint32_t)__cvta_generic_to_shared(local)), "r"(rank));
+    return remote;
+}
+__device__ __forceinline__ uint32_t dsmem_ld_at(uint32_t addr) {
+    uint32_t u;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(u) : "r"(addr));
+    return u;
+}
+// Cluster-wide barrier with release / acquire semantics for shared memory.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+                 ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
 }
 
 // Time limit of every device-side wait.  Copies finish in microseconds; the

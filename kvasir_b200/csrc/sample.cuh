@@ -82,44 +82,6 @@ __device__ __forceinline__ float block_sum_f(float v, float* red) {
     return warp_sum(v);
 }
 
-// Distributed shared memory: the same variable in CTA `rank` of this cluster.
-template <typename T>
-__device__ __forceinline__ T dsmem_ld(const T* local, uint32_t rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
-                 : "=r"(remote)
-                 : "r"((uint32_t)__cvta_generic_to_shared(local)), "r"(rank));
-    T v;
-    static_assert(sizeof(T) == 4, "32-bit values only");
-    uint32_t u;
-    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(u) : "r"(remote));
-    memcpy(&v, &u, 4);
-    return v;
-}
-// The address of `local` in CTA `rank` of this cluster, and a 32-bit load from such an address.
-__device__ __forceinline__ uint32_t dsmem_addr(const void* local, uint32_t rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
-                 : "=r"(remote)
-                 : "r"((uint32_t)__cvta_generic_to_shared(local)), "r"(rank));
-    return remote;
-}
-__device__ __forceinline__ uint32_t dsmem_ld_at(uint32_t addr) {
-    uint32_t u;
-    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(u) : "r"(addr));
-    return u;
-}
-// Cluster-wide barrier with release / acquire semantics for shared memory.
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
-                 ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
 // Weights in 32-bit fixed point (w <= 1): every histogram, mass and running
 // sum below is an exact integer, independent of the order the GPU adds in.
 // Histograms hold the high and low 16 bits of the weights in two u32 arrays

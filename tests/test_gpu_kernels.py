@@ -375,6 +375,34 @@ def test_argmax_matches_oracle(g):
     np.testing.assert_array_equal(ids.cpu().numpy(), O.argmax(logits, rows, vocab))
 
 
+@pytest.mark.parametrize("vocab,offset", [(1, 0), (5, 0), (8, 0), (9, 0), (4003, 0),
+                                          (128256, 0), (128256, 1), (128257, 0), (300001, 0)])
+def test_argmax_slices_and_ties(g, vocab, offset):
+    """Each row is scanned by several CTAs, one slice each: ties and maxima placed on
+    and across slice boundaries, the scalar path (odd vocab, unaligned rows)."""
+    rng = np.random.default_rng(vocab + offset)
+    rows = 6
+    logits = rng.normal(0, 3, (rows, vocab)).astype(np.float32)
+    logits[0, -1] = 50.0                             # maximum in the last slice
+    logits[1, vocab // 2:] = 60.0                    # tie spanning the later slices
+    logits[2, :] = -np.inf
+    logits[2, -1] = -1e30                            # the only finite value, at the end
+    logits[3, ::2] = np.nan                          # NaN never wins
+    logits[4, :] = 7.0                               # all equal: index 0
+    logits[5, :] = -np.inf
+    logits[5, 0] = np.nan                            # only NaN and -inf: index 0
+    flat = torch.zeros(rows * vocab + offset, dtype=torch.float32, device="cuda")
+    view = flat[offset:]
+    view.copy_(torch.from_numpy(logits.ravel()).cuda())
+    ids = torch.empty(rows, dtype=torch.int32, device="cuda")
+    g.argmax(view, rows, vocab, ids)
+    want = O.argmax(logits, rows, vocab)
+    np.testing.assert_array_equal(ids.cpu().numpy(), want)
+    # argmax is one launch: repeated calls give the same ids
+    g.argmax(view, rows, vocab, ids)
+    np.testing.assert_array_equal(ids.cpu().numpy(), want)
+
+
 def test_argmax_advances_counters(g):
     logits = torch.zeros(4, 10, device="cuda")
     ids = torch.empty(4, dtype=torch.int32, device="cuda")

@@ -191,8 +191,11 @@ def test_linear_matches_numpy():
 
 
 def test_argmax_first_index_and_nan():
-    logits = np.array([[1, 3, 3, 2], [np.nan, -1, -1, np.nan], [-np.inf] * 4], np.float32)
-    np.testing.assert_array_equal(O.argmax(logits, 3, 4), [1, 1, 0])
+    logits = np.array([[1, 3, 3, 2], [np.nan, -1, -1, np.nan], [-np.inf] * 4,
+                       [np.nan, -np.inf, -np.inf, np.nan], [-np.inf, -np.inf, -np.inf, -3e38]],
+                      np.float32)
+    # nothing above -inf: index 0, whatever the row holds
+    np.testing.assert_array_equal(O.argmax(logits, 5, 4), [1, 1, 0, 0, 3])
 
 
 def test_threads_do_not_change_results():
