@@ -124,6 +124,22 @@ def test_batched_decode_edge_lengths(g):
         assert_close(got, want, RTOL, ATOL, f"decode edges ws={use_ws}")
 
 
+@pytest.mark.parametrize("lens", [[1100], [0, 1, 70, 1100], [1, 2, 1100, 1099], [400, 1100]])
+def test_batched_decode_few_sequences_five_chunks(g, lens):
+    """Few sequences of ~1100 keys: five 256-key chunks each and the combine pass,
+    beside sequences shorter than one chunk or one tile, and one with no keys."""
+    lens = np.array(lens, np.int32)
+    n_q, n_kv, hd = 32, 8, 64
+    rng = np.random.default_rng(int(lens.sum()))
+    q, kc, vc, max_seq, per = _batched_case(rng, lens, max_seq=1280)
+    want = O.attention_decode(q, n_q * hd, kc, vc, lens, n_q, n_kv, hd, max_seq, 1 / 8.0)
+    want = want.reshape(len(lens), -1)
+    want[lens == 0] = 0.0
+    got = _run_batched(g, q, kc, vc, lens, n_q, n_kv, hd, max_seq, per)
+    assert_close(got, want, RTOL, ATOL, "decode five chunks")
+    assert g.device_error() == 0
+
+
 @pytest.mark.parametrize("group", [1, 2, 8, 16])
 def test_batched_decode_group_sizes(g, group):
     n_kv, hd = 2, 64
@@ -312,6 +328,7 @@ def test_bounded_wait_selftest_keeps_context_usable(g):
     ([1024] * 32, 32, 8, True),
     ([5, 200, 4096], 8, 8, True),
     ([130, 1], 64, 4, True),
+    ([1, 70, 1100], 32, 8, True),
 ])
 def test_rope_attention_decode_equals_rope_then_decode(g, dtype, lens, n_q, n_kv, with_ws):
     """kvb_rope_attention_decode == kvb_rope_kv_append_batched (positions lens - 1) +
