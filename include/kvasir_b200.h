@@ -305,9 +305,9 @@ int kvb_rope_attention_decode_paged(kvb_stream_t stream, const void* qkv, size_t
                                     size_t workspace_len, int dtype);
 
 /* Greedy sampling: ids[r] = first index of the maximum of logits[r, 0:vocab)
- * (NaN never wins).  If advance is non-NULL, advance[r] += 1 for every r and,
- * if advance2 is non-NULL, advance2[r] += 1 (position / length counters of
- * the decode loop). */
+ * (NaN never wins; a row with no value above -inf gives 0).  If advance is
+ * non-NULL, advance[r] += 1 for every r and, if advance2 is non-NULL,
+ * advance2[r] += 1 (position / length counters of the decode loop). */
 int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
                    int32_t* ids, int32_t* advance, int32_t* advance2);
 
