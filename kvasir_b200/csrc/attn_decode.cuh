@@ -97,7 +97,12 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     __shared__ uint64_t bars[kDecWarps];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
-    const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    // Grid (kv head, sequence, chunk slot); the slot counts chunks from the END of the
+    // sequence, and the last slot holds every sequence's last, partial chunk.  CTAs are
+    // dispatched slot by slot, so full chunks go first and the final wave holds the
+    // shortest pieces of work (longest first: a shorter tail).
+    const int kvh = blockIdx.x, b = blockIdx.y;
+    const int from_end = (int)gridDim.z - 1 - (int)blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
     const int G = a.group;
@@ -106,11 +111,12 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     const int n_chunks = (len + a.chunk_keys - 1) / a.chunk_keys;
     T* outb = reinterpret_cast<T*>(a.out) + (size_t)b * a.out_row_stride + (size_t)kvh * G * 64;
     if (len == 0) {  // no keys: defined as a zero output row
-        if (chunk == 0)
+        if (from_end == 0)
             for (int i = threadIdx.x; i < G * 64; i += blockDim.x) outb[i] = Elem<T>::from_f(0.f);
         return;
     }
-    if (chunk >= n_chunks) return;
+    if (from_end >= n_chunks) return;
+    const int chunk = n_chunks - 1 - from_end;
     const int key_begin = chunk * a.chunk_keys;
     const int key_end = min(len, key_begin + a.chunk_keys);
 

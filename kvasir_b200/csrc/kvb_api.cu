@@ -367,11 +367,13 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
     } else {
         a.ws = static_cast<float*>(L.ws);
     }
+    // chunks are the grid's z extent: at most 65535 (wider chunks need less workspace)
+    if ((L.max_len + ck - 1) / ck > 65535) ck = (int)(((L.max_len + 65534) / 65535 + 255) / 256 * 256);
     a.chunk_keys = ck;
     a.max_chunks = (int)((L.max_len + ck - 1) / ck);
     if (a.max_chunks < 1) a.max_chunks = 1;
 
-    dim3 grid(a.max_chunks, (unsigned)L.n_kv, (unsigned)L.n_seq);
+    dim3 grid((unsigned)L.n_kv, (unsigned)L.n_seq, a.max_chunks);
 #define KVB_DECODE_LAUNCH(T, ROPE)                                                   \
     do {                                                                             \
         set_max_smem(attn_decode_kernel<T, ROPE>, kDecSmemBytes);                    \
