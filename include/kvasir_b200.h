@@ -173,6 +173,14 @@ int kvb_rope_kv_append_prefill(kvb_stream_t stream, void* qkv, size_t qkv_len,
                                size_t n_q, size_t n_kv, size_t head_dim, size_t max_seq,
                                int dtype);
 
+/* kvb_embedding_gather(ids, table, x) followed by kvb_rmsnorm(x, w, out) (the
+ * first norm of a decode step: Gpu::embedding_gather, kernels.rs:59-88, then
+ * Gpu::rmsnorm, kernels.rs:90-121), in one launch for decode-sized batches;
+ * x and out are bit-equal to the two calls.  x is [t, hidden] (the residual
+ * stream), out [t, hidden]; ids outside the table give zero rows. */
+int kvb_embedding_rmsnorm(kvb_stream_t stream, const int32_t* ids, size_t t, const void* table,
+                          size_t table_len, const void* w, size_t w_len, void* x, size_t x_len,
+                          void* out, size_t out_len, size_t hidden, float eps, int dtype);
 /* kvb_add_inplace(x, y) followed by kvb_rmsnorm(x, w, out): the residual
  * stream x is updated in place and its normalised copy written to out. */
 int kvb_add_rmsnorm(kvb_stream_t stream, void* x, size_t x_len, const void* y, size_t y_len,

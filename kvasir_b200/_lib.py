@@ -46,6 +46,8 @@ SIGNATURES = {
     "kvb_device_error": (_int, [C.POINTER(C.c_uint32)]),
     "kvb_embedding_gather": (_int, [_p, _p, _sz, _p, _sz, _p, _sz, _sz, _int]),
     "kvb_rmsnorm": (_int, [_p, _p, _sz, _p, _sz, _p, _sz, _sz, _sz, C.c_float, _int]),
+    "kvb_embedding_rmsnorm": (_int, [_p, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _p, _sz, _sz,
+                                     C.c_float, _int]),
     "kvb_rope_inplace": (_int, [_p, _p, _sz, _p, _sz, _p, _sz, _sz, _sz, _sz, _sz, _sz, _int]),
     "kvb_silu_mul": (_int, [_p, _p, _sz, _p, _sz, _sz, _sz, _int]),
     "kvb_add_inplace": (_int, [_p, _p, _sz, _p, _sz, _int]),

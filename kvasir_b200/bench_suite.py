@@ -127,22 +127,39 @@ def cfg1(args):
         g.attention(qkv, kc, vc, out, 1, pos, nq, nkv, hd, max_seq, workspace=ws)
         g.silu_mul(gu, act, 1, I)
 
-    for _ in range(5):
-        chain()
-    eager_ms = time_loop(chain, 200)
-    stream = torch.cuda.Stream()
-    stream.wait_stream(torch.cuda.current_stream())
-    graph = torch.cuda.CUDAGraph()
-    g.stream = stream
-    with torch.cuda.stream(stream):
-        chain()  # warm on the capture stream
-        torch.cuda.synchronize()
-        with torch.cuda.graph(graph, stream=stream):
-            chain()
-    g.stream = torch.cuda.current_stream()
-    for _ in range(5):
-        graph.replay()
-    graph_ms = time_loop(graph.replay, 500)
+    # The same chain through the fused entry points: embedding + RMSNorm in one launch,
+    # RoPE + KV append + decode attention in one (the new key at lens - 1 = pos).
+    lens = torch.tensor([pos + 1], dtype=torch.int32, device="cuda")
+    qkv_u = qkv0.clone()  # read unrotated by the fused attention, never modified
+    dws = torch.empty(max(16, g.attention_decode_workspace_bytes(1, pos + 1, nq, nkv, hd)),
+                      dtype=torch.uint8, device="cuda")
+
+    def chain_fused():
+        g.embedding_rmsnorm(ids, table, w, x, h, H, 1e-5)
+        g.rope_attention_decode(qkv_u, cos, sin, kc, vc, nkv * max_seq * hd, lens, pos + 1, nq,
+                                nkv, hd, max_seq, out, nq * hd, workspace=dws)
+        g.silu_mul(gu, act, 1, I)
+
+    def timed(fn):
+        for _ in range(5):
+            fn()
+        eager = time_loop(fn, 200)
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        g.stream = stream
+        with torch.cuda.stream(stream):
+            fn()  # warm on the capture stream
+            torch.cuda.synchronize()
+            with torch.cuda.graph(graph, stream=stream):
+                fn()
+        g.stream = torch.cuda.current_stream()
+        for _ in range(5):
+            graph.replay()
+        return eager, time_loop(graph.replay, 500)
+
+    eager_ms, graph_ms = timed(chain)
+    fused_eager_ms, fused_graph_ms = timed(chain_fused)
     alg = (2 * H * 2) + (3 * H * 2) + (40 * hd * 2 * 2 + 8 * hd * 2 * 2 + 256 * 4) + \
           (513 * nkv * hd * 4 + 2 * nq * hd * 2) + (3 * I * 2)
     # CPU: the same chain through the oracle
@@ -168,6 +185,13 @@ def cfg1(args):
            "launches_per_chain": 5 + (1 if ws.numel() > 16 else 0),
            "alg_bytes": alg, "gbs_informative": alg / (graph_ms * 1e-3) / 1e9,
            "cpu_oracle_us": cpu_us, "cpu_threads": _cpu_threads()})
+    _emit({"workload": "cfg1 fused: the same chain through kvb_embedding_rmsnorm, "
+                       "kvb_rope_attention_decode and kvb_silu_mul",
+           "metric": "us per chain", "value": fused_graph_ms * 1e3,
+           "eager_us": fused_eager_ms * 1e3, "graph_us": fused_graph_ms * 1e3, "unit": "us",
+           "higher_is_better": False,
+           "launches_per_chain": 3 + (1 if dws.numel() > 16 else 0),
+           "alg_bytes": alg, "gbs_informative": alg / (fused_graph_ms * 1e-3) / 1e9})
 
 
 # ----------------------------------------------------------------------------- config 2

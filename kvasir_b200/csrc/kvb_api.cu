@@ -634,6 +634,45 @@ int kvb_rmsnorm(kvb_stream_t stream, const void* x, size_t x_len, const void* w,
                                  dtype);
 }
 
+int kvb_embedding_rmsnorm(kvb_stream_t stream, const int32_t* ids, size_t t, const void* table,
+                          size_t table_len, const void* w, size_t w_len, void* x, size_t x_len,
+                          void* out, size_t out_len, size_t hidden, float eps, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(hidden > 0, "embedding_rmsnorm: hidden must be > 0");
+    KVB_CHECK(x_len == t * hidden, "embedding_rmsnorm: x has %zu elems, want %zux%zu", x_len, t,
+              hidden);
+    KVB_CHECK(out_len == t * hidden, "embedding_rmsnorm: out has %zu elems, want %zux%zu", out_len,
+              t, hidden);
+    KVB_CHECK(w_len == hidden, "embedding_rmsnorm: w has %zu elems, want %zu", w_len, hidden);
+    KVB_CHECK(table_len % hidden == 0,
+              "embedding_rmsnorm: table len %zu not a multiple of hidden %zu", table_len, hidden);
+    KVB_CHECK(fits_i32(hidden) && fits_i32(t), "embedding_rmsnorm: a dimension does not fit in i32");
+    const size_t vocab = table_len / hidden;
+    KVB_CHECK(fits_i32(vocab), "embedding_rmsnorm: vocab=%zu does not fit in i32", vocab);
+    if (t == 0) return KVB_OK;
+    const size_t chunks = hidden / 8;
+    // the rows kvb_rmsnorm normalises with rmsnorm_row_kernel: one launch
+    const bool fused = embedding_rmsnorm_fused(t, hidden) && aligned(table, 16) &&
+                       aligned(w, 16) && aligned(x, 16) && aligned(out, 16);
+    if (!fused) {  // the same two kernels as the unfused calls
+        const int st = kvb_embedding_gather(stream, ids, t, table, table_len, x, x_len, hidden,
+                                            dtype);
+        if (st) return st;
+        return kvb_rmsnorm(stream, x, x_len, w, w_len, out, out_len, t, hidden, eps, dtype);
+    }
+    const float ih = 1.0f / (float)hidden;
+    if (dtype == KVB_BF16)
+        embedding_rmsnorm_row_kernel<__nv_bfloat16><<<(unsigned)t, (unsigned)chunks, 0, stream>>>(
+            ids, (const uint4*)table, (const uint4*)w, (uint4*)x, (uint4*)out, (int)chunks,
+            (int)vocab, ih, eps);
+    else
+        embedding_rmsnorm_row_kernel<__half><<<(unsigned)t, (unsigned)chunks, 0, stream>>>(
+            ids, (const uint4*)table, (const uint4*)w, (uint4*)x, (uint4*)out, (int)chunks,
+            (int)vocab, ih, eps);
+    KVB_CHECK_LAUNCH("embedding_rmsnorm launch");
+    return KVB_OK;
+}
+
 int kvb_add_rmsnorm(kvb_stream_t stream, void* x, size_t x_len, const void* y, size_t y_len,
                     const void* w, size_t w_len, void* out, size_t out_len, size_t rows,
                     size_t hidden, float eps, int dtype) {

@@ -119,11 +119,12 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
         (is_lib) ? ++lib : ++own;  \
     } while (0)
 
-    STEP(kvb_embedding_gather(s, d->at<int32_t>(L.ids_in), B, d->embed, (size_t)c.vocab * H,
-                              d->at(L.x), B * H, H, dt),
+    // embedding gather + layer 0's attention norm (one launch for decode-sized batches)
+    STEP(kvb_embedding_rmsnorm(s, d->at<int32_t>(L.ids_in), B, d->embed, (size_t)c.vocab * H,
+                               d->attn_norm[0], H, d->at(L.x), B * H, d->at(L.h), B * H, H, c.eps,
+                               dt),
          false);
-    STEP(kvb_rmsnorm(s, d->at(L.x), B * H, d->attn_norm[0], H, d->at(L.h), B * H, B, H, c.eps, dt),
-         false);
+    if (!kvb::embedding_rmsnorm_fused(B, H)) ++own;  // it ran as two launches
     for (int l = 0; l < c.n_layers; ++l) {
         STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->w_qkv[l], qkvd * H, d->at(L.qkv), B * qkvd,
                         B, H, qkvd, dt, 0),

@@ -22,6 +22,12 @@ inline bool valid_dtype(int d) { return d == KVB_BF16 || d == KVB_F16; }
 
 // Streaming multiprocessors of the current device (cached per device).
 int num_sms();
+// kvb_embedding_rmsnorm runs as one launch (else as the gather and the norm): the
+// rows kvb_rmsnorm normalises with its per-row kernel, buffers 16-byte aligned.
+inline bool embedding_rmsnorm_fused(size_t rows, size_t hidden) {
+    return hidden % 8 == 0 && (hidden / 8) % 32 == 0 && hidden / 8 <= 32 * 16 &&
+           rows <= (size_t)num_sms() * 4;
+}
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
 // dims / box are innermost-first; strides_bytes has rank-1 entries (the

@@ -199,6 +199,45 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_kernel(uint4* __restrict__ x
     out[row * chunks + c] = pack8<T>(v);
 }
 
+// Embedding gather fused with the RMSNorm that follows it (the first norm of a
+// decode step): x row r = table[ids[r]] (a zero row for an id outside the table,
+// as embedding_gather_vec_kernel), out row r = RMSNorm(x row r) * w with the
+// arithmetic of rmsnorm_row_kernel<T, false>, so x and out equal the two-launch
+// form bit for bit.  One CTA per row, one 16-byte chunk per thread.
+template <typename T>
+__global__ void __launch_bounds__(1024) embedding_rmsnorm_row_kernel(
+    const int32_t* __restrict__ ids, const uint4* __restrict__ table, const uint4* __restrict__ w,
+    uint4* __restrict__ x, uint4* __restrict__ out, int chunks, int vocab, float inv_hidden,
+    float eps) {
+    __shared__ float red[32];
+    const size_t row = blockIdx.x;
+    const int c = threadIdx.x;
+    const int lane = c & 31, warp = c >> 5;
+    const int id = ids[row];
+    uint4 e = make_uint4(0, 0, 0, 0);
+    if (id >= 0 && id < vocab) e = table[(size_t)id * chunks + c];
+    x[row * chunks + c] = e;
+    float v[8], wf[8];
+    unpack8<T>(e, v);
+    unpack8<T>(w[c], wf);
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) ss += v[k] * v[k];
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    if (warp == 0) {
+        float r = lane < (int)(blockDim.x >> 5) ? red[lane] : 0.f;
+        r = warp_sum(r);
+        if (lane == 0) red[0] = r;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] * inv_hidden + eps);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = v[k] * inv * wf[k];
+    out[row * chunks + c] = pack8<T>(v);
+}
+
 // Any width, any alignment: one CTA per row, two passes over the row.
 template <typename T, bool kAdd>
 __global__ void __launch_bounds__(256) rmsnorm_generic_kernel(T* __restrict__ x,

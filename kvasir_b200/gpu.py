@@ -124,6 +124,14 @@ class Gpu:
         check(self._lib.kvb_rmsnorm(self._s, _ptr(x), x.numel(), _ptr(w), w.numel(), _ptr(out),
                                     out.numel(), rows, hidden, eps, dtype_tag(x)))
 
+    def embedding_rmsnorm(self, ids, table, w, x, out, hidden, eps):
+        """kvb_embedding_rmsnorm: embedding_gather into x, then rmsnorm(x, w) into out,
+        in one launch for decode-sized batches (bit-equal to the two calls)."""
+        check(self._lib.kvb_embedding_rmsnorm(self._s, _ptr(ids), ids.numel(), _ptr(table),
+                                              table.numel(), _ptr(w), w.numel(), _ptr(x),
+                                              x.numel(), _ptr(out), out.numel(), hidden, eps,
+                                              dtype_tag(table)))
+
     def rope_inplace(self, qkv, cos, sin, t, pos0, n_q, n_kv, head_dim):
         """kernels.rs:124-169"""
         check(self._lib.kvb_rope_inplace(self._s, _ptr(qkv), qkv.numel(), _ptr(cos), cos.numel(),

@@ -57,6 +57,34 @@ def test_embedding_prefill_rows(g):
     np.testing.assert_array_equal(host_bits(out), O.embedding_gather(ids, table, hidden))
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("vocab,hidden,ids", [
+    (128256, 2048, [5]),                                    # batch-1 decode: one launch
+    (128256, 2048, list(range(0, 128256, 4009))),           # 32 rows
+    (1000, 256, [-1, 3, 1000, 999]),                        # ids outside the table: zero rows
+    (300, 4096, [7, 0, 299]),                               # 512 chunks, the widest fused row
+    (300, 4104, [7, 0, 299]),                               # wider: the two kernels
+    (50, 300, [7, 0, 49]),                                  # odd width: the two kernels
+    (40, 256, list(range(40)) * 16),                        # 640 rows: the two kernels
+])
+def test_embedding_rmsnorm_equals_gather_then_rmsnorm(g, dtype, vocab, hidden, ids):
+    rng = np.random.default_rng(hidden + len(ids))
+    table = O.uniform16(rng, vocab * hidden, 1.0, dtype)
+    w = O.uniform16(rng, hidden, 1.5, dtype)
+    ids = np.array(ids, np.int32)
+    d_ids, d_table, d_w = torch.from_numpy(ids).cuda(), dev(table, dtype), dev(w, dtype)
+    tdt = d_table.dtype
+    n = len(ids) * hidden
+    x_a, out_a = torch.full((n,), 3.0, dtype=tdt, device="cuda"), torch.empty(n, dtype=tdt, device="cuda")
+    g.embedding_rmsnorm(d_ids, d_table, d_w, x_a, out_a, hidden, 1e-5)
+    x_b, out_b = torch.empty(n, dtype=tdt, device="cuda"), torch.empty(n, dtype=tdt, device="cuda")
+    g.embedding_gather(d_ids, d_table, x_b, hidden)
+    g.rmsnorm(x_b, d_w, out_b, len(ids), hidden, 1e-5)
+    np.testing.assert_array_equal(host_bits(x_a), O.embedding_gather(ids, table, hidden))
+    np.testing.assert_array_equal(host_bits(x_a), host_bits(x_b))
+    np.testing.assert_array_equal(host_bits(out_a), host_bits(out_b))
+
+
 # ------------------------------------------------------------------ rmsnorm
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("rows,hidden", [(5, 2048), (3, 100), (1, 2048), (7, 4096), (2, 8),
