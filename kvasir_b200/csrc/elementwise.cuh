@@ -133,7 +133,7 @@ __device__ __forceinline__ void argmax_warp(float& v, int& i) {
 // One 8-CTA cluster per row: CTA r scans the row's r-th contiguous slice (`slice`
 // elements, a multiple of 4) with kArgmaxUnroll independent loads in flight per
 // thread, and CTA 0 merges the eight partials through distributed shared memory.
-// A 128,256-token row is 64 KB per SM, one round of loads (one CTA per row kept a
+// A 128,256-token row is 64 KB per SM, one batch of loads (one CTA per row kept a
 // single SM's loads waiting on L2 latency ~60 times in a row).
 constexpr int kArgmaxCluster = 8;
 constexpr int kArgmaxThreads = 512;
