@@ -85,6 +85,19 @@ def test_shape_errors_are_reported_not_launched():
     assert st == L.KVB_ERR_SHAPE and "silu_mul" in msg
     st, msg = _status(lib.kvb_rmsnorm, None, fake, 8, fake, 4, fake, 8, 2, 4, 1e-5, 7)
     assert st == L.KVB_ERR_SHAPE and "dtype" in msg
+    # embedding + norm: w must be one row, x and out t rows, the table whole rows
+    st, msg = _status(lib.kvb_embedding_rmsnorm, None, fake, 2, fake, 10 * 256, fake, 255, fake,
+                      2 * 256, fake, 2 * 256, 256, 1e-5, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "w has 255" in msg
+    st, msg = _status(lib.kvb_embedding_rmsnorm, None, fake, 2, fake, 10 * 256, fake, 256, fake,
+                      3 * 256, fake, 2 * 256, 256, 1e-5, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "x has 768" in msg
+    st, msg = _status(lib.kvb_embedding_rmsnorm, None, fake, 2, fake, 10 * 256 + 1, fake, 256,
+                      fake, 2 * 256, fake, 2 * 256, 256, 1e-5, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "multiple of hidden" in msg
+    # argmax: eight CTAs per row, so rows must keep the grid within 2^31 - 1 CTAs
+    st, msg = _status(lib.kvb_argmax_f32, None, fake, 1 << 28, 10, fake, None, None)
+    assert st == L.KVB_ERR_SHAPE and "rows" in msg
 
 
 @pytest.mark.parametrize("scaled", [True, False])
