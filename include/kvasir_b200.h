@@ -259,11 +259,19 @@ int kvb_attention_decode_paged(kvb_stream_t stream, const void* q, size_t q_row_
  * all belongs to long-lived weight / cache structs (the reference's own rule
  * for its launch wrappers), or code running where an allocation's implicit
  * device synchronisation is not acceptable.  The call allocates and frees
- * nothing.  Requests whose partials need more than KVB_NOALLOC_SCRATCH_BYTES
- * (kvb_attention_decode_workspace_bytes) return KVB_ERR_SHAPE.  The first call
+ * nothing.  Its output equals kvb_attention_decode's, bit for bit, when that
+ * call is given a workspace of kvb_attention_decode_workspace_bytes.  Calls
+ * that take the split-KV kernel (head_dim 64, n_q / n_kv <= 16, 16-byte aligned
+ * q / kc / vc, row strides multiples of 8 elements, seq_stride a multiple of
+ * 64) and whose partials need more than KVB_NOALLOC_SCRATCH_BYTES
+ * (kvb_attention_decode_workspace_bytes) return KVB_ERR_SHAPE; other shapes run
+ * kvb_attention_decode's general kernel, which needs no scratch.  The first call
  * on a device looks up the array's device address (cudaGetSymbolAddress) with
- * that device current; make that first call before any stream capture.  All
- * calls on a device share the one array: calls that may overlap on the GPU
+ * that device current and keeps it with the id of the device's CUDA context;
+ * when that context changes (a cudaDeviceReset and a new context) the next call
+ * looks it up again.  Make the first call on a device, and the first after a
+ * reset, outside any stream capture: inside one it returns KVB_ERR_UNSUPPORTED.
+ * All calls on a device share the one array: calls that may overlap on the GPU
  * (different streams, or graphs replayed concurrently) race on it. */
 #define KVB_NOALLOC_SCRATCH_BYTES (8u << 20)
 int kvb_attention_decode_noalloc(kvb_stream_t stream, const void* q, size_t q_row_stride,
@@ -281,6 +289,17 @@ int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, 
                           const void* vc, size_t cache_len, void* out, size_t out_len,
                           size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
                           size_t head_dim, size_t max_seq, int dtype);
+
+/* kvb_attention_prefill with f32 output rows: the kernel's results before the
+ * one rounding to the 16-bit type (rounding them to nearest even gives
+ * kvb_attention_prefill's output bit for bit).  For callers that feed
+ * attention into f32 work, and for measuring the kernel's own error.  head_dim
+ * 64 and 16-byte aligned buffers only (else KVB_ERR_UNSUPPORTED).  New: the
+ * reference's attention (engine/src/gpu/kernels.rs:294-371) writes 16-bit rows. */
+int kvb_attention_prefill_f32(kvb_stream_t stream, const void* qkv, size_t qkv_len, const void* kc,
+                              const void* vc, size_t cache_len, float* out, size_t out_len,
+                              size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
+                              size_t head_dim, size_t max_seq, int dtype);
 
 /* Decode step of the attention block in one launch: kvb_rope_kv_append_batched
  * followed by kvb_attention_decode, bit for bit, where the new token of

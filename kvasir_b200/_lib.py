@@ -18,6 +18,7 @@ HEADER = os.path.join(os.path.dirname(HERE), "include", "kvasir_b200.h")
  KVB_ERR_IO) = range(7)
 KVB_BF16, KVB_F16 = 0, 1
 KVB_CKPT_BF16, KVB_CKPT_F16, KVB_CKPT_F32, KVB_CKPT_OTHER = range(4)
+KVB_NOALLOC_SCRATCH_BYTES = 8 << 20  # include/kvasir_b200.h
 
 _sz = C.c_size_t
 _p = C.c_void_p
@@ -82,6 +83,8 @@ SIGNATURES = {
     "kvb_attention_decode_noalloc": (_int, [_p, _p, _sz, _p, _p, _sz, _sz, _p, _sz, _sz, _sz, _sz,
                                             _sz, _sz, C.c_float, _p, _sz, _int]),
     "kvb_attention_prefill": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _sz, _sz, _sz, _sz, _sz, _sz,
+                                     _sz, _sz, _int]),
+    "kvb_attention_prefill_f32": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _sz, _sz, _sz, _sz, _sz, _sz,
                                      _sz, _sz, _int]),
     "kvb_argmax_f32": (_int, [_p, _p, _sz, _sz, _p, _p, _p]),
     "kvb_rope_attention_decode_paged": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _p, _sz, _p, _sz, _sz,

@@ -130,7 +130,9 @@ __device__ __forceinline__ void split_bf16_pair(float p0, float p1, uint32_t& hi
     lo = Elem<__nv_bfloat16>::pack(r0, r1);
 }
 
-template <typename T>
+// kOutF32: the rows are written as f32 (a.out holds floats), the values that the
+// 16-bit form rounds once.
+template <typename T, bool kOutF32 = false>
 // 2 CTAs x 6 warps: three warps on each SM sub-partition (16K registers each),
 // at most 168 registers a thread.
 __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
@@ -443,8 +445,8 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
                 tc_fence_after();
                 const float inv = 1.f / l;
                 const bool valid = row < rows_valid;
-                T* orow = reinterpret_cast<T*>(a.out) +
-                          ((size_t)seq * a.t + q0 + row) * a.out_row_stride + (size_t)h * 64;
+                const size_t orow_off =
+                    ((size_t)seq * a.t + q0 + row) * a.out_row_stride + (size_t)h * 64;
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     float o[32];
@@ -456,7 +458,15 @@ __global__ void __launch_bounds__(kPfThreads, kPfCtasPerSm)
                             float f[8];
 #pragma unroll
                             for (int e = 0; e < 8; ++e) f[e] = o[8 * k + e] * inv;
-                            *reinterpret_cast<uint4*>(orow + 32 * hf + 8 * k) = pack8<T>(f);
+                            if constexpr (kOutF32) {
+                                float4* orow = reinterpret_cast<float4*>(
+                                    reinterpret_cast<float*>(a.out) + orow_off + 32 * hf + 8 * k);
+                                orow[0] = make_float4(f[0], f[1], f[2], f[3]);
+                                orow[1] = make_float4(f[4], f[5], f[6], f[7]);
+                            } else {
+                                T* orow = reinterpret_cast<T*>(a.out) + orow_off;
+                                *reinterpret_cast<uint4*>(orow + 32 * hf + 8 * k) = pack8<T>(f);
+                            }
                         }
                     }
                 }

@@ -291,6 +291,20 @@ static int decode_chunk_keys(size_t n_seq, size_t n_kv, size_t max_len) {
     return (int)(per_cta * 64);
 }
 
+// kvb_attention_decode takes the split-KV tensor-core kernel (and its workspace)
+// for these shapes and buffers; every other valid call runs the general kernel,
+// which uses no workspace.
+static bool decode_fast_path(const void* q, size_t q_row_stride, const void* kc, const void* vc,
+                             size_t seq_stride, size_t n_seq, size_t n_q, size_t n_kv,
+                             size_t head_dim, size_t max_seq, size_t out_row_stride) {
+    if (n_seq == 0 || n_kv == 0 || n_q % n_kv != 0) return false;
+    const size_t per_seq = n_kv * max_seq * head_dim;
+    const size_t total_rows = ((n_seq - 1) * seq_stride + per_seq) / 64;
+    return head_dim == 64 && n_q / n_kv <= 16 && n_seq <= 65535 && n_kv <= 65535 &&
+           seq_stride % 64 == 0 && q_row_stride % 8 == 0 && out_row_stride % 8 == 0 &&
+           aligned(q, 16) && aligned(kc, 16) && aligned(vc, 16) && fits_i32(total_rows);
+}
+
 static size_t decode_ws_bytes(size_t n_seq, size_t max_len, size_t n_q, size_t n_kv) {
     if (max_len == 0 || n_kv == 0) return 0;
     const size_t ck = (size_t)decode_chunk_keys(n_seq, n_kv, max_len);
@@ -415,7 +429,8 @@ static int launch_generic_attn(kvb_stream_t stream, const GenericAttnArgs& a, si
 static int launch_prefill(kvb_stream_t stream, const void* qkv, const void* kc, const void* vc,
                           void* out, size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
                           size_t max_seq, int dtype, const int32_t* block_table = nullptr,
-                          size_t max_blocks = 0, size_t block_size = 0, size_t pool_len = 0) {
+                          size_t max_blocks = 0, size_t block_size = 0, size_t pool_len = 0,
+                          bool out_f32 = false) {
     const size_t stride = (n_q + 2 * n_kv) * 64;
     CUtensorMap qmap, kmap, vmap;
     {
@@ -458,14 +473,20 @@ static int launch_prefill(kvb_stream_t stream, const void* qkv, const void* kc, 
     a.out = static_cast<uint16_t*>(out);
     a.out_row_stride = (long long)(n_q * 64);
     dim3 grid((unsigned)n_q, (unsigned)n_seq, (unsigned)a.n_qblocks);
+#define KVB_PREFILL_LAUNCH(T, F32)                                                       \
+    do {                                                                                 \
+        set_max_smem(attn_prefill_kernel<T, F32>, kPfSmemBytes);                         \
+        attn_prefill_kernel<T, F32><<<grid, kPfThreads, kPfSmemBytes, stream>>>(qmap, kmap, \
+                                                                                vmap, a); \
+    } while (0)
     if (dtype == KVB_BF16) {
-        set_max_smem(attn_prefill_kernel<__nv_bfloat16>, kPfSmemBytes);
-        attn_prefill_kernel<__nv_bfloat16><<<grid, kPfThreads, kPfSmemBytes, stream>>>(qmap, kmap,
-                                                                                       vmap, a);
+        if (out_f32) KVB_PREFILL_LAUNCH(__nv_bfloat16, true);
+        else KVB_PREFILL_LAUNCH(__nv_bfloat16, false);
     } else {
-        set_max_smem(attn_prefill_kernel<__half>, kPfSmemBytes);
-        attn_prefill_kernel<__half><<<grid, kPfThreads, kPfSmemBytes, stream>>>(qmap, kmap, vmap, a);
+        if (out_f32) KVB_PREFILL_LAUNCH(__half, true);
+        else KVB_PREFILL_LAUNCH(__half, false);
     }
+#undef KVB_PREFILL_LAUNCH
     KVB_CHECK_LAUNCH("attention prefill launch");
     return KVB_OK;
 }
@@ -652,8 +673,7 @@ int kvb_embedding_rmsnorm(kvb_stream_t stream, const int32_t* ids, size_t t, con
     if (t == 0) return KVB_OK;
     const size_t chunks = hidden / 8;
     // the rows kvb_rmsnorm normalises with rmsnorm_row_kernel: one launch
-    const bool fused = embedding_rmsnorm_fused(t, hidden) && aligned(table, 16) &&
-                       aligned(w, 16) && aligned(x, 16) && aligned(out, 16);
+    const bool fused = embedding_rmsnorm_fused(t, hidden, table, w, x, out);
     if (!fused) {  // the same two kernels as the unfused calls
         const int st = kvb_embedding_gather(stream, ids, t, table, table_len, x, x_len, hidden,
                                             dtype);
@@ -1059,13 +1079,9 @@ int kvb_attention_decode(kvb_stream_t stream, const void* q, size_t q_row_stride
     KVB_CHECK(fits_i32(n_seq) && fits_i32(max_seq) && fits_i32(max_len),
               "attention_decode: a dimension does not fit in i32");
     if (n_seq == 0) return KVB_OK;
-    const size_t group = n_q / n_kv;
-    const size_t total_rows = n_seq == 0 ? 0 : ((n_seq - 1) * seq_stride + per_seq) / 64;
-    const bool fast = head_dim == 64 && group <= 16 && n_seq <= 65535 && n_kv <= 65535 &&
-                      seq_stride % 64 == 0 && q_row_stride % 8 == 0 && out_row_stride % 8 == 0 &&
-                      aligned(q, 16) && aligned(kc, 16) && aligned(vc, 16) && fits_i32(total_rows) &&
-                      total_rows < (1ull << 32);
-    if (fast) {
+    const size_t total_rows = ((n_seq - 1) * seq_stride + per_seq) / 64;
+    if (decode_fast_path(q, q_row_stride, kc, vc, seq_stride, n_seq, n_q, n_kv, head_dim, max_seq,
+                         out_row_stride)) {
         DecodeLaunch L;
         L.q = q;
         L.q_row_stride = q_row_stride;
@@ -1215,6 +1231,36 @@ int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, 
     a.out = static_cast<uint16_t*>(out);
     a.out_row_stride = (long long)(n_q * head_dim);
     return launch_generic_attn(stream, a, n_seq * t, dtype);
+}
+
+int kvb_attention_prefill_f32(kvb_stream_t stream, const void* qkv, size_t qkv_len, const void* kc,
+                              const void* vc, size_t cache_len, float* out, size_t out_len,
+                              size_t n_seq, size_t t, size_t pos0, size_t n_q, size_t n_kv,
+                              size_t head_dim, size_t max_seq, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(qkv_len == n_seq * t * (n_q + 2 * n_kv) * head_dim,
+              "attention_prefill_f32: qkv has %zu elems, want %zux%zu", qkv_len, n_seq * t,
+              (n_q + 2 * n_kv) * head_dim);
+    KVB_CHECK(cache_len == n_seq * n_kv * max_seq * head_dim,
+              "attention_prefill_f32: bad cache sizes");
+    KVB_CHECK(out_len == n_seq * t * n_q * head_dim,
+              "attention_prefill_f32: out has %zu elems, want %zux%zu", out_len, n_seq * t,
+              n_q * head_dim);
+    KVB_CHECK(n_kv > 0 && n_q % n_kv == 0,
+              "attention_prefill_f32: n_q %zu not a multiple of n_kv %zu", n_q, n_kv);
+    KVB_CHECK(pos0 + t <= max_seq, "attention_prefill_f32: kv length %zu exceeds max_seq %zu",
+              pos0 + t, max_seq);
+    const size_t stride = (n_q + 2 * n_kv) * head_dim;
+    KVB_CHECK(fits_i32(n_seq * t) && fits_i32(pos0 + t) && fits_i32(stride) &&
+                  fits_i32(n_seq * n_kv),
+              "attention_prefill_f32: a dimension does not fit in i32");
+    if (n_seq == 0 || t == 0) return KVB_OK;
+    if (!(head_dim == 64 && n_seq <= 65535 && aligned(qkv, 16) && aligned(kc, 16) &&
+          aligned(vc, 16) && aligned(out, 16)))
+        return fail(KVB_ERR_UNSUPPORTED,
+                    "attention_prefill_f32: needs head_dim 64 and 16-byte aligned buffers");
+    return launch_prefill(stream, qkv, kc, vc, out, n_seq, t, pos0, n_q, n_kv, max_seq, dtype,
+                          nullptr, 0, 0, 0, true);
 }
 
 int kvb_attention_prefill_paged(kvb_stream_t stream, const void* qkv, size_t qkv_len,
@@ -1398,11 +1444,43 @@ int kvb_attention_decode_paged(kvb_stream_t stream, const void* q, size_t q_row_
 // device array; the device address comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[KVB_NOALLOC_SCRATCH_BYTES];
 
-// Device address of g_noalloc_scratch on the current device, looked up once
-// per device (with that device current) and cached.
-static void* noalloc_scratch_address(int* status) {
+// Unique id of the calling thread's current CUDA context (cuCtxGetId, through
+// the runtime's driver entry points as for the tensor maps); 0 if unavailable.
+static unsigned long long current_context_id() {
+    typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+    typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long*);
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 12000, cudaEnableDefault,
+                                             &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<CtxGetIdFn>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current && get_id && get_current(&ctx) == CUDA_SUCCESS && ctx &&
+        get_id(ctx, &id) == CUDA_SUCCESS)
+        return id;
+    return 0;
+}
+
+// Device address of g_noalloc_scratch on the current device, looked up with
+// that device current on the first call and cached together with the id of
+// the device's context.  A new context on the device (after cudaDeviceReset)
+// holds a new copy of the array, so a changed id repeats the look-up.  The
+// look-up is refused while `stream` is being captured into a graph.
+static void* noalloc_scratch_address(kvb_stream_t stream, int* status) {
     static std::mutex mu;
     static void* addr[64] = {};
+    static unsigned long long ctx_id[64] = {};
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) {
@@ -1413,8 +1491,23 @@ static void* noalloc_scratch_address(int* status) {
         *status = fail(KVB_ERR_UNSUPPORTED, "attention_decode_noalloc: device ordinal %d > 63", dev);
         return nullptr;
     }
+    const unsigned long long id = current_context_id();
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev]) {
+    if (!addr[dev] || ctx_id[dev] != id) {
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        e = cudaStreamIsCapturing(stream, &cs);
+        if (e != cudaSuccess) {
+            *status = cuda_fail(e, "attention_decode_noalloc: cudaStreamIsCapturing");
+            return nullptr;
+        }
+        if (cs != cudaStreamCaptureStatusNone) {
+            *status = fail(KVB_ERR_UNSUPPORTED,
+                           "attention_decode_noalloc: the first call on device %d runs inside a "
+                           "stream capture; make one call before capturing (it looks up the "
+                           "scratch array's device address)",
+                           dev);
+            return nullptr;
+        }
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || p == nullptr) {
@@ -1422,6 +1515,7 @@ static void* noalloc_scratch_address(int* status) {
             return nullptr;
         }
         addr[dev] = p;
+        ctx_id[dev] = id;
     }
     return addr[dev];
 }
@@ -1435,8 +1529,14 @@ int kvb_attention_decode_noalloc(kvb_stream_t stream, const void* q, size_t q_ro
                                  size_t max_seq, float scale, void* out, size_t out_row_stride,
                                  int dtype) {
     // Every partial the combine pass reads is written earlier in the same
-    // call, so no part of the shared array has to start at zero.
-    const size_t need = kvb_attention_decode_workspace_bytes(n_seq, max_len, n_q, n_kv, head_dim);
+    // call, so no part of the shared array has to start at zero.  Only the
+    // split-KV kernel uses scratch; calls that kvb_attention_decode sends to
+    // its general kernel pass none and meet no size limit.
+    const size_t need =
+        decode_fast_path(q, q_row_stride, kc, vc, seq_stride, n_seq, n_q, n_kv, head_dim, max_seq,
+                         out_row_stride)
+            ? kvb_attention_decode_workspace_bytes(n_seq, max_len, n_q, n_kv, head_dim)
+            : 0;
     KVB_CHECK(need <= KVB_NOALLOC_SCRATCH_BYTES,
               "attention_decode_noalloc: the split-KV partials need %zu bytes, more than the "
               "%u-byte scratch array; use kvb_attention_decode with a workspace",
@@ -1444,7 +1544,7 @@ int kvb_attention_decode_noalloc(kvb_stream_t stream, const void* q, size_t q_ro
     void* ws = nullptr;
     if (need > 0) {
         int st = KVB_OK;
-        ws = noalloc_scratch_address(&st);
+        ws = noalloc_scratch_address(stream, &st);
         if (!ws) return st;
     }
     return kvb_attention_decode(stream, q, q_row_stride, kc, vc, seq_stride, cache_len, lens,

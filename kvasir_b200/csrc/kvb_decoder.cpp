@@ -124,7 +124,8 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
                                d->attn_norm[0], H, d->at(L.x), B * H, d->at(L.h), B * H, H, c.eps,
                                dt),
          false);
-    if (!kvb::embedding_rmsnorm_fused(B, H)) ++own;  // it ran as two launches
+    if (!kvb::embedding_rmsnorm_fused(B, H, d->embed, d->attn_norm[0], d->at(L.x), d->at(L.h)))
+        ++own;  // it ran as two launches
     for (int l = 0; l < c.n_layers; ++l) {
         STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->w_qkv[l], qkvd * H, d->at(L.qkv), B * qkvd,
                         B, H, qkvd, dt, 0),

@@ -24,9 +24,11 @@ inline bool valid_dtype(int d) { return d == KVB_BF16 || d == KVB_F16; }
 int num_sms();
 // kvb_embedding_rmsnorm runs as one launch (else as the gather and the norm): the
 // rows kvb_rmsnorm normalises with its per-row kernel, buffers 16-byte aligned.
-inline bool embedding_rmsnorm_fused(size_t rows, size_t hidden) {
+inline bool embedding_rmsnorm_fused(size_t rows, size_t hidden, const void* table, const void* w,
+                                    const void* x, const void* out) {
     return hidden % 8 == 0 && (hidden / 8) % 32 == 0 && hidden / 8 <= 32 * 16 &&
-           rows <= (size_t)num_sms() * 4;
+           rows <= (size_t)num_sms() * 4 && aligned(table, 16) && aligned(w, 16) &&
+           aligned(x, 16) && aligned(out, 16);
 }
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).

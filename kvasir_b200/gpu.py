@@ -313,6 +313,16 @@ class Gpu:
                                               kc.numel(), _ptr(out), out.numel(), n_seq, t, pos0,
                                               n_q, n_kv, head_dim, max_seq, dtype_tag(qkv)))
 
+    def attention_prefill_f32(self, qkv, kc, vc, out, n_seq, t, pos0, n_q, n_kv, head_dim,
+                              max_seq):
+        """kvb_attention_prefill_f32: the prefill rows as f32, before the one rounding."""
+        if vc.numel() != kc.numel() or out.dtype != torch.float32:
+            raise ShapeError("attention_prefill_f32: bad cache sizes or non-f32 output")
+        check(self._lib.kvb_attention_prefill_f32(self._s, _ptr(qkv), qkv.numel(), _ptr(kc),
+                                                  _ptr(vc), kc.numel(), _ptr(out), out.numel(),
+                                                  n_seq, t, pos0, n_q, n_kv, head_dim, max_seq,
+                                                  dtype_tag(qkv)))
+
     def argmax(self, logits, rows, vocab, ids, advance=None, advance2=None):
         if logits.dtype != torch.float32 or ids.dtype != torch.int32:
             raise ShapeError("argmax: f32 logits and int32 ids expected")

@@ -114,3 +114,10 @@ def test_rope_table_matches_oracle_bitwise(scaled):
     oc, os_ = O.cos_sin_table(hd, max_pos, 500000.0, scaled)
     np.testing.assert_array_equal(c, oc)
     np.testing.assert_array_equal(s, os_)
+
+
+def test_noalloc_scratch_size_matches_header():
+    import re
+    with open(L.HEADER) as f:
+        m = re.search(r"#define KVB_NOALLOC_SCRATCH_BYTES \((\d+)u << (\d+)\)", f.read())
+    assert m and int(m.group(1)) << int(m.group(2)) == L.KVB_NOALLOC_SCRATCH_BYTES

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from gpu_util import assert_close, dev, host_bits, host_f32, normal16
+from gpu_util import assert_close, assert_within_ulp, dev, host_bits, host_f32, normal16
 from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -108,6 +108,47 @@ def test_batched_decode_config2(g):
     O.set_threads(1)
     assert_close(got, want, RTOL, ATOL, "decode config 2")
     assert g.device_error() == 0
+
+
+def test_decode_error_before_output_rounding(g):
+    """The split-KV decode kernel's own error, before its output is rounded: 8
+    sequences of 16385 keys (config-5 length), each split over several chunks.
+    Every chunk leaves f32 partials in the workspace -- per query head the
+    unnormalised O row, the running max m (log2 units) and the sum l -- which
+    are folded here in f64 (O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c)
+    and held to the plain 2e-3 max-abs bar against the f64 oracle.  The bf16
+    rows of the same call are that fold rounded once (within one ulp: the
+    combine kernel folds in f32)."""
+    n_seq, n_q, n_kv, hd = 8, 32, 8, 64
+    G = n_q // n_kv
+    length = 16385
+    lens = np.full(n_seq, length, np.int32)
+    rng = np.random.default_rng(16385)
+    q, kc, vc, max_seq, per = _batched_case(rng, lens, max_seq=length)
+    nbytes = g.attention_decode_workspace_bytes(n_seq, length, n_q, n_kv, hd)
+    chunks = nbytes // (n_seq * n_kv * G * 66 * 4)
+    assert chunks >= 2 and nbytes == n_seq * n_kv * chunks * G * 66 * 4
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty(n_seq * n_q * hd, dtype=torch.bfloat16, device="cuda")
+    g.attention_decode(dev(q), n_q * hd, dev(kc), dev(vc), per,
+                       torch.from_numpy(lens).cuda(), length, n_q, n_kv, hd, max_seq, out,
+                       n_q * hd, workspace=ws)
+    assert g.device_error() == 0
+    part = ws.view(torch.float32).cpu().numpy().astype(np.float64)
+    part = part.reshape(n_seq, n_kv, chunks, G * 66)
+    o = part[..., :G * 64].reshape(n_seq, n_kv, chunks, G, hd)
+    m = part[..., G * 64:G * 65]
+    l = part[..., G * 65:G * 66]
+    M = m.max(axis=2, keepdims=True)
+    w = np.exp2(m - M)
+    pre = (o * w[..., None]).sum(axis=2) / (l * w).sum(axis=2)[..., None]
+    pre = pre.reshape(n_seq, n_q * hd)
+    O.set_threads(8)
+    want = O.attention_decode(q, n_q * hd, kc, vc, lens, n_q, n_kv, hd, max_seq, 1 / 8.0)
+    O.set_threads(1)
+    err = assert_close(pre, want, 0.0, 2e-3, "decode f32 partials folded")
+    assert_within_ulp(host_bits(out), pre.ravel(), ulps=1.0, name="decode rows vs fold")
+    print(f"decode 8 x 16385 keys: max |err| before output rounding {err:.2e}")
 
 
 def test_batched_decode_edge_lengths(g):
@@ -216,8 +257,14 @@ def test_prefill_f16_against_oracle(g, t, pos0):
 
 def test_prefill_config3_shape(g):
     """4 sequences x 2048 tokens, 32/8 heads, hd 64, N(0,1),
-    empty cache filled by the fused RoPE + KV append.  The oracle checks
-    sequences 0 and 3 on kv head 0 and 7 (its f64 cost is ~68 GFLOP for all)."""
+    every (sequence, kv head) pair against the oracle (~69 GFLOP of f64 work,
+    spread over all host cores).
+
+    Two bars.  The 16-bit rows: 2e-3 + 2^-8 |want| (the 2e-3 bar plus their own
+    rounding).  The kernel's f32 rows before that rounding
+    (kvb_attention_prefill_f32): the plain 2e-3 max-abs bar; rounding them to
+    bf16 must give the 16-bit rows bit for bit."""
+    import os
     n_seq, t, n_q, n_kv, hd = 4, 2048, 32, 8, 64
     rng = np.random.default_rng(33)
     stride = (n_q + 2 * n_kv) * hd
@@ -226,19 +273,27 @@ def test_prefill_config3_shape(g):
     kc, vc = normal16(rng, n_seq * per), normal16(rng, n_seq * per)
     out = torch.empty(n_seq * t * n_q * hd, dtype=torch.bfloat16, device="cuda")
     g.attention_prefill(dev(qkv), dev(kc), dev(vc), out, n_seq, t, 0, n_q, n_kv, hd, t)
-    got = host_f32(out).reshape(n_seq, t, n_q, hd)
-    q4 = qkv.reshape(n_seq, t, n_q + 2 * n_kv, hd)
-    O.set_threads(8)
-    for seq in (0, 3):
-        for kvh in (0, 7):
-            heads = list(range(kvh * 4, kvh * 4 + 4))
-            sub = np.concatenate([q4[seq][:, heads], q4[seq][:, n_q + kvh:n_q + kvh + 1],
-                                  q4[seq][:, n_q + n_kv + kvh:n_q + n_kv + kvh + 1]], axis=1)
-            kk = kc.reshape(n_seq, n_kv, t, hd)[seq, kvh:kvh + 1]
-            vv = vc.reshape(n_seq, n_kv, t, hd)[seq, kvh:kvh + 1]
-            want = O.attention(sub, kk, vv, t, 0, 4, 1, hd, t).reshape(t, 4, hd)
-            assert_close(got[seq][:, heads], want, RTOL, ATOL, f"prefill seq {seq} kvh {kvh}")
-    O.set_threads(1)
+    out32 = torch.empty(n_seq * t * n_q * hd, dtype=torch.float32, device="cuda")
+    g.attention_prefill_f32(dev(qkv), dev(kc), dev(vc), out32, n_seq, t, 0, n_q, n_kv, hd, t)
+    assert g.device_error() == 0
+    got_bits = host_bits(out)
+    got32 = out32.cpu().numpy()
+    np.testing.assert_array_equal(O.from_f32(got32), got_bits)
+    got = O.to_f32(got_bits).reshape(n_seq, t * n_q * hd)
+    got32 = got32.reshape(n_seq, t * n_q * hd)
+    O.set_threads(os.cpu_count() or 1)
+    worst16 = worst32 = 0.0
+    try:
+        for seq in range(n_seq):
+            want = O.attention(qkv[seq * t * stride:(seq + 1) * t * stride],
+                               kc[seq * per:(seq + 1) * per], vc[seq * per:(seq + 1) * per], t, 0,
+                               n_q, n_kv, hd, t)
+            worst16 = max(worst16, assert_close(got[seq], want, RTOL, ATOL, f"prefill seq {seq}"))
+            worst32 = max(worst32, assert_close(got32[seq], want, 0.0, 2e-3,
+                                                f"prefill seq {seq}, f32 rows"))
+    finally:
+        O.set_threads(1)
+    print(f"config 3 prefill: max |err| 16-bit rows {worst16:.2e}, f32 rows {worst32:.2e}")
 
 
 def test_prefill_v_scale_is_exact(g):
