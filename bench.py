@@ -11,17 +11,23 @@ projections + the kvb kernels + greedy argmax, replayed as one CUDA graph.
             CUDA-event timed over K steps, max over ranks;
   e2e       the same through kvb_decoder_step_host (pinned host ids in,
             H2D, step, D2H, sync) every step;
-  roofline  the dominant kernel, split-KV decode attention (kvb_attention_decode,
-            decode + combine passes), timed alone on the same stream with
-            CUDA events: algorithmic K+V+Q+O bytes per call / mean duration,
-            against the measured HBM copy bandwidth;
+  roofline  the dominant kernel, the step's own RoPE + KV append + split-KV
+            decode attention launch (kvb_rope_attention_decode, decode + combine
+            passes), timed alone on the same stream with CUDA events:
+            algorithmic bytes per call / mean duration, against the measured
+            HBM copy bandwidth;
+  ids_gather  each rank keeps its sampled ids of the e2e steps; after the
+            timed loop they are all-gathered (the path's only exchange) into
+            one [steps, sequences] table in sequence order;
   cpu_baseline  the CPU oracle's decode step (the reference's f64 CPU-reference
             kernels composed, oracle/) on a bounded sample of sequences,
             rank 0 at N = 1 only.
 
 `--impl reference` times only that CPU path (the reference arm).
 `--workload cfg1|cfg2|cfg3|cfg4` print per-kernel lines for the other
-BASELINE configs instead; `--workload sample` times the device-side sampler.
+BASELINE configs instead; `--workload sample` times the device-side sampler;
+`--workload attn5` times the config-5 attention launch alone (`--seqs` sets
+its size).
 """
 from __future__ import annotations
 
@@ -262,11 +268,12 @@ def run_decode(args):
     from kvasir_b200 import Gpu
     from kvasir_b200.config import LlamaConfig
     from kvasir_b200.decoder import Decoder
-    from kvasir_b200.shard import shard_sequences
+    from kvasir_b200.shard import RankMonitor, gather_ids_checked, shard_sequences
 
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     dist = init_dist(world, local)
+    monitor = RankMonitor() if dist is not None else None
     peaks, peak_kind = load_peaks()
     cfg = LlamaConfig.llama_3_2_1b()
     n_total, ctx = args.seqs, args.context
@@ -275,7 +282,8 @@ def run_decode(args):
     max_seq = ctx + W + 2 * K + 2
     bs = args.paged or None
     dec = Decoder(cfg, n_local, max_seq, device=f"cuda:{local}", seed=0, paged_block_size=bs)
-    dec.fill_kv_normal(seed=1000 + rank)
+    # every sequence's context is seeded by its global index: the same data at any N
+    dec.fill_kv_normal(seed=1000, first_seq=first)
     dec.set_lengths(ctx)
     rng = np.random.default_rng(7)
     ids0 = rng.integers(0, cfg.vocab_size, n_total).astype(np.int32)[first:first + n_local]
@@ -301,27 +309,43 @@ def run_decode(args):
     ms = max_over_ranks(ev0.elapsed_time(ev1) / K, dist, torch)
     value = n_total / (ms / 1e3)
 
-    # ---- end to end through the host-facing step (pinned ids in / out)
+    # ---- end to end through the host-facing step (pinned ids in / out); each
+    # step's sampled ids are kept on the host for the gather after the loop
     h_in = torch.from_numpy(dec.ids_out.cpu().numpy()).pin_memory()
     h_out = torch.empty(n_local, dtype=torch.int32).pin_memory()
+    table = torch.empty((K, n_local), dtype=torch.int32)
     barrier(dist, torch)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(K):
+    for i in range(K):
         dec.step_host(h_in, h_out, stream)
         h_in.copy_(h_out)
+        table[i].copy_(h_out)
     e1.record(stream)
     e1.synchronize()
     barrier(dist, torch)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / K, dist, torch)
 
-    # ---- dominant kernel alone: decode attention over layer 0's cache
+    # ---- the only exchange: the sampled ids of all ranks, in sequence order
+    t0 = time.perf_counter()
+    if dist is not None:
+        full, st = gather_ids_checked(table, n_total, monitor, timeout_s=120.0)
+        if full is None:
+            raise RuntimeError(f"id gather failed: {st.reason}")
+    else:
+        full = table
+    gather_ms = (time.perf_counter() - t0) * 1e3
+    if rank == 0 and args.ids_out:
+        np.save(args.ids_out, full.numpy())
+
+    # ---- dominant kernel alone: the step's RoPE + KV append + decode attention
+    # launch (kvb_rope_attention_decode, split-KV decode + combine) over layer 0
     g = Gpu(local)
     hd, nkv, nq = cfg.head_dim, cfg.num_kv_heads, cfg.num_heads
     per = nkv * max_seq * hd
     lens_host = np.full(n_local, ctx + 1, np.int32)
     lens = torch.from_numpy(lens_host).cuda()
-    q = torch.randn(n_local, cfg.qkv_dim, dtype=torch.bfloat16, device="cuda")
+    qkv = torch.randn(n_local, cfg.qkv_dim, dtype=torch.bfloat16, device="cuda")
     out = torch.empty(n_local, cfg.q_dim, dtype=torch.bfloat16, device="cuda")
     wsb = g.attention_decode_workspace_bytes(n_local, max_seq, nq, nkv, hd)
     ws = torch.empty(max(wsb, 16), dtype=torch.uint8, device="cuda")
@@ -329,12 +353,12 @@ def run_decode(args):
 
     def attn():
         if bs:
-            g.attention_decode_paged(q, cfg.qkv_dim, kc0, vc0, dec.block_table,
-                                     dec.block_table.shape[1], bs, lens, max_seq, nq, nkv, hd,
-                                     out, cfg.q_dim, workspace=ws)
+            g.rope_attention_decode_paged(qkv, dec.cos, dec.sin, kc0, vc0, dec.block_table,
+                                          dec.block_table.shape[1], bs, lens, max_seq, nq, nkv,
+                                          hd, out, cfg.q_dim, workspace=ws)
         else:
-            g.attention_decode(q, cfg.qkv_dim, kc0, vc0, per, lens, max_seq, nq, nkv, hd, max_seq,
-                               out, cfg.q_dim, workspace=ws)
+            g.rope_attention_decode(qkv, dec.cos, dec.sin, kc0, vc0, per, lens, max_seq, nq, nkv,
+                                    hd, max_seq, out, cfg.q_dim, workspace=ws)
 
     for _ in range(3):
         attn()
@@ -347,12 +371,14 @@ def run_decode(args):
     a1.record(stream)
     a1.synchronize()
     attn_ms = a0.elapsed_time(a1) / reps
-    alg_bytes = int(lens_host.sum()) * nkv * hd * 2 * 2 + n_local * nq * hd * 2 * 2
+    # K + V of every key read, the qkv row read, the new k / v row written, the output written
+    alg_bytes = (int(lens_host.sum()) * nkv * hd * 2 * 2 + n_local * cfg.qkv_dim * 2 +
+                 n_local * 2 * nkv * hd * 2 + n_local * nq * hd * 2)
     achieved = alg_bytes / (attn_ms / 1e3) / 1e9
     # DRAM traffic per launch: the ncu-measured (read + write) / algorithmic ratio of the
-    # committed capture (profiles/attn_decode_cfg5_small.md), scaled to this launch
+    # committed capture of this kernel, scaled to this launch
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "attn_decode_cfg5_small.md")
+    tp = os.path.join(ROOT, "profiles", "attn_rope_decode_cfg5_small.md")
     if os.path.exists(tp):
         with open(tp) as f:
             for line in f:
@@ -375,24 +401,22 @@ def run_decode(args):
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
             "steps": K, "warmup": W, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic: random-init weights N(0,0.02), KV N(0,1), uniform random ids",
-            "config": {"workload": "cfg5: sequence-sharded long-context decode, Llama-3.2-1B "
-                                   "(16 layers, random init), 256 sequences x 16384-token KV",
-                       "n_seq_total": n_total, "context": ctx, "n_seq_per_gpu": n_local,
-                       "parallelism": f"independent sequences over {world} GPU(s)",
-                       "kv_cache": (f"paged, {bs}-token blocks scattered by a seeded table"
-                                    if bs else "contiguous per sequence"),
-                       "l2": "inputs larger than L2 (KV %.1f GB per GPU, weights 2.47 GB)" %
-                             (2 * cfg.num_layers * n_local * per * 2 / 1e9)},
+            "data": "synthetic: random-init weights N(0,0.02), KV N(0,1) seeded per sequence, "
+                    "uniform random ids",
+            "config": cfg5_config(n_total, ctx, n_local, world, bs, cfg, per),
             "e2e": {"value": n_total / (e2e_ms / 1e3), "unit": "tokens/s",
                     "h2d_bytes_per_step": 4 * n_total, "d2h_bytes_per_step": 4 * n_total},
+            "ids_gather": {"shape": list(full.shape), "ms": gather_ms,
+                           "how": ("all_gather over NCCL after the timed steps, behind a "
+                                   "store arrival check" if dist is not None else "one rank")},
             "gpu_launches": K * own,
             "launches_per_step": {"own": own, "cublas": lib},
             "roofline": {"bound": "hbm", "achieved": achieved,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
-                         "kernel": ("kvb_attention_decode_paged" if bs else "kvb_attention_decode")
-                                   + " (split-KV decode + combine), layer 0",
+                         "kernel": ("kvb_rope_attention_decode_paged" if bs
+                                    else "kvb_rope_attention_decode")
+                                   + " (RoPE + KV append + split-KV decode, + combine), layer 0",
                          "alg_bytes_per_launch": alg_bytes, "ms_per_launch": attn_ms,
                          "peak_source": f"{peak_kind} hbm_gbs"},
             "cpu_baseline": cpu,
@@ -401,6 +425,17 @@ def run_decode(args):
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
+
+
+def cfg5_config(n_total, ctx, n_local, world, bs, cfg, per):
+    return {"workload": "cfg5: sequence-sharded long-context decode, Llama-3.2-1B "
+                        "(16 layers, random init), 256 sequences x 16384-token KV",
+            "n_seq_total": n_total, "context": ctx, "n_seq_per_gpu": n_local,
+            "parallelism": f"independent sequences over {world} GPU(s)",
+            "kv_cache": (f"paged, {bs}-token blocks scattered by a seeded table"
+                         if bs else "contiguous per sequence"),
+            "l2": "inputs larger than L2 (KV %.1f GB per GPU, weights 2.47 GB)" %
+                  (2 * cfg.num_layers * n_local * per * 2 / 1e9)}
 
 
 def run_reference(args):
@@ -418,13 +453,19 @@ def run_reference(args):
     per_step = [sample.step() for _ in range(steps)]
     sec = statistics.mean(per_step)
     v = 1.0 / sec
+    n_total = args.seqs
+    n_local = -(-n_total // max(world, 1))
+    per = cfg.num_kv_heads * (args.context + 1) * cfg.head_dim
+    config = cfg5_config(n_total, args.context, n_local, world, None, cfg, per)
+    config["sample"] = ("the oracle's f64 decode step of 1 sequence per timed step, "
+                        f"{steps} timed steps after {warmup} warm-up (capped at 5 and 3: a "
+                        "CPU step takes ~0.3 s); sequences are independent, so tokens/s for "
+                        f"{n_total} sequences is the per-sequence rate")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
             "n_gpus": world, "steps": steps, "warmup": warmup, "ms_per_step": sec * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic: seeded N(0,0.02) weights, N(0,1) KV",
-            "config": {"workload": "cfg5: sequence-sharded long-context decode, Llama-3.2-1B "
-                                   "(16 layers, random init), 256 sequences x 16384-token KV",
-                       "context": args.context},
+            "config": config,
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "port",
                              "sample": f"oracle decode step of 1 sequence per timed step at "
                                        f"context {args.context} ({cpu_model()})"},
@@ -439,7 +480,7 @@ def main():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kernel", choices=["kernel", "reference"])
-    ap.add_argument("--workload", default="cfg5", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "sample"])
+    ap.add_argument("--workload", default="cfg5", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "sample", "attn5"])
     ap.add_argument("--seqs", type=int, default=256, help="total sequences (cfg5)")
     ap.add_argument("--context", type=int, default=16384, help="KV tokens per sequence (cfg5)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -447,6 +488,8 @@ def main():
     ap.add_argument("--ncu-window", action="store_true",
                     help="call cudaProfilerStart just before the first timed decode steps, so that "
                          "`ncu --profile-from-start off` lists only step launches (cfg4, cfg5)")
+    ap.add_argument("--ids-out", default="",
+                    help="cfg5: write the gathered [steps, seqs] table of sampled ids (.npy, rank 0)")
     ap.add_argument("--paged", type=int, default=0,
                     help="cfg5 on a paged KV cache with this block size (a multiple of 64); "
                          "0 = contiguous")
@@ -457,7 +500,7 @@ def main():
         return run_reference(args)
     if args.workload == "cfg5":
         return run_decode(args)
-    from kvasir_b200 import bench_suite
+    import bench_suite
     bench_suite.run(args.workload, args)
 
 

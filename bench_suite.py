@@ -19,11 +19,11 @@ import time
 import numpy as np
 import torch
 
-from . import Gpu
-from .config import LlamaConfig
-from .rope import cos_sin_table
+from kvasir_b200 import Gpu
+from kvasir_b200.config import LlamaConfig
+from kvasir_b200.rope import cos_sin_table
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ROOT = os.path.dirname(os.path.abspath(__file__))
 
 
 def _peaks():
@@ -415,7 +415,7 @@ def _library_prefill_reference(n_seq, T, nq, nkv, hd, flops, flush):
 def cfg4(args):
     """Full 16-layer decode, context 1024, batch 1 and 32, 256 greedy steps
     from uniform random prompt ids (random-init weights, N(0,1) context KV)."""
-    from .decoder import Decoder
+    from kvasir_b200.decoder import Decoder
     peaks, kind = _peaks()
     cfg = LlamaConfig.llama_3_2_1b()
     steps, ctx = 256, 1024
@@ -509,5 +509,52 @@ def sample(args):
                    "top_p_us": us, "argmax_us": argmax_us})
 
 
+
+# ----------------------------------------------------------------------------- config 5 kernel
+def attn5(args):
+    """The config-5 step's dominant launch alone: RoPE + KV append + split-KV decode
+    attention (kvb_rope_attention_decode, decode + combine) over one layer's cache of
+    `--seqs` sequences at `--context` keys (+ the new one).  Sized by --seqs so that
+    a profiler capture can run it on a small case (8 sequences: 269 MB of K/V, above
+    L2)."""
+    peaks, kind = _peaks()
+    g = Gpu(0)
+    n_seq, ctx = args.seqs, args.context
+    nq, nkv, hd = 32, 8, 64
+    max_seq = ctx + 8
+    qkv_dim = (nq + 2 * nkv) * hd
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    per = nkv * max_seq * hd
+    kc = torch.empty(n_seq * per, dtype=torch.bfloat16, device="cuda").normal_(generator=gen)
+    vc = torch.empty(n_seq * per, dtype=torch.bfloat16, device="cuda").normal_(generator=gen)
+    qkv = torch.randn(n_seq * qkv_dim, generator=gen, device="cuda").to(torch.bfloat16)
+    cos, sin = cos_sin_table(LlamaConfig.llama_3_2_1b(), max_seq)
+    cos_t, sin_t = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    lens_host = np.full(n_seq, ctx + 1, np.int32)
+    lens = torch.from_numpy(lens_host).cuda()
+    out = torch.empty(n_seq * nq * hd, dtype=torch.bfloat16, device="cuda")
+    nb = g.attention_decode_workspace_bytes(n_seq, max_seq, nq, nkv, hd)
+    ws = torch.empty(max(nb, 16), dtype=torch.uint8, device="cuda")
+
+    def run():
+        g.rope_attention_decode(qkv, cos_t, sin_t, kc, vc, per, lens, max_seq, nq, nkv, hd,
+                                max_seq, out, nq * hd, workspace=ws)
+
+    for _ in range(3):
+        run()
+    reps = max(3, min(50, args.steps))
+    ms = time_loop(run, reps) if n_seq * per * 4 > (1 << 30) else time_each(run, reps, _Flusher())
+    alg = (int(lens_host.sum()) * nkv * hd * 2 * 2 + n_seq * qkv_dim * 2 +
+           n_seq * 2 * nkv * hd * 2 + n_seq * nq * hd * 2)
+    gbs = alg / (ms * 1e-3) / 1e9
+    _emit({"workload": f"cfg5 attention launch: RoPE + KV append + split-KV decode, {n_seq} seqs "
+                       f"x {ctx + 1} keys, 32/8 heads, hd 64, one layer",
+           "metric": "attention HBM GB/s", "value": gbs, "unit": "GB/s", "us": ms * 1e3,
+           "alg_bytes": alg, "frac_of_peak": gbs / peaks["hbm_gbs"],
+           "peak": f"{peaks['hbm_gbs']} GB/s ({kind})",
+           "l2": "K/V above L2" if n_seq * per * 4 > (1 << 30) else "flushed between launches"})
+
+
 def run(name, args):
-    {"cfg1": cfg1, "cfg2": cfg2, "cfg3": cfg3, "cfg4": cfg4, "sample": sample}[name](args)
+    {"cfg1": cfg1, "cfg2": cfg2, "cfg3": cfg3, "cfg4": cfg4, "sample": sample,
+     "attn5": attn5}[name](args)

@@ -134,13 +134,41 @@ class Decoder:
             pass
 
     # ------------------------------------------------------------ cache set-up
-    def fill_kv_normal(self, seed: int = 1, std: float = 1.0) -> None:
-        """Fills the whole KV cache with N(0, std) (the synthetic context)."""
+    def fill_kv_normal(self, seed: int = 1, std: float = 1.0, first_seq: int | None = None) -> None:
+        """Fills the whole KV cache with N(0, std) (the synthetic context).
+
+        first_seq=None: one generator over the whole cache.  first_seq=g: local
+        sequence b is filled from generators seeded by (seed, g + b, layer, k|v)
+        only, so a sequence's context does not depend on how the sequences are
+        split over ranks (a paged cache gets the same contents through its
+        block table)."""
         g = torch.Generator(device=self.device)
-        g.manual_seed(seed)
-        for l in range(self.cfg.num_layers):
-            self.kc[l].normal_(0.0, std, generator=g)
-            self.vc[l].normal_(0.0, std, generator=g)
+        if first_seq is None:
+            g.manual_seed(seed)
+            for l in range(self.cfg.num_layers):
+                self.kc[l].normal_(0.0, std, generator=g)
+                self.vc[l].normal_(0.0, std, generator=g)
+            return
+        nkv, hd = self.cfg.num_kv_heads, self.cfg.head_dim
+        paged = getattr(self, "_paged", None)
+        tmp = seq = None
+        if paged is not None:
+            bs = self.kc.shape[3]
+            mb = self.block_table.shape[1]
+            tmp = torch.zeros(nkv, mb * bs, hd, dtype=self.dtype, device=self.device)
+            seq = torch.empty(nkv, self.max_seq, hd, dtype=self.dtype, device=self.device)
+        for b in range(self.n_seq):
+            for l in range(self.cfg.num_layers):
+                for kind, cache in ((0, self.kc), (1, self.vc)):
+                    s = (((seed * 1000003 + first_seq + b) * 1024 + l) * 2 + kind) & (2 ** 63 - 1)
+                    g.manual_seed(s)
+                    if paged is None:
+                        cache[l, b].normal_(0.0, std, generator=g)
+                    else:  # the contiguous contents, scattered into the pool's blocks
+                        seq.normal_(0.0, std, generator=g)
+                        tmp[:, :self.max_seq] = seq
+                        blocks = tmp.view(nkv, mb, bs, hd).permute(1, 0, 2, 3)
+                        cache[l][self.block_table[b].long()] = blocks
 
     def use_paged_cache(self, k_pools, v_pools, block_table, max_blocks: int,
                         block_size: int) -> None:

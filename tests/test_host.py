@@ -3,6 +3,7 @@ engine/src/model/config.rs:144-172), sequence sharding, and the id gather
 across ranks as world-size-2 gloo process groups."""
 import os
 import socket
+import time
 
 import pytest
 import torch
@@ -93,3 +94,103 @@ def test_gather_ids_world_2_gloo(n_total):
         assert p.exitcode == 0
     want = [[step * 1000 + i for i in range(n_total)] for step in range(steps)]
     assert results[0] == want and results[1] == want
+
+
+# ------------------------------------------------------------------ failure detection
+# A CPU stand-in for the per-rank decode loop: each step maps ids to new ids, as
+# the decoder does on the device.  One rank is made to fail (raise) or stall
+# between steps; the other must get an error status naming it from the checked
+# gather within the stated limit, instead of waiting in the collective for good.
+GATHER_LIMIT_S = 2.0
+
+
+def _standin_step(ids: torch.Tensor) -> torch.Tensor:
+    return (ids * 31 + 7) % 128256
+
+
+def _failure_worker(rank, world, port, mode, q):
+    from kvasir_b200.shard import RankFailure, RankMonitor, gather_ids_checked
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    mon = RankMonitor()
+    n_total, steps = 8, 4
+    s, c = shard_sequences(n_total, world, rank)
+    ids = torch.arange(s, s + c, dtype=torch.int32)
+    table = []
+    try:
+        with mon.guard():
+            for step in range(steps):
+                if rank == 1 and step == 2:
+                    if mode == "raise":
+                        raise RuntimeError("stand-in step failed on purpose")
+                    if mode == "stall":
+                        time.sleep(3600)  # the test process terminates this rank
+                mon.check()
+                ids = _standin_step(ids)
+                table.append(ids.clone())
+        t0 = time.monotonic()
+        full, st = gather_ids_checked(torch.stack(table), n_total, mon, timeout_s=GATHER_LIMIT_S)
+        q.put((rank, st.ok, st.rank, st.reason, time.monotonic() - t0,
+               None if full is None else full.tolist()))
+    except RankFailure as e:  # seen between steps, before the gather
+        q.put((rank, False, e.rank, str(e), 0.0, None))
+    except RuntimeError as e:  # this rank's own failure
+        q.put((rank, False, rank, f"raised: {e}", 0.0, None))
+    if mode == "none":
+        dist.destroy_process_group()
+    q.close()
+    q.join_thread()  # flush the report before the hard exit
+    os._exit(0)
+
+
+def _run_failure_case(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_failure_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    want_reports = 2 if mode != "stall" else 1
+    try:
+        reports = {}
+        for _ in range(want_reports):
+            r = q.get(timeout=120)
+            reports[r[0]] = r
+    finally:
+        for p in procs:
+            if mode == "stall" and p is procs[1]:
+                p.terminate()
+            p.join(timeout=60)
+    return reports
+
+
+def test_checked_gather_all_ranks_healthy():
+    reports = _run_failure_case("none")
+    want = []
+    ids = torch.arange(8, dtype=torch.int32)
+    for _ in range(4):
+        ids = _standin_step(ids)
+        want.append(ids.tolist())
+    for r in (0, 1):
+        assert reports[r][1], reports[r][3]
+        assert reports[r][5] == want
+
+
+def test_checked_gather_names_a_rank_that_raised():
+    reports = _run_failure_case("raise")
+    ok, bad_rank, reason, waited = reports[0][1:5]
+    assert not ok and bad_rank == 1
+    assert "rank 1 failed" in reason and "on purpose" in reason
+    assert waited < GATHER_LIMIT_S + 1.0  # seen between steps (0 s) or at the gather
+    assert reports[1][1] is False  # the failing rank itself reports its own error
+
+
+def test_checked_gather_times_out_on_a_stalled_rank():
+    reports = _run_failure_case("stall")
+    ok, bad_rank, reason, waited = reports[0][1:5]
+    assert not ok and bad_rank == 1
+    assert "did not reach" in reason
+    assert GATHER_LIMIT_S - 0.1 <= waited < GATHER_LIMIT_S + 2.0
