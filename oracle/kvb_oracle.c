@@ -413,6 +413,35 @@ static void round_array(const float* in, uint16_t* out, size_t n, int dtype) {
     kvo_from_f32_array(in, out, n, dtype);
 }
 
+/* Rounding dither of the composed decode step (kvo_set_round_dither): each value
+ * is scaled by (1 + u * rel), u uniform in [-1, 1) from a counter-based hash,
+ * before it is rounded to 16 bits.  It models the freedom of another correct
+ * evaluation whose sums are formed in f32 and in another order (a GPU): such a
+ * sum differs from the f64 one by a small relative amount, and where that
+ * straddles a rounding boundary the 16-bit results differ by one ulp.  Applied
+ * only at rounding points that follow a sum (norms, projections, attention,
+ * SiLU), not after RoPE or the residual add, which both sides compute exactly
+ * alike. */
+static double g_dither_rel = 0.0;
+static uint64_t g_dither_ctr = 0;
+
+void kvo_set_round_dither(double rel, uint64_t seed) {
+    g_dither_rel = rel;
+    g_dither_ctr = mix64(seed);
+}
+
+static void round_dithered(const float* in, uint16_t* out, size_t n, int dtype) {
+    if (g_dither_rel <= 0.0) {
+        round_array(in, out, n, dtype);
+        return;
+    }
+    for (size_t i = 0; i < n; ++i) {
+        const uint64_t h = mix64(g_dither_ctr++);
+        const double u = (double)(h >> 11) * (2.0 / 9007199254740992.0) - 1.0; /* [-1, 1) */
+        out[i] = kvo_from_f32((float)((double)in[i] * (1.0 + u * g_dither_rel)), dtype);
+    }
+}
+
 /* One decode step, composed as the reference's planned forward pass orders
  * it (reference DESIGN.md:36-74, §3 call stack of the planned llama.rs):
  * embedding -> per layer [rmsnorm, qkv linear, rope, kv_append, attention,
@@ -443,30 +472,30 @@ void kvo_decode_step(const kvo_model_dims* d, const kvo_model_weights* w, const 
             uint16_t* kl = kc + b * seq_cache + l * layer_cache;
             uint16_t* vl = vc + b * seq_cache + l * layer_cache;
             kvo_rmsnorm(x, w->attn_norm[l], f, 1, H, d->eps, dtype);
-            round_array(f, hbuf, H, dtype);
+            round_dithered(f, hbuf, H, dtype);
             kvo_linear(hbuf, w->w_qkv[l], f, 1, H, qkvd, dtype);
-            round_array(f, qkv, qkvd, dtype);
+            round_dithered(f, qkv, qkvd, dtype);
             kvo_rope(qkv, cos_t, sin_t, f, 1, (size_t)p, d->n_q, d->n_kv, hd, dtype);
             round_array(f, qkv, qkvd, dtype);
             kvo_kv_append(qkv, kl, vl, 1, (size_t)p, d->n_q, d->n_kv, hd, d->max_seq);
             kvo_attention_decode(qkv, qkvd, kl, vl, &len, 1, d->n_q, d->n_kv, hd, d->max_seq,
                                  1.0 / sqrt((double)hd), f, dtype);
-            round_array(f, attn, qd, dtype);
+            round_dithered(f, attn, qd, dtype);
             kvo_linear(attn, w->w_o[l], f, 1, qd, H, dtype);
-            round_array(f, o, H, dtype);
+            round_dithered(f, o, H, dtype);
             kvo_add(x, o, x, H, dtype);
             kvo_rmsnorm(x, w->mlp_norm[l], f, 1, H, d->eps, dtype);
-            round_array(f, hbuf, H, dtype);
+            round_dithered(f, hbuf, H, dtype);
             kvo_linear(hbuf, w->w_gu[l], f, 1, H, 2 * I, dtype);
-            round_array(f, gu, 2 * I, dtype);
+            round_dithered(f, gu, 2 * I, dtype);
             kvo_silu_mul(gu, f, 1, I, dtype);
-            round_array(f, act, I, dtype);
+            round_dithered(f, act, I, dtype);
             kvo_linear(act, w->w_down[l], f, 1, I, H, dtype);
-            round_array(f, o, H, dtype);
+            round_dithered(f, o, H, dtype);
             kvo_add(x, o, x, H, dtype);
         }
         kvo_rmsnorm(x, w->final_norm, f, 1, H, d->eps, dtype);
-        round_array(f, hbuf, H, dtype);
+        round_dithered(f, hbuf, H, dtype);
         kvo_linear(hbuf, w->embed, logits + b * d->vocab, 1, H, d->vocab, dtype);
         kvo_argmax(logits + b * d->vocab, 1, d->vocab, &ids_out[b]);
     }

@@ -102,6 +102,13 @@ typedef struct {
     const uint16_t* const* w_down;
 } kvo_model_weights;
 
+/* Rounding dither of kvo_decode_step (0 = off, the default): every value rounded to
+ * 16 bits after a sum (norms, projections, attention, SiLU) is first scaled by
+ * (1 + u*rel), u uniform in [-1, 1), seeded.  Two runs, dithered and not, show how
+ * far the logits move when the 16-bit roundings of the chain land as another
+ * correct evaluation in f32 may land them. */
+void kvo_set_round_dither(double rel, uint64_t seed);
+
 void kvo_decode_step(const kvo_model_dims* d, const kvo_model_weights* w, const float* cos_t,
                      const float* sin_t, uint16_t* kc, uint16_t* vc, const int32_t* ids,
                      const int32_t* pos, size_t n_seq, float* logits, int32_t* ids_out, int dtype);

@@ -68,6 +68,7 @@ def _declare(L):
                                C.c_double, _f64p]
     L.kvo_cos_sin_table.argtypes = [_sz, C.c_double, C.c_int, C.c_double, C.c_double, C.c_double,
                                     C.c_double, _sz, _f32p, _f32p]
+    L.kvo_set_round_dither.argtypes = [C.c_double, C.c_uint64]
     L.kvo_decode_step.argtypes = [C.POINTER(ModelDims), C.POINTER(ModelWeights), _f32p, _f32p,
                                   _u16p, _u16p, _i32p, _i32p, _sz, _f32p, _i32p, C.c_int]
 
@@ -295,6 +296,11 @@ def cos_sin_table(hd, max_pos, theta, scaled, factor=32.0, low=1.0, high=4.0, or
     s = np.empty(max_pos * (hd // 2), np.float32)
     lib().kvo_cos_sin_table(hd, theta, int(scaled), factor, low, high, orig, max_pos, c, s)
     return c, s
+
+
+def set_round_dither(rel: float, seed: int = 0) -> None:
+    """Rounding dither of decode_step (kvo_set_round_dither); rel = 0 turns it off."""
+    lib().kvo_set_round_dither(float(rel), int(seed) & 0xFFFFFFFFFFFFFFFF)
 
 
 def decode_step(dims: dict, weights: dict, cos, sin, kc, vc, ids, pos, dtype="bf16"):

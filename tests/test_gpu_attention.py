@@ -110,9 +110,12 @@ def test_batched_decode_config2(g):
     assert g.device_error() == 0
 
 
-def test_decode_error_before_output_rounding(g):
+@pytest.mark.parametrize("length,q_std", [(16385, 1.0), (700, 4.0)])
+def test_decode_error_before_output_rounding(g, length, q_std):
     """The split-KV decode kernel's own error, before its output is rounded: 8
-    sequences of 16385 keys (config-5 length), each split over several chunks.
+    sequences, each split over several chunks -- at the config-5 length with
+    N(0,1) inputs (flat softmax, small outputs), and at 700 keys with q scaled
+    by 4 (peaked softmax: outputs of unit scale, where the bar bites).
     Every chunk leaves f32 partials in the workspace -- per query head the
     unnormalised O row, the running max m (log2 units) and the sum l -- which
     are folded here in f64 (O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c)
@@ -121,10 +124,10 @@ def test_decode_error_before_output_rounding(g):
     combine kernel folds in f32)."""
     n_seq, n_q, n_kv, hd = 8, 32, 8, 64
     G = n_q // n_kv
-    length = 16385
     lens = np.full(n_seq, length, np.int32)
-    rng = np.random.default_rng(16385)
+    rng = np.random.default_rng(length)
     q, kc, vc, max_seq, per = _batched_case(rng, lens, max_seq=length)
+    q = O.from_f32(O.to_f32(q) * np.float32(q_std))
     nbytes = g.attention_decode_workspace_bytes(n_seq, length, n_q, n_kv, hd)
     chunks = nbytes // (n_seq * n_kv * G * 66 * 4)
     assert chunks >= 2 and nbytes == n_seq * n_kv * chunks * G * 66 * 4
@@ -148,7 +151,8 @@ def test_decode_error_before_output_rounding(g):
     O.set_threads(1)
     err = assert_close(pre, want, 0.0, 2e-3, "decode f32 partials folded")
     assert_within_ulp(host_bits(out), pre.ravel(), ulps=1.0, name="decode rows vs fold")
-    print(f"decode 8 x 16385 keys: max |err| before output rounding {err:.2e}")
+    print(f"decode 8 x {length} keys, q x {q_std:g}: max |err| before output rounding "
+          f"{err:.2e} (max |out| {np.abs(want).max():.2f})")
 
 
 def test_batched_decode_edge_lengths(g):

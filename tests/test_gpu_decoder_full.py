@@ -1,0 +1,140 @@
+"""The decode step the bench times, at its own shape: the 16-layer Llama-3.2-1B
+decoder (hidden 2048, 32 / 8 heads, ffn 8192, vocab 128256, tied embedding,
+random N(0, 0.02) weights) on three sequences at context 1024 and one at
+16384, three greedy steps, against the oracle's composed step
+(reference engine/tests/kernels.rs:44-289 in the planned order of
+DESIGN.md:36-74) on the same bits.
+
+Tolerance, from bf16 rounding.  Both sides round every activation to bf16 at
+the same points, but the GPU forms its sums in f32 (cuBLAS, split-KV
+attention) and in another order than the oracle's f64 sums.  Where the two
+sums straddle a rounding boundary the bf16 values differ by one ulp, and those
+one-ulp differences travel through the residual stream of 16 layers.  How far
+that moves the logits is measured on the CPU, independently of the GPU: the
+oracle's step is run again with every rounding point that follows a sum
+dithered by a relative 2^-16 (oracle.set_round_dither; an f32 sum of a few
+thousand terms is accurate to ~2^-20), and the largest |logit| difference
+between the two oracle runs is the spread S of that step (about 0.1 at logit
+rms 0.9; 2^-18 and 2^-14 dithers give about the same, since the flips
+saturate within a few layers).  Bars: every GPU logit within LOGIT_TOL_FACTOR *
+S of the oracle's, the rms difference within LOGIT_TOL_FACTOR * the rms
+spread, and the greedy ids equal wherever the oracle's top-2 margin exceeds
+twice the row's largest logit error (on every row the GPU's pick is a token
+within that distance of the oracle's best).  A wrong layer moves the logits
+by their own scale (rms 0.9), an order of magnitude above the bar.
+
+Also: the first layer's new K / V rows (embedding, RMSNorm, qkv projection,
+RoPE, no residual history yet) equal the oracle's bit for bit in >= 99% of
+elements, and the same sequences decoded one per decoder (other GEMM shapes
+and split-KV chunking) agree with the batched step within the same bar."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import LLAMA1B_LOGIT_SPREAD, LOGIT_TOL_FACTOR, host_bits
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+DITHER_REL = 2.0 ** -16
+
+
+def _weight_bits(dec):
+    w = dec.w
+    return dict(embed=host_bits(w["embed"]).ravel(), final_norm=host_bits(w["final_norm"]),
+                **{k: [host_bits(t).ravel() for t in w[k]] for k in
+                   ("attn_norm", "w_qkv", "w_o", "mlp_norm", "w_gu", "w_down")})
+
+
+def test_full_llama_1b_decode_step_matches_oracle():
+    from kvasir_b200.config import LlamaConfig
+    from kvasir_b200.decoder import Decoder
+    from kvasir_b200.rope import cos_sin_table
+    cfg = LlamaConfig.llama_3_2_1b()
+    L, nkv, hd = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim
+    lens = np.array([1024, 1024, 1024, 16384], np.int32)
+    n_seq, max_seq, steps = len(lens), 16384 + 8, 3
+    dec = Decoder(cfg, n_seq, max_seq, seed=0)
+    dec.fill_kv_normal(seed=1000, first_seq=0)
+    dec.set_lengths(lens)
+    ids = np.random.default_rng(3).integers(0, cfg.vocab_size, n_seq).astype(np.int32)
+    dec.ids_in.copy_(torch.from_numpy(ids).cuda())
+    singles = []
+    for b in range(n_seq):
+        d1 = Decoder(cfg, 1, max_seq, weights=dec.w)
+        d1.kc.copy_(dec.kc[:, b:b + 1])
+        d1.vc.copy_(dec.vc[:, b:b + 1])
+        d1.set_lengths(lens[b:b + 1])
+        singles.append(d1)
+    torch.cuda.synchronize()
+    wb = _weight_bits(dec)
+    # oracle caches [seq][layer][n_kv][max_seq][hd]
+    okc = np.ascontiguousarray(host_bits(dec.kc).reshape(L, n_seq, -1).transpose(1, 0, 2))
+    ovc = np.ascontiguousarray(host_bits(dec.vc).reshape(L, n_seq, -1).transpose(1, 0, 2))
+    cos, sin = cos_sin_table(cfg, max_seq)
+    dims = dict(hidden=cfg.hidden_size, inter=cfg.intermediate_size, n_layers=L,
+                n_q=cfg.num_heads, n_kv=nkv, head_dim=hd, vocab=cfg.vocab_size,
+                max_seq=max_seq, eps=cfg.rms_norm_eps)
+    O.set_threads(os.cpu_count() or 1)
+    pos = lens.copy()
+    compared = 0
+    try:
+        for step in range(steps):
+            for b, d1 in enumerate(singles):
+                d1.ids_in.copy_(torch.from_numpy(ids[b:b + 1]).cuda())
+            dec.step()
+            for d1 in singles:
+                d1.step()
+            torch.cuda.synchronize()
+            # dithered run first: it writes only the new K / V rows at pos, which the
+            # plain run below rewrites before its attention reads them
+            O.set_round_dither(DITHER_REL, seed=17 + step)
+            dith, _ = O.decode_step(dims, wb, cos, sin, okc, ovc, ids, pos)
+            O.set_round_dither(0.0)
+            want, want_ids = O.decode_step(dims, wb, cos, sin, okc, ovc, ids, pos)
+            want = want.astype(np.float64)
+            spread = np.abs(dith - want).max(axis=1)
+            spread_rms = np.sqrt(((dith - want) ** 2).mean(axis=1))
+            got = dec.logits.cpu().numpy().astype(np.float64)
+            one = np.concatenate([d1.logits.cpu().numpy() for d1 in singles]).astype(np.float64)
+            err = np.abs(got - want)
+            tol = LOGIT_TOL_FACTOR * spread
+            msg = (f"step {step}: max |err| {err.max(axis=1)}, bar {tol}; rms "
+                   f"{np.sqrt((err ** 2).mean(axis=1))}, bar {LOGIT_TOL_FACTOR * spread_rms}")
+            print(msg)
+            assert (err.max(axis=1) <= tol).all(), msg
+            assert (np.sqrt((err ** 2).mean(axis=1)) <= LOGIT_TOL_FACTOR * spread_rms).all(), msg
+            assert (np.abs(one - got).max(axis=1) <= tol).all(), f"step {step}: batch vs single"
+            assert (spread <= LLAMA1B_LOGIT_SPREAD).all(), f"spread {spread}"
+            # ids: the greedy pick of the GPU's own logits (first index of the max), equal
+            # to the oracle's wherever the oracle's top-2 margin exceeds twice the row's
+            # largest logit error (no order can change there), and on every row a token
+            # whose oracle logit is within that distance of the oracle's best
+            got_ids = dec.ids_out.cpu().numpy()
+            np.testing.assert_array_equal(got_ids, np.argmax(got, axis=1))
+            top2 = np.sort(want, axis=1)[:, -2:]
+            row_err = err.max(axis=1)
+            clear = (top2[:, 1] - top2[:, 0]) > 2 * row_err
+            np.testing.assert_array_equal(got_ids[clear], want_ids[clear])
+            picked = want[np.arange(n_seq), got_ids]
+            assert (picked >= top2[:, 1] - 2 * row_err).all(), (step, picked, top2[:, 1])
+            compared += int(clear.sum())
+            kg = host_bits(dec.kc).reshape(L, n_seq, nkv, max_seq, hd)
+            vg = host_bits(dec.vc).reshape(L, n_seq, nkv, max_seq, hd)
+            ko = okc.reshape(n_seq, L, nkv, max_seq, hd)
+            vo = ovc.reshape(n_seq, L, nkv, max_seq, hd)
+            for b in range(n_seq):
+                same_k = (kg[0, b, :, pos[b]] == ko[b, 0, :, pos[b]]).mean()
+                same_v = (vg[0, b, :, pos[b]] == vo[b, 0, :, pos[b]]).mean()
+                assert same_k >= 0.99 and same_v >= 0.99, (step, b, same_k, same_v)
+            # continue from the GPU's tokens (near ties may pick another one)
+            ids = got_ids.astype(np.int32)
+            pos = pos + 1
+    finally:
+        O.set_round_dither(0.0)
+        O.set_threads(1)
+        for d in singles + [dec]:
+            d.close()
+    print(f"ids compared exactly on {compared} of {steps * n_seq} (sequence, step) pairs")
