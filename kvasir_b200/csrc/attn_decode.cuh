@@ -101,6 +101,9 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     // sequence, and the last slot holds every sequence's last, partial chunk.  CTAs are
     // dispatched slot by slot, so full chunks go first and the final wave holds the
     // shortest pieces of work (longest first: a shorter tail).
+    // the combine pass (a programmatic dependent) may launch once every CTA got here;
+    // it still waits for this grid's completion before it reads any partial
+    asm volatile("griddepcontrol.launch_dependents;");
     const int kvh = blockIdx.x, b = blockIdx.y;
     const int from_end = (int)gridDim.z - 1 - (int)blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -375,46 +378,66 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
 }
 
 // Folds the per-chunk partials of every (sequence, kv head) with more than one chunk.
-// Up to kCombineUnroll chunks are loaded in one go (all loads in flight at once);
-// more chunks take further rounds.
-constexpr int kCombineUnroll = 8;
+// The CTA first stages the partials of up to kCombineSmemBytes worth of chunks in
+// shared memory with coalesced loads (one round of memory latency for all of them),
+// then each thread folds its output elements from there: the row max M over the
+// chunks, then L = sum l_c 2^(m_c - M) and O = sum o_c 2^(m_c - M).  Launched as a
+// programmatic dependent of the decode kernel: griddepcontrol.wait holds it until
+// every decode CTA has finished and its partials are visible, while its launch and
+// CTA set-up overlap the decode kernel's last wave.
+constexpr int kCombineSmemBytes = 48 * 1024;
+constexpr int kCombineThreads = 256;
 template <typename T>
-__global__ void __launch_bounds__(256) attn_combine_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(DecodeArgs a) {
+    extern __shared__ float sp[];
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int kvh = blockIdx.x, b = blockIdx.y;
     const int G = a.group;
     const int len = decode_len(a, b);
     const int n_chunks = (len + a.chunk_keys - 1) / a.chunk_keys;
     if (n_chunks <= 1) return;
-    const float* base = a.ws + ((size_t)b * a.n_kv + kvh) * a.max_chunks * (size_t)G * 66;
+    const int per = G * 66;                          // floats per chunk: O[G][64], m[G], l[G]
+    const int cap = kCombineSmemBytes / (per * 4);   // chunks per round (>= 11: G <= 16)
+    const float* base = a.ws + ((size_t)b * a.n_kv + kvh) * a.max_chunks * (size_t)per;
     T* outb = reinterpret_cast<T*>(a.out) + (size_t)b * a.out_row_stride + (size_t)kvh * G * 64;
-    for (int i = threadIdx.x; i < G * 64; i += blockDim.x) {
-        const int r = i >> 6;
-        float M = -INFINITY, L = 0.f, O = 0.f;
-        for (int c0 = 0; c0 < n_chunks; c0 += kCombineUnroll) {
-            float mv[kCombineUnroll], lv[kCombineUnroll], ov[kCombineUnroll];
+    constexpr int kPer = 4;  // outputs per thread: G * 64 <= 1024
+    float M[kPer], L[kPer], O[kPer];
 #pragma unroll
-            for (int k = 0; k < kCombineUnroll; ++k) {
-                const float* p = base + (size_t)(c0 + k) * G * 66;
-                const bool in = c0 + k < n_chunks;
-                mv[k] = in ? p[G * 64 + r] : -INFINITY;
-                lv[k] = in ? p[G * 65 + r] : 0.f;
-                ov[k] = in ? p[i] : 0.f;
+    for (int u = 0; u < kPer; ++u) {
+        M[u] = -INFINITY;
+        L[u] = O[u] = 0.f;
+    }
+    for (int c0 = 0; c0 < n_chunks; c0 += cap) {
+        const int nc = min(cap, n_chunks - c0);
+        const float* src = base + (size_t)c0 * per;
+        __syncthreads();  // the previous round's reads are done
+#pragma unroll 8
+        for (int k = threadIdx.x; k < nc * per; k += kCombineThreads) sp[k] = src[k];
+        __syncthreads();
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            const int i = threadIdx.x + u * kCombineThreads;
+            if (i >= G * 64) break;
+            const int r = i >> 6;
+            float Mn = M[u];
+            for (int c = 0; c < nc; ++c) Mn = fmaxf(Mn, sp[c * per + G * 64 + r]);
+            const float f0 = M[u] == -INFINITY ? 0.f : exp2f(M[u] - Mn);  // earlier rounds
+            float Lu = L[u] * f0, Ou = O[u] * f0;
+            for (int c = 0; c < nc; ++c) {
+                const float mc = sp[c * per + G * 64 + r];
+                const float f = mc == -INFINITY ? 0.f : exp2f(mc - Mn);
+                Lu += sp[c * per + G * 65 + r] * f;
+                Ou += sp[c * per + i] * f;
             }
-            float Mn = M;
-#pragma unroll
-            for (int k = 0; k < kCombineUnroll; ++k) Mn = fmaxf(Mn, mv[k]);
-            const float f0 = M == -INFINITY ? 0.f : exp2f(M - Mn);  // rescale what came before
-            L *= f0;
-            O *= f0;
-#pragma unroll
-            for (int k = 0; k < kCombineUnroll; ++k) {
-                const float f = mv[k] == -INFINITY ? 0.f : exp2f(mv[k] - Mn);
-                L += lv[k] * f;
-                O += ov[k] * f;
-            }
-            M = Mn;
+            M[u] = Mn;
+            L[u] = Lu;
+            O[u] = Ou;
         }
-        outb[i] = Elem<T>::from_f(O / L);
+    }
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        const int i = threadIdx.x + u * kCombineThreads;
+        if (i < G * 64) outb[i] = Elem<T>::from_f(O[u] / L[u]);
     }
 }
 

@@ -403,12 +403,23 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
 #undef KVB_DECODE_LAUNCH
     KVB_CHECK_LAUNCH("attention decode launch");
     if (a.max_chunks > 1) {
-        dim3 g2((unsigned)L.n_kv, (unsigned)L.n_seq);
-        if (L.dtype == KVB_BF16)
-            attn_combine_kernel<__nv_bfloat16><<<g2, 256, 0, stream>>>(a);
-        else
-            attn_combine_kernel<__half><<<g2, 256, 0, stream>>>(a);
-        KVB_CHECK_LAUNCH("attention combine launch");
+        // programmatic dependent launch: set-up overlaps the decode kernel's tail
+        const int per_bytes = a.group * 66 * 4;
+        const int cap = kCombineSmemBytes / per_bytes;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)L.n_kv, (unsigned)L.n_seq);
+        cfg.blockDim = dim3(kCombineThreads);
+        cfg.dynamicSmemBytes = (size_t)(a.max_chunks < cap ? a.max_chunks : cap) * per_bytes;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = L.dtype == KVB_BF16
+                                  ? cudaLaunchKernelEx(&cfg, attn_combine_kernel<__nv_bfloat16>, a)
+                                  : cudaLaunchKernelEx(&cfg, attn_combine_kernel<__half>, a);
+        if (e != cudaSuccess) return cuda_fail(e, "attention combine launch");
     }
     return KVB_OK;
 }
