@@ -371,7 +371,7 @@ def cfg3(args):
     O.attention(sub, kb, vb, T, 0, 4, 1, hd, T)
     cpu_s = (time.perf_counter() - t0) * (n_seq * nkv)
     O.set_threads(1)
-    lib_ref = _library_prefill_reference(n_seq, T, nq, nkv, hd, flops, flush)
+    lib_ref = _library_prefill_reference(g, n_seq, T, nq, nkv, hd, flops, flush)
     _emit({"workload": "cfg3: prefill 4 x 2048, causal GQA attention 32/8 heads hd 64 (tcgen05)",
            "metric": "TFLOP/s", "value": tflops, "unit": "TFLOP/s", "us": ms_att * 1e3,
            "flops": flops, "frac_of_peak": tflops / peaks["bf16_tflops"],
@@ -386,11 +386,15 @@ def cfg3(args):
            "equal_to_contiguous": paged_equal})
 
 
-def _library_prefill_reference(n_seq, T, nq, nkv, hd, flops, flush):
+def _library_prefill_reference(g, n_seq, T, nq, nkv, hd, flops, flush):
     """torch SDPA with the cuDNN backend on the same shapes (causal, bf16), timed the
     same way: what NVIDIA's own attention reaches on this GPU at head_dim 64.  A
     comparison only; nothing of this library runs through it.  K and V are expanded
-    to the query heads (cuDNN's GQA support varies by version)."""
+    to the query heads (cuDNN's GQA support varies by version).  Its accuracy is
+    reported beside its speed: the largest difference from this library's f32 rows
+    (kvb_attention_prefill_f32, within ~1e-5 of the f64 oracle on these shapes) and
+    the share of its bf16 outputs outside this library's 16-bit attention bar,
+    2e-3 + 2^-8 |want|."""
     import torch.nn.functional as F
     try:
         from torch.nn.attention import SDPBackend, sdpa_kernel
@@ -405,8 +409,23 @@ def _library_prefill_reference(n_seq, T, nq, nkv, hd, flops, flush):
             for _ in range(3):
                 f()
             ms = time_each(f, 30, flush)
+            lib_out = f()
+        # the same inputs through this library: q in the qkv rows, K / V as the caches
+        stride = (nq + 2 * nkv) * hd
+        qkv = torch.zeros(n_seq, T, stride, dtype=torch.bfloat16, device="cuda")
+        qkv[:, :, :nq * hd] = q.permute(0, 2, 1, 3).reshape(n_seq, T, nq * hd)
+        kc = k[:, ::nq // nkv].contiguous()
+        vc = v[:, ::nq // nkv].contiguous()
+        out32 = torch.empty(n_seq * T * nq * hd, dtype=torch.float32, device="cuda")
+        g.attention_prefill_f32(qkv.reshape(-1), kc.reshape(-1), vc.reshape(-1), out32, n_seq, T,
+                                0, nq, nkv, hd, T)
+        want = out32.view(n_seq, T, nq, hd).permute(0, 2, 1, 3).double()
+        err = (lib_out.double() - want).abs()
+        outside = (err > 2e-3 + 2.0 ** -8 * want.abs()).double().mean()
         return {"impl": "torch SDPA, cuDNN backend (K/V expanded to 32 heads)",
-                "tflops": flops / (ms * 1e-3) / 1e12, "us": ms * 1e3}
+                "tflops": flops / (ms * 1e-3) / 1e12, "us": ms * 1e3,
+                "max_abs_err_vs_f32_rows": float(err.max()),
+                "share_outside_16bit_attention_bar": float(outside)}
     except Exception as e:  # a torch build without the backend
         return {"impl": "torch SDPA, cuDNN backend", "unavailable": str(e).splitlines()[0][:200]}
 
