@@ -282,6 +282,8 @@ def run_decode(args):
     max_seq = ctx + W + 2 * K + 2
     bs = args.paged or None
     dec = Decoder(cfg, n_local, max_seq, device=f"cuda:{local}", seed=0, paged_block_size=bs)
+    # greedy steps end in kvb_lm_head_argmax where it applies (32 or fewer sequences per GPU)
+    dec.set_fused_lm_head(not args.unfused_lm_head)
     # every sequence's context is seeded by its global index: the same data at any N
     dec.fill_kv_normal(seed=1000, first_seq=first)
     dec.set_lengths(ctx)
@@ -411,6 +413,8 @@ def run_decode(args):
                                    "store arrival check" if dist is not None else "one rank")},
             "gpu_launches": K * own,
             "launches_per_step": {"own": own, "cublas": lib},
+            "lm_head": ("kvb_lm_head_argmax (LM head + argmax in one pass)"
+                        if lib == 4 * cfg.num_layers else "cuBLAS f32 logits + kvb_argmax_f32"),
             "roofline": {"bound": "hbm", "achieved": achieved,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
@@ -480,7 +484,8 @@ def main():
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kernel", choices=["kernel", "reference"])
-    ap.add_argument("--workload", default="cfg5", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "sample", "attn5"])
+    ap.add_argument("--workload", default="cfg5", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "sample", "attn5",
+                                                 "lmhead"])
     ap.add_argument("--seqs", type=int, default=256, help="total sequences (cfg5)")
     ap.add_argument("--context", type=int, default=16384, help="KV tokens per sequence (cfg5)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -488,6 +493,8 @@ def main():
     ap.add_argument("--ncu-window", action="store_true",
                     help="call cudaProfilerStart just before the first timed decode steps, so that "
                          "`ncu --profile-from-start off` lists only step launches (cfg4, cfg5)")
+    ap.add_argument("--unfused-lm-head", action="store_true",
+                    help="cfg5: keep the cuBLAS LM head + argmax even where the fused pass applies")
     ap.add_argument("--ids-out", default="",
                     help="cfg5: write the gathered [steps, seqs] table of sampled ids (.npy, rank 0)")
     ap.add_argument("--paged", type=int, default=0,

@@ -465,10 +465,37 @@ def cfg4(args):
         kv = B * (ctx + steps / 2) * cfg.num_layers * cfg.num_kv_heads * cfg.head_dim * 2 * 2
         step_bytes = dec.weight_bytes() + kv + B * cfg.vocab_size * 4
         roof_tps = B / (step_bytes / (peaks["hbm_gbs"] * 1e9))
+        own, lib = dec.launches_per_step()
         _emit({"workload": f"cfg4: 16-layer decode, batch {B}, context 1024, 256 greedy steps",
                "metric": "tokens/s", "value": tps, "unit": "tokens/s", "ms_per_step": ms / steps,
                "bytes_per_step": step_bytes, "hbm_roofline_tokens_s": roof_tps,
-               "frac_of_roofline": tps / roof_tps, "peak": f"{peaks['hbm_gbs']} GB/s ({kind})"})
+               "frac_of_roofline": tps / roof_tps, "peak": f"{peaks['hbm_gbs']} GB/s ({kind})",
+               "lm_head": "cuBLAS f32 logits + kvb_argmax_f32",
+               "launches_per_step": {"own": own, "cublas": lib}})
+        # the same greedy steps with the LM head and the argmax in one pass
+        dec.set_fused_lm_head(True)
+        dec.set_lengths(ctx)
+        for _ in range(3):
+            dec.step()
+        dec.set_lengths(ctx)
+        torch.cuda.synchronize()
+        a.record(s)
+        for _ in range(steps):
+            dec.step()
+        b.record(s)
+        b.synchronize()
+        ms_f = a.elapsed_time(b)
+        own, lib = dec.launches_per_step()
+        fused_bytes = step_bytes - B * cfg.vocab_size * 4
+        _emit({"workload": f"cfg4: 16-layer decode, batch {B}, context 1024, 256 greedy steps, "
+                           f"LM head + argmax fused",
+               "metric": "tokens/s", "value": B * steps / (ms_f * 1e-3), "unit": "tokens/s",
+               "ms_per_step": ms_f / steps, "bytes_per_step": fused_bytes,
+               "frac_of_roofline": (B * steps / (ms_f * 1e-3)) /
+                                   (B / (fused_bytes / (peaks["hbm_gbs"] * 1e9))),
+               "lm_head": "kvb_lm_head_argmax (f32 logits never stored)",
+               "launches_per_step": {"own": own, "cublas": lib}})
+        dec.set_fused_lm_head(False)
         # the same steps with device-side temperature / top-p sampling in place of argmax,
         # and the two sampling kernels alone on this step's logits
         dec.set_sampling(0.8, 0.95, seed=1)
@@ -529,6 +556,53 @@ def sample(args):
 
 
 
+# ----------------------------------------------------------------------------- LM head + argmax
+def lmhead(args):
+    """The tied Llama-3.2-1B LM head (128256 x 2048 bf16, 525 MB) and greedy argmax
+    for 1, 8 and 32 rows: kvb_lm_head_argmax (one pass, logits never stored)
+    against kvb_linear (cuBLAS, f32 logits, autotuned) + kvb_argmax_f32.  The
+    weights are far above L2, so back-to-back launches read them from HBM."""
+    peaks, kind = _peaks()
+    g = Gpu(0)
+    H, V = 2048, 128256
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    w = torch.empty(V * H, dtype=torch.bfloat16, device="cuda").normal_(0, 0.02, generator=gen)
+    from kvasir_b200 import _lib as L
+    import ctypes as C
+    blas = C.c_void_p()
+    L.lib().kvb_blas_create(C.byref(blas))
+    L.lib().kvb_blas_set_autotune(blas, 1)
+    for B in (1, 8, 32):
+        x = torch.randn(B * H, generator=gen, device="cuda").to(torch.bfloat16)
+        ids_f = torch.empty(B, dtype=torch.int32, device="cuda")
+        ids_u = torch.empty(B, dtype=torch.int32, device="cuda")
+        y = torch.empty(B * V, dtype=torch.float32, device="cuda")
+        ws = torch.empty(int(L.lib().kvb_lm_head_argmax_workspace_bytes(B)), dtype=torch.uint8,
+                         device="cuda")
+        fused = lambda: g.lm_head_argmax(x, w, B, H, V, ids_f, workspace=ws)
+
+        def unfused():
+            s = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+            L.lib().kvb_linear(blas, s, C.c_void_p(x.data_ptr()), x.numel(), C.c_void_p(w.data_ptr()),
+                               w.numel(), C.c_void_p(y.data_ptr()), y.numel(), B, H, V, L.KVB_BF16, 1)
+            g.argmax(y, B, V, ids_u)
+
+        for f in (fused, unfused):
+            for _ in range(3):
+                f()
+        torch.cuda.synchronize()
+        us_f = time_loop(fused, 30) * 1e3
+        us_u = time_loop(unfused, 30) * 1e3
+        wb = V * H * 2
+        _emit({"workload": f"LM head + greedy argmax, {B} rows, vocab {V}, hidden {H}",
+               "metric": "us", "value": us_f, "unit": "us", "fused_us": us_f,
+               "cublas_plus_argmax_us": us_u, "fused_weight_gbs": wb / (us_f * 1e-6) / 1e9,
+               "frac_of_peak": wb / (us_f * 1e-6) / 1e9 / peaks["hbm_gbs"],
+               "ids_equal": bool(torch.equal(ids_f, ids_u)),
+               "peak": f"{peaks['hbm_gbs']} GB/s ({kind})"})
+    L.lib().kvb_blas_destroy(blas)
+
+
 # ----------------------------------------------------------------------------- config 5 kernel
 def attn5(args):
     """The config-5 step's dominant launch alone: RoPE + KV append + split-KV decode
@@ -576,4 +650,4 @@ def attn5(args):
 
 def run(name, args):
     {"cfg1": cfg1, "cfg2": cfg2, "cfg3": cfg3, "cfg4": cfg4, "sample": sample,
-     "attn5": attn5}[name](args)
+     "attn5": attn5, "lmhead": lmhead}[name](args)

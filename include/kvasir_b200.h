@@ -338,6 +338,23 @@ int kvb_rope_attention_decode_paged(kvb_stream_t stream, const void* qkv, size_t
 int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t vocab,
                    int32_t* ids, int32_t* advance, int32_t* advance2);
 
+/* The tied LM head and greedy argmax in one pass, f32 logits never stored
+ * (replaces gemm::linear_f32 of the LM head, engine/src/gpu/gemm.rs:90-115,
+ * followed by kvb_argmax_f32).  ids[r] = the first index of the maximum over
+ * v < vocab of sum_k x[r, k] w[v, k] (f32 accumulation on the tensor cores),
+ * with kvb_argmax_f32's rule: NaN never wins, a -inf never wins a tie, a row
+ * with nothing above -inf gives 0; advance / advance2 as for kvb_argmax_f32.
+ * x [rows, hidden], w [vocab, hidden] (16-bit, dtype).  rows <= 32, hidden a
+ * multiple of 64 with rows <= 16 ? hidden <= 4096 : hidden <= 2048, 16-byte
+ * aligned buffers, else KVB_ERR_UNSUPPORTED.  The workspace
+ * (kvb_lm_head_argmax_workspace_bytes(rows)) holds per-CTA partials; its
+ * contents need no initialisation.  Two launches. */
+size_t kvb_lm_head_argmax_workspace_bytes(size_t rows);
+int kvb_lm_head_argmax(kvb_stream_t stream, const void* x, size_t x_len, const void* w,
+                       size_t w_len, size_t rows, size_t hidden, size_t vocab, void* workspace,
+                       size_t workspace_len, int32_t* ids, int32_t* advance, int32_t* advance2,
+                       int dtype);
+
 /* Temperature / top-p sampling on the device (the reference plans it on the
  * host over copied logits: kvasir DESIGN.md:24,109, "greedy / temperature /
  * top-p", seeded).  Per row: integer weights w_i = floor(2^32 * exp((l_i -
@@ -427,6 +444,14 @@ int kvb_decoder_launches_per_step(kvb_decoder_t dec, int* own, int* library);
  * its position, so every step draws afresh and a rerun from the same state
  * repeats.  The next step re-records its graph. */
 int kvb_decoder_set_sampling(kvb_decoder_t dec, float temperature, float top_p, uint64_t seed);
+/* enable != 0: greedy steps (temperature <= 0) end with kvb_lm_head_argmax (the
+ * LM head and the argmax in one pass) where it applies (n_seq <= 32 and its
+ * hidden / alignment limits), so kvb_decoder_logits is not written by those
+ * steps; otherwise, and by default, the LM head is kvb_linear (f32 logits kept)
+ * and kvb_argmax_f32.  The ids agree except where two logits of a row are within
+ * the f32 rounding of their sums.  The next step re-records its graph.  New: the
+ * fusion the reference's plan lists after its GEMM (engine/src/gpu/gemm.rs:90-115). */
+int kvb_decoder_set_fused_lm_head(kvb_decoder_t dec, int enable);
 /* Untied checkpoints (reference Weights::head, engine/src/model/weights.rs:29-32):
  * the LM head [vocab, hidden] used instead of the embedding table.  NULL goes
  * back to the tied head.  The next step re-records its graph. */

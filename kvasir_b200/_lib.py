@@ -87,6 +87,9 @@ SIGNATURES = {
     "kvb_attention_prefill_f32": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _sz, _sz, _sz, _sz, _sz, _sz,
                                      _sz, _sz, _int]),
     "kvb_argmax_f32": (_int, [_p, _p, _sz, _sz, _p, _p, _p]),
+    "kvb_lm_head_argmax_workspace_bytes": (_sz, [_sz]),
+    "kvb_decoder_set_fused_lm_head": (_int, [_p, _int]),
+    "kvb_lm_head_argmax": (_int, [_p, _p, _sz, _p, _sz, _sz, _sz, _sz, _p, _sz, _p, _p, _p, _int]),
     "kvb_rope_attention_decode_paged": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _p, _sz, _p, _sz, _sz,
                                                _p, _sz, _sz, _sz, _sz, _sz, C.c_float, _p, _sz, _p,
                                                _sz, _int]),

@@ -17,6 +17,7 @@
 #include "attn_prefill.cuh"
 #include "elementwise.cuh"
 #include "kvb_host.h"
+#include "lm_head.cuh"
 #include "norm.cuh"
 #include "rope.cuh"
 #include "sample.cuh"
@@ -1600,6 +1601,77 @@ int kvb_sample_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t
              : launch_sample<kSampleCluster>(stream, logits, rows, vocab, 1.0f / temperature,
                                              top_p, seed, counters, ids, advance, advance2, vec4);
     if (e != cudaSuccess) return cuda_fail(e, "sample launch");
+    return KVB_OK;
+}
+
+// ------------------------------------------------------------------ LM head + argmax
+size_t kvb_lm_head_argmax_workspace_bytes(size_t rows) {
+    return rows * (size_t)kLmMaxCtas * (sizeof(float) + sizeof(int32_t));
+}
+
+int kvb_lm_head_argmax(kvb_stream_t stream, const void* x, size_t x_len, const void* w,
+                       size_t w_len, size_t rows, size_t hidden, size_t vocab, void* workspace,
+                       size_t workspace_len, int32_t* ids, int32_t* advance, int32_t* advance2,
+                       int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(x_len == rows * hidden, "lm_head_argmax: x has %zu elems, want %zux%zu", x_len, rows,
+              hidden);
+    KVB_CHECK(w_len == vocab * hidden, "lm_head_argmax: w has %zu elems, want %zux%zu", w_len,
+              vocab, hidden);
+    KVB_CHECK(vocab > 0 && fits_i32(vocab) && fits_i32(hidden),
+              "lm_head_argmax: vocab %zu / hidden %zu out of range", vocab, hidden);
+    KVB_CHECK(ids != nullptr, "lm_head_argmax: null ids");
+    if (rows == 0) return KVB_OK;
+    const size_t need = kvb_lm_head_argmax_workspace_bytes(rows);
+    KVB_CHECK(workspace != nullptr && workspace_len >= need,
+              "lm_head_argmax: workspace of %zu bytes, need %zu", workspace_len, need);
+    const int n = rows <= 16 ? 16 : 32;
+    if (!(rows <= (size_t)kLmMaxRows && hidden > 0 && hidden % kLmK == 0 &&
+          (size_t)n * hidden * 2 <= (size_t)kLmMaxXBytes && aligned(x, 16) && aligned(w, 16) &&
+          aligned(workspace, 16)))
+        return fail(KVB_ERR_UNSUPPORTED,
+                    "lm_head_argmax: needs rows <= %d, hidden a multiple of 64 with rows' x in "
+                    "128 KB, 16-byte aligned buffers (use kvb_linear + kvb_argmax_f32)",
+                    kLmMaxRows);
+    CUtensorMap wmap, xmap;
+    {
+        const uint64_t dims[2] = {hidden, vocab};
+        const uint64_t strides[1] = {hidden * 2};
+        const uint32_t box[2] = {(uint32_t)kLmK, (uint32_t)kLmRows};
+        int st = encode_tmap(&wmap, w, 2, dims, strides, box, dtype);
+        if (st) return st;
+    }
+    {
+        const uint64_t dims[2] = {hidden, rows};
+        const uint64_t strides[1] = {hidden * 2};
+        const uint32_t box[2] = {(uint32_t)kLmK, (uint32_t)n};  // rows past `rows` read as 0
+        int st = encode_tmap(&xmap, x, 2, dims, strides, box, dtype);
+        if (st) return st;
+    }
+    LmArgs a;
+    a.vocab = (int)vocab;
+    a.hidden = (int)hidden;
+    a.rows = (int)rows;
+    a.n_tiles = (int)((vocab + kLmRows - 1) / kLmRows);
+    int grid = num_sms();
+    if (grid > a.n_tiles) grid = a.n_tiles;
+    if (grid > kLmMaxCtas) grid = kLmMaxCtas;
+    a.part_v = static_cast<float*>(workspace);
+    a.part_i = reinterpret_cast<int32_t*>(static_cast<float*>(workspace) + (size_t)kLmMaxCtas * rows);
+    const uint32_t fmt = dtype == KVB_BF16 ? 1u : 0u;
+    const int smem = lm_smem_bytes(n, (int)hidden);
+    if (n == 16) {
+        set_max_smem(lm_head_argmax_kernel<16>, lm_smem_bytes(16, kLmMaxXBytes / 32));
+        lm_head_argmax_kernel<16><<<grid, kLmThreads, smem, stream>>>(wmap, xmap, a, fmt);
+    } else {
+        set_max_smem(lm_head_argmax_kernel<32>, lm_smem_bytes(32, kLmMaxXBytes / 64));
+        lm_head_argmax_kernel<32><<<grid, kLmThreads, smem, stream>>>(wmap, xmap, a, fmt);
+    }
+    KVB_CHECK_LAUNCH("lm_head_argmax launch");
+    lm_head_argmax_finish_kernel<<<(unsigned)rows, 32, 0, stream>>>(a.part_v, a.part_i, grid,
+                                                                    (int)rows, ids, advance,
+                                                                    advance2);
+    KVB_CHECK_LAUNCH("lm_head_argmax finish launch");
     return KVB_OK;
 }
 

@@ -29,8 +29,9 @@ constexpr size_t kBlasWorkspace = 32u << 20;
 size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 struct Layout {  // byte offsets into the workspace
-    size_t x, h, qkv, attn, o, gu, act, logits, ids_in, ids_out, pos, lens, attn_ws, blas_ws, total;
-    size_t attn_ws_len;
+    size_t x, h, qkv, attn, o, gu, act, logits, ids_in, ids_out, pos, lens, attn_ws, lm_ws, blas_ws,
+        total;
+    size_t attn_ws_len, lm_ws_len;
 };
 
 Layout make_layout(const kvb_decoder_config& c) {
@@ -59,6 +60,8 @@ Layout make_layout(const kvb_decoder_config& c) {
     L.attn_ws_len = kvb_attention_decode_workspace_bytes(B, (size_t)c.max_seq, (size_t)c.n_q,
                                                          (size_t)c.n_kv, (size_t)c.head_dim);
     L.attn_ws = take(L.attn_ws_len);
+    L.lm_ws_len = B <= 32 ? kvb_lm_head_argmax_workspace_bytes(B) : 0;
+    L.lm_ws = take(L.lm_ws_len);
     L.blas_ws = take(kBlasWorkspace);
     L.total = off;
     return L;
@@ -75,6 +78,7 @@ struct kvb_decoder_s {
     float temperature = 0.f;        // <= 0: greedy
     float top_p = 1.f;
     uint64_t seed = 0;
+    bool fused_lm_head = false;     // greedy steps: kvb_lm_head_argmax where it applies
     const void* final_norm = nullptr;
     std::vector<const void*> attn_norm, w_qkv, w_o, mlp_norm, w_gu, w_down;
     uint8_t* kc = nullptr;
@@ -182,15 +186,27 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
                              B, H, c.eps, dt),
              false);
     }
-    STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->lm_head ? d->lm_head : d->embed,
-                    (size_t)c.vocab * H, d->at<float>(L.logits), B * (size_t)c.vocab, B, H,
-                    (size_t)c.vocab, dt, 1),
-         true);
-    // sampling reads each sequence's position as its counter, then advances it
-    STEP(kvb_sample_f32(s, d->at<float>(L.logits), B, (size_t)c.vocab, d->temperature, d->top_p,
-                        d->seed, d->at<int32_t>(L.pos), d->at<int32_t>(L.ids_out),
-                        d->at<int32_t>(L.pos), d->at<int32_t>(L.lens)),
-         false);
+    const void* head = d->lm_head ? d->lm_head : d->embed;
+    int fst = KVB_ERR_UNSUPPORTED;
+    if (d->fused_lm_head && d->temperature <= 0.f && L.lm_ws_len > 0) {
+        // LM head + greedy argmax in one pass: the logits are never stored
+        fst = kvb_lm_head_argmax(s, d->at(L.h), B * H, head, (size_t)c.vocab * H, B, H,
+                                 (size_t)c.vocab, d->at(L.lm_ws), L.lm_ws_len,
+                                 d->at<int32_t>(L.ids_out), d->at<int32_t>(L.pos),
+                                 d->at<int32_t>(L.lens), dt);
+        if (fst != KVB_OK && fst != KVB_ERR_UNSUPPORTED) return fst;
+        if (fst == KVB_OK) own += 2;  // the pass and the merge of its per-CTA partials
+    }
+    if (fst != KVB_OK) {
+        STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, head, (size_t)c.vocab * H,
+                        d->at<float>(L.logits), B * (size_t)c.vocab, B, H, (size_t)c.vocab, dt, 1),
+             true);
+        // sampling reads each sequence's position as its counter, then advances it
+        STEP(kvb_sample_f32(s, d->at<float>(L.logits), B, (size_t)c.vocab, d->temperature, d->top_p,
+                            d->seed, d->at<int32_t>(L.pos), d->at<int32_t>(L.ids_out),
+                            d->at<int32_t>(L.pos), d->at<int32_t>(L.lens)),
+             false);
+    }
     cudaError_t e = cudaMemcpyAsync(d->at(L.ids_in), d->at(L.ids_out), B * 4,
                                     cudaMemcpyDeviceToDevice, s);
     if (e != cudaSuccess) return kvb::cuda_fail(e, "decoder: ids copy");
@@ -315,6 +331,13 @@ int kvb_decoder_set_sampling(kvb_decoder_t d, float temperature, float top_p, ui
     d->temperature = temperature;
     d->top_p = top_p;
     d->seed = seed;
+    drop_graph(d);
+    return KVB_OK;
+}
+
+int kvb_decoder_set_fused_lm_head(kvb_decoder_t d, int enable) {
+    KVB_CHECK(d, "decoder_set_fused_lm_head: null decoder");
+    d->fused_lm_head = enable != 0;
     drop_graph(d);
     return KVB_OK;
 }

@@ -188,6 +188,11 @@ class Decoder:
         check(self._lib.kvb_decoder_set_sampling(self._h, temperature, top_p,
                                                  seed & 0xFFFFFFFFFFFFFFFF))
 
+    def set_fused_lm_head(self, enable: bool = True) -> None:
+        """Greedy steps through kvb_lm_head_argmax (LM head + argmax in one pass;
+        self.logits is then not written by those steps)."""
+        check(self._lib.kvb_decoder_set_fused_lm_head(self._h, 1 if enable else 0))
+
     def set_lengths(self, cur_len) -> None:
         """Tokens already in each sequence's cache; the next step writes there."""
         arr = np.ascontiguousarray(np.broadcast_to(np.asarray(cur_len, np.int32), (self.n_seq,)))

@@ -323,6 +323,19 @@ class Gpu:
                                                   n_seq, t, pos0, n_q, n_kv, head_dim, max_seq,
                                                   dtype_tag(qkv)))
 
+    def lm_head_argmax(self, x, w, rows, hidden, vocab, ids, workspace=None, advance=None,
+                       advance2=None):
+        """kvb_lm_head_argmax: greedy ids of x @ w^T (f32 logits never stored)."""
+        if ids.dtype != torch.int32 or ids.numel() != rows:
+            raise ShapeError("lm_head_argmax: int32 ids of rows elements expected")
+        if workspace is None:
+            nb = int(self._lib.kvb_lm_head_argmax_workspace_bytes(rows))
+            workspace = torch.empty(max(nb, 16), dtype=torch.uint8, device=x.device)
+        ws_len = workspace.numel() * workspace.element_size()
+        check(self._lib.kvb_lm_head_argmax(self._s, _ptr(x), x.numel(), _ptr(w), w.numel(), rows,
+                                           hidden, vocab, _ptr(workspace), ws_len, _ptr(ids),
+                                           _ptr(advance), _ptr(advance2), dtype_tag(x)))
+
     def argmax(self, logits, rows, vocab, ids, advance=None, advance2=None):
         if logits.dtype != torch.float32 or ids.dtype != torch.int32:
             raise ShapeError("argmax: f32 logits and int32 ids expected")

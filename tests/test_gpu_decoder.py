@@ -165,3 +165,46 @@ def test_decoder_paged_cache_equals_contiguous():
         assert torch.equal(decs[0].ids_out, decs[1].ids_out), f"step {step}"
     for d in decs:
         d.close()
+
+
+def test_decoder_fused_lm_head_equals_unfused_ids():
+    """kvb_decoder_set_fused_lm_head: greedy steps through kvb_lm_head_argmax give the
+    unfused step's ids (kvb_linear's f32 logits + kvb_argmax_f32) wherever the
+    unfused logits' top-2 margin exceeds twice the f32 rounding bound of the sums
+    (hidden * 2^-24 * sum |x w|, at most ~1.2e-3 here); both decoders are fed the
+    same ids every step.  The step launches one cuBLAS GEMM fewer and one kernel of
+    this library more (the LM-head pass and the merge of its partials, in place of
+    the argmax)."""
+    from kvasir_b200.decoder import Decoder
+    cfg = _tiny_cfg()
+    n_seq, max_seq = 5, 64
+    a = Decoder(cfg, n_seq, max_seq, seed=6)
+    b = Decoder(cfg, n_seq, max_seq, weights=a.w)
+    a.kc.normal_(0, 1)
+    a.vc.normal_(0, 1)
+    b.kc.copy_(a.kc)
+    b.vc.copy_(a.vc)
+    for d in (a, b):
+        d.set_lengths([3, 20, 33, 40, 50])
+    b.set_fused_lm_head(True)
+    ids = torch.tensor([1, 22, 333, 444, 999], dtype=torch.int32, device="cuda")
+    compared = 0
+    for step in range(4):
+        a.ids_in.copy_(ids)
+        b.ids_in.copy_(ids)
+        a.step()
+        b.step()
+        torch.cuda.synchronize()
+        la = a.logits.cpu().numpy().astype(np.float64)
+        top2 = np.sort(la, axis=1)[:, -2:]
+        clear = (top2[:, 1] - top2[:, 0]) > 5e-3
+        ia, ib = a.ids_out.cpu().numpy(), b.ids_out.cpu().numpy()
+        np.testing.assert_array_equal(ib[clear], ia[clear])
+        compared += int(clear.sum())
+        ids = a.ids_out.clone()
+    assert compared >= 15
+    own_a, lib_a = a.launches_per_step()
+    own_b, lib_b = b.launches_per_step()
+    assert (own_b, lib_b) == (own_a + 1, lib_a - 1)
+    a.close()
+    b.close()
