@@ -51,9 +51,13 @@ class RankFailure(RuntimeError):
 
 
 def _default_store():
+    """The key-value store of the initialised default process group (under a prefix)."""
     import torch.distributed as dist
     from torch.distributed import distributed_c10d as c10d
-    return dist.PrefixStore("kvb_monitor", c10d._get_default_store())
+    get = getattr(c10d, "_get_default_store", None)
+    if get is None or not dist.is_initialized():
+        raise RuntimeError("RankMonitor: no default process group store; pass store=")
+    return dist.PrefixStore("kvb_monitor", get())
 
 
 class RankMonitor:
