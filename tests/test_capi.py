@@ -121,3 +121,22 @@ def test_noalloc_scratch_size_matches_header():
     with open(L.HEADER) as f:
         m = re.search(r"#define KVB_NOALLOC_SCRATCH_BYTES \((\d+)u << (\d+)\)", f.read())
     assert m and int(m.group(1)) << int(m.group(2)) == L.KVB_NOALLOC_SCRATCH_BYTES
+
+
+def test_lm_head_argmax_and_prefill_f32_check_shapes_before_launch():
+    lib = L.lib()
+    fake = C.c_void_p(0x1000)
+    st, msg = _status(lib.kvb_lm_head_argmax, None, fake, 4 * 64 - 1, fake, 100 * 64, 4, 64, 100,
+                      fake, 1 << 20, fake, None, None, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "lm_head_argmax: x has" in msg
+    st, msg = _status(lib.kvb_lm_head_argmax, None, fake, 4 * 64, fake, 100 * 64, 4, 64, 100,
+                      fake, 16, fake, None, None, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "workspace" in msg
+    st, msg = _status(lib.kvb_lm_head_argmax, None, fake, 4 * 64, fake, 100 * 64, 4, 64, 100,
+                      fake, 1 << 20, None, None, None, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "null ids" in msg
+    assert lib.kvb_lm_head_argmax_workspace_bytes(32) >= 32 * 8 * 148
+    # one sequence of 2 tokens, 8 / 2 heads, max_seq 16: a cache one element short
+    st, msg = _status(lib.kvb_attention_prefill_f32, None, fake, 2 * 768, fake, fake,
+                      2 * 16 * 64 - 1, fake, 2 * 8 * 64, 1, 2, 0, 8, 2, 64, 16, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "bad cache sizes" in msg

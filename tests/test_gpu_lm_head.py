@@ -126,6 +126,20 @@ def test_lm_head_argmax_ties_nan_inf_and_partial_tile(g):
     assert got3[0] == 3
 
 
+@pytest.mark.parametrize("rows,hidden,vocab", [(3, 4096, 300), (16, 4096, 127), (2, 128, 5)])
+def test_lm_head_argmax_shape_limits(g, rows, hidden, vocab):
+    """hidden 4096 on the 16-column path (x fills its 128 KB), vocab below one tile."""
+    rng = np.random.default_rng(rows + hidden + vocab)
+    x = normal16(rng, rows * hidden)
+    w = normal16(rng, vocab * hidden, std=0.05)
+    got = _fused(g, x, w, rows, hidden, vocab, adv=True)
+    cub, logits = _cublas_argmax(g, x, w, rows, hidden, vocab)
+    top2 = np.sort(logits, axis=1)[:, -2:]
+    clear = top2[:, 1] - top2[:, 0] > 1e-2
+    np.testing.assert_array_equal(got[clear], cub[clear])
+    assert ((got >= 0) & (got < vocab)).all()
+
+
 def test_lm_head_argmax_rejects_unsupported(g):
     from kvasir_b200.gpu import UnsupportedError
     x = torch.zeros(33 * 64, dtype=torch.bfloat16, device="cuda")
@@ -133,3 +147,8 @@ def test_lm_head_argmax_rejects_unsupported(g):
     ids = torch.zeros(33, dtype=torch.int32, device="cuda")
     with pytest.raises(UnsupportedError, match="rows <= 32"):
         g.lm_head_argmax(x, w, 33, 64, 256, ids)
+    # 17 rows take the 32-column path: x of 32 x 4096 would not fit its 128 KB
+    x2 = torch.zeros(17 * 4096, dtype=torch.bfloat16, device="cuda")
+    w2 = torch.zeros(64 * 4096, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(UnsupportedError):
+        g.lm_head_argmax(x2, w2, 17, 4096, 64, torch.zeros(17, dtype=torch.int32, device="cuda"))
