@@ -208,3 +208,31 @@ def test_decoder_fused_lm_head_equals_unfused_ids():
     assert (own_b, lib_b) == (own_a + 1, lib_a - 1)
     a.close()
     b.close()
+
+
+def test_fill_kv_by_global_index_is_the_same_paged_and_contiguous():
+    """Decoder.fill_kv_normal(first_seq=g) gives each sequence the contents of its
+    global index alone: a paged decoder (blocks scattered by its table) and a
+    contiguous one seeded alike step to the same logits, bit for bit, and a decoder
+    holding only sequences 2.. (first_seq=2) holds exactly their caches."""
+    from kvasir_b200.decoder import Decoder
+    cfg = _tiny_cfg()
+    n_seq, max_seq = 4, 192
+    a = Decoder(cfg, n_seq, max_seq, seed=8)
+    b = Decoder(cfg, n_seq, max_seq, weights=a.w, seed=8, paged_block_size=64)
+    c = Decoder(cfg, n_seq - 2, max_seq, weights=a.w, seed=8)
+    a.fill_kv_normal(seed=5, first_seq=0)
+    b.fill_kv_normal(seed=5, first_seq=0)
+    c.fill_kv_normal(seed=5, first_seq=2)
+    torch.testing.assert_close(c.kc, a.kc[:, 2:], rtol=0, atol=0)
+    lens = np.array([7, 64, 100, 150], np.int32)
+    ids = torch.tensor([5, 50, 500, 900], dtype=torch.int32, device="cuda")
+    for d in (a, b):
+        d.set_lengths(lens)
+        d.ids_in.copy_(ids)
+        d.step()
+    torch.cuda.synchronize()
+    assert torch.equal(a.logits, b.logits)
+    assert torch.equal(a.ids_out, b.ids_out)
+    for d in (a, b, c):
+        d.close()
