@@ -284,6 +284,8 @@ def run_decode(args):
     dec = Decoder(cfg, n_local, max_seq, device=f"cuda:{local}", seed=0, paged_block_size=bs)
     # greedy steps end in kvb_lm_head_argmax where it applies (32 or fewer sequences per GPU)
     dec.set_fused_lm_head(not args.unfused_lm_head)
+    row_proj = args.projections == "rows" or (args.projections == "auto" and n_local <= 32)
+    dec.set_row_projections(row_proj)
     # every sequence's context is seeded by its global index: the same data at any N
     dec.fill_kv_normal(seed=1000, first_seq=first)
     dec.set_lengths(ctx)
@@ -413,8 +415,11 @@ def run_decode(args):
                                    "store arrival check" if dist is not None else "one rank")},
             "gpu_launches": K * own,
             "launches_per_step": {"own": own, "cublas": lib},
+            "projections": ("kvb_linear_rows + kvb_linear_silu_mul" if row_proj
+                            else "cuBLAS (autotuned) + kvb_silu_mul"),
             "lm_head": ("kvb_lm_head_argmax (LM head + argmax in one pass)"
-                        if lib == 4 * cfg.num_layers else "cuBLAS f32 logits + kvb_argmax_f32"),
+                        if lib == (0 if row_proj else 4 * cfg.num_layers)
+                        else "cuBLAS f32 logits + kvb_argmax_f32"),
             "roofline": {"bound": "hbm", "achieved": achieved,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved / peaks["hbm_gbs"], "traffic": traffic,
@@ -495,6 +500,10 @@ def main():
                          "`ncu --profile-from-start off` lists only step launches (cfg4, cfg5)")
     ap.add_argument("--unfused-lm-head", action="store_true",
                     help="cfg5: keep the cuBLAS LM head + argmax even where the fused pass applies")
+    ap.add_argument("--projections", default="auto", choices=["auto", "cublas", "rows"],
+                    help="cfg5: qkv / o / gate-up / down projections on cuBLAS or on "
+                         "kvb_linear_rows + kvb_linear_silu_mul (auto: rows for <= 32 "
+                         "sequences per GPU)")
     ap.add_argument("--ids-out", default="",
                     help="cfg5: write the gathered [steps, seqs] table of sampled ids (.npy, rank 0)")
     ap.add_argument("--paged", type=int, default=0,

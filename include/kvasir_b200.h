@@ -133,6 +133,34 @@ int kvb_blas_set_workspace(kvb_blas_t blas, void* workspace, size_t workspace_le
  * stream.  Inside a capture an untuned shape uses cublasGemmEx. */
 int kvb_blas_set_autotune(kvb_blas_t blas, int enable);
 
+/* New: linear_f16 (engine/src/gpu/gemm.rs:63-88) for decode-sized batches on
+ * this library's own tensor-core kernel, no cuBLAS handle: y[rows,out] =
+ * x[rows,in] * w[out,in]^T, f32 accumulate, 16-bit y.  W is streamed from HBM
+ * once; the in dimension is cut into `splits` slices per 128-row tile of w
+ * (0: chosen for the shape; at most 8 and at most ceil(in / 64)), whose
+ * partial tiles are added in a fixed order, so a call gives the same bits on
+ * every run.  The launch is a programmatic dependent of the kernel before it on
+ * the stream: it reads x and writes y only after that kernel has completed, but
+ * starts reading w as soon as it runs, which can be while the kernels in front
+ * of it that were themselves launched that way (this library's row-norm,
+ * decode-attention, combine and kvb_linear_rows / kvb_linear_silu_mul kernels)
+ * are still running -- w must not be the output of such a kernel still in
+ * flight.  Supported: rows <= 128, in a multiple of 8, out a multiple of 4, x
+ * and w 16-byte aligned, y 8-byte aligned; otherwise KVB_ERR_UNSUPPORTED
+ * (kvb_linear serves every shape). */
+int kvb_linear_rows(kvb_stream_t stream, const void* x, size_t x_len, const void* w, size_t w_len,
+                    void* y, size_t y_len, size_t rows, size_t in_dim, size_t out_dim, int splits,
+                    int dtype);
+/* New: the gate/up projection and SiLU*mul in one pass: act[rows,inter] =
+ * silu(G) * U with [G | U] = x[rows,hidden] * w_gu[2*inter,hidden]^T (w_gu rows
+ * 0..inter-1 gate, inter..2*inter-1 up, the layout of engine/src/model/weights.rs).
+ * G and U are rounded to the 16-bit type before the SiLU*mul, as in kvb_linear
+ * followed by kvb_silu_mul; the [rows, 2*inter] intermediate is never stored.
+ * Splits, ordering and support as kvb_linear_rows (inter a multiple of 4). */
+int kvb_linear_silu_mul(kvb_stream_t stream, const void* x, size_t x_len, const void* w_gu,
+                        size_t w_len, void* act, size_t act_len, size_t rows, size_t hidden,
+                        size_t inter, int splits, int dtype);
+
 /* Host-side RoPE table (engine/src/model/rope.rs:3-39): f64 inverse
  * frequencies with optional llama3 scaling, f32 cos/sin [max_pos, head_dim/2]
  * written to HOST arrays cos_t/sin_t of max_pos*head_dim/2 floats. */
@@ -452,6 +480,12 @@ int kvb_decoder_set_sampling(kvb_decoder_t dec, float temperature, float top_p, 
  * the f32 rounding of their sums.  The next step re-records its graph.  New: the
  * fusion the reference's plan lists after its GEMM (engine/src/gpu/gemm.rs:90-115). */
 int kvb_decoder_set_fused_lm_head(kvb_decoder_t dec, int enable);
+/* enable != 0: the qkv, o and down projections run on kvb_linear_rows and the
+ * gate/up projection with SiLU*mul on kvb_linear_silu_mul, where they apply
+ * (n_seq <= 128 and their shape limits); otherwise, and by default, cuBLAS
+ * (kvb_linear) and kvb_silu_mul.  Both accumulate in f32; the 16-bit results
+ * agree within one rounding.  The next step re-records its graph. */
+int kvb_decoder_set_row_projections(kvb_decoder_t dec, int enable);
 /* Untied checkpoints (reference Weights::head, engine/src/model/weights.rs:29-32):
  * the LM head [vocab, hidden] used instead of the embedding table.  NULL goes
  * back to the tied head.  The next step re-records its graph. */

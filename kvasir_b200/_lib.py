@@ -90,6 +90,9 @@ SIGNATURES = {
     "kvb_lm_head_argmax_workspace_bytes": (_sz, [_sz]),
     "kvb_decoder_set_fused_lm_head": (_int, [_p, _int]),
     "kvb_lm_head_argmax": (_int, [_p, _p, _sz, _p, _sz, _sz, _sz, _sz, _p, _sz, _p, _p, _p, _int]),
+    "kvb_linear_rows": (_int, [_p, _p, _sz, _p, _sz, _p, _sz, _sz, _sz, _sz, _int, _int]),
+    "kvb_linear_silu_mul": (_int, [_p, _p, _sz, _p, _sz, _p, _sz, _sz, _sz, _sz, _int, _int]),
+    "kvb_decoder_set_row_projections": (_int, [_p, _int]),
     "kvb_rope_attention_decode_paged": (_int, [_p, _p, _sz, _p, _p, _sz, _p, _p, _sz, _p, _sz, _sz,
                                                _p, _sz, _sz, _sz, _sz, _sz, C.c_float, _p, _sz, _p,
                                                _sz, _int]),

@@ -102,8 +102,11 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     // dispatched slot by slot, so full chunks go first and the final wave holds the
     // shortest pieces of work (longest first: a shorter tail).
     // the combine pass (a programmatic dependent) may launch once every CTA got here;
-    // it still waits for this grid's completion before it reads any partial
+    // it still waits for this grid's completion before it reads any partial.  This
+    // kernel is launched the same way after the qkv projection: it touches no memory
+    // before that kernel has completed.
     asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int kvh = blockIdx.x, b = blockIdx.y;
     const int from_end = (int)gridDim.z - 1 - (int)blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -130,37 +133,9 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
             if (threadIdx.x == 0) raise_dev_error(kDevErrBadPosition);
             rope_p = -1;
         }
-        if (rope_p >= 0 && chunk == n_chunks - 1) {  // this CTA reads the new key
-            const T* kin = reinterpret_cast<const T*>(a.q) + (size_t)b * a.q_row_stride +
-                           (size_t)(a.n_kv * G + kvh) * 64;
-            const T* vin = kin + (size_t)a.n_kv * 64;
-            size_t row = (size_t)b * a.cache_seq_stride + ((size_t)kvh * a.max_seq + rope_p) * 64;
-            bool write = true;
-            if (a.block_table) {  // paged: the block holding position rope_p
-                const int lb = rope_p / a.block_size;
-                const int blk = a.block_table[(size_t)b * a.max_blocks + lb];
-                if (blk < 0 || blk >= a.n_blocks) {  // reported; the tile read sees zeros there
-                    if (threadIdx.x == 0) raise_dev_error(kDevErrBadPosition);
-                    write = false;
-                }
-                row = (((size_t)blk * a.n_kv + kvh) * a.block_size + (rope_p - lb * a.block_size)) * 64;
-            }
-            T* kout = reinterpret_cast<T*>(a.kc_w) + row;
-            T* vout = reinterpret_cast<T*>(a.vc_w) + row;
-            const int t = threadIdx.x;
-            if (write && t < 32) {
-                const float x0 = Elem<T>::to_f(kin[t]), x1 = Elem<T>::to_f(kin[t + 32]);
-                const float cs = a.rope_cos[(size_t)rope_p * 32 + t];
-                const float sn = a.rope_sin[(size_t)rope_p * 32 + t];
-                kout[t] = Elem<T>::from_f(rot_a(x0, x1, cs, sn));
-                kout[t + 32] = Elem<T>::from_f(rot_b(x0, x1, cs, sn));
-            } else if (write && t >= 64) {
-                vout[t - 64] = vin[t - 64];
-            }
-            // the tensor copies below read this row through the async proxy
-            asm volatile("fence.proxy.async.global;" ::: "memory");
-        }
     }
+    // this CTA appends the new key (fused RoPE, last chunk): CTA-uniform
+    const bool appends = kRope && rope_p >= 0 && chunk == n_chunks - 1;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < kDecWarps; ++i) mbar_init(&bars[i], 1);
@@ -170,8 +145,56 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
 
     uint8_t* ktile = smem + warp * 2 * kDecTileBytes;
     uint8_t* vtile = ktile + kDecTileBytes;
-    const uint32_t kb = smem_u32(ktile), vb = smem_u32(vtile);
     const int row_base = (int)((long long)b * a.seq_rows + (long long)kvh * a.max_seq);
+    // paged: lane 0 reads the block of its next tile while the current one loads
+    int blk_next = lane == 0 ? decode_block_of(a, b, key_begin + warp * kDecTileKeys) : 0;
+    auto issue = [&](int kt0) {  // lane 0: the K and V tiles of keys kt0 .. kt0 + 63
+        const int row = decode_tile_row(a, b, kvh, row_base, kt0, blk_next);
+        mbar_expect_tx(&bars[warp], 2 * kDecTileBytes);
+        tma_load_2d(ktile, &kmap, &bars[warp], 0, row);
+        tma_load_2d(vtile, &vmap, &bars[warp], 0, row);
+        const int kn = kt0 + kDecWarps * kDecTileKeys;
+        if (kn < key_end) blk_next = decode_block_of(a, b, kn);
+    };
+    // The first tile's copy is in flight while q is loaded (and the new row written):
+    // only the tile that holds the new key waits for that write.
+    const int kt_first = key_begin + warp * kDecTileKeys;
+    const bool early = kt_first < key_end && !(appends && rope_p < kt_first + kDecTileKeys);
+    if (early && lane == 0) issue(kt_first);
+
+    if (appends) {
+        const T* kin = reinterpret_cast<const T*>(a.q) + (size_t)b * a.q_row_stride +
+                       (size_t)(a.n_kv * G + kvh) * 64;
+        const T* vin = kin + (size_t)a.n_kv * 64;
+        size_t row = (size_t)b * a.cache_seq_stride + ((size_t)kvh * a.max_seq + rope_p) * 64;
+        bool write = true;
+        if (a.block_table) {  // paged: the block holding position rope_p
+            const int lb = rope_p / a.block_size;
+            const int blk = a.block_table[(size_t)b * a.max_blocks + lb];
+            if (blk < 0 || blk >= a.n_blocks) {  // reported; the tile read sees zeros there
+                if (threadIdx.x == 0) raise_dev_error(kDevErrBadPosition);
+                write = false;
+            }
+            row = (((size_t)blk * a.n_kv + kvh) * a.block_size + (rope_p - lb * a.block_size)) * 64;
+        }
+        T* kout = reinterpret_cast<T*>(a.kc_w) + row;
+        T* vout = reinterpret_cast<T*>(a.vc_w) + row;
+        const int t = threadIdx.x;
+        if (write && t < 32) {
+            const float x0 = Elem<T>::to_f(kin[t]), x1 = Elem<T>::to_f(kin[t + 32]);
+            const float cs = a.rope_cos[(size_t)rope_p * 32 + t];
+            const float sn = a.rope_sin[(size_t)rope_p * 32 + t];
+            kout[t] = Elem<T>::from_f(rot_a(x0, x1, cs, sn));
+            kout[t + 32] = Elem<T>::from_f(rot_b(x0, x1, cs, sn));
+        } else if (write && t >= 64) {
+            vout[t - 64] = vin[t - 64];
+        }
+        // the tensor copies below read this row through the async proxy
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __syncthreads();  // written before the copy of its tile is issued
+    }
+
+    const uint32_t kb = smem_u32(ktile), vb = smem_u32(vtile);
 
     // Q fragments (A operand, rows = the group's heads, padded to 16).
     uint32_t qa[4][4];
@@ -211,19 +234,9 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     uint32_t phase = 0;
     bool ok = true;
 
-    // paged: lane 0 reads the block of its next tile while the current one loads
-    int blk_next = lane == 0 ? decode_block_of(a, b, key_begin + warp * kDecTileKeys) : 0;
-    for (int kt0 = key_begin + warp * kDecTileKeys; kt0 < key_end && ok;
-         kt0 += kDecWarps * kDecTileKeys) {
+    for (int kt0 = kt_first; kt0 < key_end && ok; kt0 += kDecWarps * kDecTileKeys) {
         const int nk = min(kDecTileKeys, key_end - kt0);
-        if (lane == 0) {
-            const int row = decode_tile_row(a, b, kvh, row_base, kt0, blk_next);
-            mbar_expect_tx(&bars[warp], 2 * kDecTileBytes);
-            tma_load_2d(ktile, &kmap, &bars[warp], 0, row);
-            tma_load_2d(vtile, &vmap, &bars[warp], 0, row);
-            const int kn = kt0 + kDecWarps * kDecTileKeys;
-            if (kn < key_end) blk_next = decode_block_of(a, b, kn);
-        }
+        if (lane == 0 && !(early && kt0 == kt_first)) issue(kt0);
         ok = mbar_wait(&bars[warp], phase);
         phase ^= 1;
         if (!ok) break;
@@ -390,6 +403,9 @@ constexpr int kCombineThreads = 256;
 template <typename T>
 __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(DecodeArgs a) {
     extern __shared__ float sp[];
+    // the projection after this pass (a programmatic dependent) may start streaming its
+    // weights; it reads the attention output only after this grid completes
+    asm volatile("griddepcontrol.launch_dependents;");
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int kvh = blockIdx.x, b = blockIdx.y;
     const int G = a.group;

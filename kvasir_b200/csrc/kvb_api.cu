@@ -17,6 +17,7 @@
 #include "attn_prefill.cuh"
 #include "elementwise.cuh"
 #include "kvb_host.h"
+#include "linear_rows.cuh"
 #include "lm_head.cuh"
 #include "norm.cuh"
 #include "rope.cuh"
@@ -118,6 +119,26 @@ static void set_max_smem(F* kernel, int bytes) {
         if (d.first == dev && d.second == key) return;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     done.emplace_back(dev, key);
+}
+
+// Launches `kernel` as a programmatic dependent of the kernel before it on the
+// stream: its CTAs may be scheduled while that kernel drains.  The kernel
+// executes griddepcontrol.wait before its first access to memory that earlier
+// kernels write or read.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
 // ---------------------------------------------------------------- sampler launcher
@@ -392,7 +413,9 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
 #define KVB_DECODE_LAUNCH(T, ROPE)                                                   \
     do {                                                                             \
         set_max_smem(attn_decode_kernel<T, ROPE>, kDecSmemBytes);                    \
-        attn_decode_kernel<T, ROPE><<<grid, 128, kDecSmemBytes, stream>>>(kmap, vmap, a); \
+        const cudaError_t le = launch_pdl(attn_decode_kernel<T, ROPE>, grid, dim3(128),  \
+                                          kDecSmemBytes, stream, kmap, vmap, a);      \
+        if (le != cudaSuccess) return cuda_fail(le, "attention decode launch");       \
     } while (0)
     if (L.dtype == KVB_BF16) {
         if (L.rope_cos) KVB_DECODE_LAUNCH(__nv_bfloat16, true);
@@ -548,12 +571,15 @@ static int launch_rmsnorm(kvb_stream_t stream, void* x, const void* y, const voi
                          rows <= (size_t)num_sms() * 4;
     if (per_row) {
         const float ih = 1.0f / (float)hidden;
-        if (dtype == KVB_BF16)
-            rmsnorm_row_kernel<__nv_bfloat16, kAdd><<<(unsigned)rows, (unsigned)chunks, 0, stream>>>(
-                (uint4*)x, (const uint4*)y, (const uint4*)w, (uint4*)out, (int)chunks, ih, eps);
-        else
-            rmsnorm_row_kernel<__half, kAdd><<<(unsigned)rows, (unsigned)chunks, 0, stream>>>(
-                (uint4*)x, (const uint4*)y, (const uint4*)w, (uint4*)out, (int)chunks, ih, eps);
+        const cudaError_t le =
+            dtype == KVB_BF16
+                ? launch_pdl(rmsnorm_row_kernel<__nv_bfloat16, kAdd>, dim3((unsigned)rows),
+                             dim3((unsigned)chunks), 0, stream, (uint4*)x, (const uint4*)y,
+                             (const uint4*)w, (uint4*)out, (int)chunks, ih, eps)
+                : launch_pdl(rmsnorm_row_kernel<__half, kAdd>, dim3((unsigned)rows),
+                             dim3((unsigned)chunks), 0, stream, (uint4*)x, (const uint4*)y,
+                             (const uint4*)w, (uint4*)out, (int)chunks, ih, eps);
+        if (le != cudaSuccess) return cuda_fail(le, "rmsnorm launch");
     } else if (vec) {
         const float ih = 1.0f / (float)hidden;
         const int nv = chunks <= 32 ? 1 : chunks <= 64 ? 2 : chunks <= 128 ? 4 : chunks <= 256 ? 8 : 16;
@@ -590,6 +616,112 @@ static int launch_rmsnorm(kvb_stream_t stream, void* x, const void* y, const voi
                 (__half*)x, (const __half*)y, (const __half*)w, (__half*)out, (int)hidden, eps);
     }
     KVB_CHECK_LAUNCH("rmsnorm launch");
+    return KVB_OK;
+}
+
+// ---------------------------------------------------------------- projections of few rows
+// linear_rows_kernel<N, kGlu, T>: a grid of n_tiles x splits CTAs in clusters of
+// `splits`, launched as a programmatic dependent of the preceding kernel.
+template <int N, bool kGlu, typename T>
+static cudaError_t launch_linear_rows(cudaStream_t stream, const CUtensorMap& wmap,
+                                      const CUtensorMap& xmap, const LinearRowsArgs& a,
+                                      int n_tiles, uint32_t fmt) {
+    auto* kernel = linear_rows_kernel<N, kGlu, T>;
+    set_max_smem(kernel, lr_smem_bytes(N));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(n_tiles * a.splits));
+    cfg.blockDim = dim3(kLrThreads);
+    cfg.dynamicSmemBytes = lr_smem_bytes(N);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int n_attr = 0;
+    attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n_attr++].val.programmaticStreamSerializationAllowed = 1;
+    if (a.splits > 1) {
+        attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+        attr[n_attr].val.clusterDim.x = (unsigned)a.splits;
+        attr[n_attr].val.clusterDim.y = 1;
+        attr[n_attr++].val.clusterDim.z = 1;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n_attr;
+    return cudaLaunchKernelEx(&cfg, kernel, wmap, xmap, a, fmt);
+}
+
+template <bool kGlu, typename T>
+static cudaError_t launch_linear_rows_n(int n, cudaStream_t stream, const CUtensorMap& wmap,
+                                        const CUtensorMap& xmap, const LinearRowsArgs& a,
+                                        int n_tiles, uint32_t fmt) {
+    switch (n) {
+        case 16: return launch_linear_rows<16, kGlu, T>(stream, wmap, xmap, a, n_tiles, fmt);
+        case 32: return launch_linear_rows<32, kGlu, T>(stream, wmap, xmap, a, n_tiles, fmt);
+        case 64: return launch_linear_rows<64, kGlu, T>(stream, wmap, xmap, a, n_tiles, fmt);
+        default: return launch_linear_rows<128, kGlu, T>(stream, wmap, xmap, a, n_tiles, fmt);
+    }
+}
+
+// Shared body of kvb_linear_rows (glu false: W has out rows) and
+// kvb_linear_silu_mul (glu true: W_gu has 2 * out rows, Y is [rows, out]).
+// The caller has checked the lengths; rows and out are positive.
+static int linear_rows_launch(cudaStream_t stream, const void* x, const void* w, void* y,
+                              size_t rows, size_t in_dim, size_t out, bool glu, int splits,
+                              int dtype, const char* name) {
+    const size_t w_rows = glu ? 2 * out : out;
+    if (!(rows <= (size_t)kLrMaxRows && in_dim > 0 && in_dim % 8 == 0 && out % 4 == 0 &&
+          fits_i32(in_dim) && fits_i32(w_rows) && aligned(x, 16) && aligned(w, 16) &&
+          aligned(y, 8)))
+        return fail(KVB_ERR_UNSUPPORTED,
+                    "%s: needs rows <= %d, in a multiple of 8, out a multiple of 4, 16-byte "
+                    "aligned x and w, 8-byte aligned output (use kvb_linear)",
+                    name, kLrMaxRows);
+    const int n = rows <= 16 ? 16 : rows <= 32 ? 32 : rows <= 64 ? 64 : 128;
+    const int kchunks = (int)((in_dim + kLrK - 1) / kLrK);
+    const int n_tiles = (int)(glu ? (out + 63) / 64 : (out + kLrTile - 1) / kLrTile);
+    int s = splits;
+    if (s == 0) {
+        // about 8 chunks (160 KB of W) per CTA, which the ring requests at once;
+        // clusters of at most 6 and at most two thirds of the SMs.  Measured on B200
+        // at the Llama-3.2-1B shapes: 8-CTA clusters and wider grids finish later
+        // (cluster placement, and the next projection finds no SMs to start on)
+        s = kchunks / 8;
+        if (s > 6) s = 6;
+        const int by_sms = (num_sms() * 2 / 3) / n_tiles;
+        if (s > by_sms) s = by_sms;
+    }
+    if (s > kchunks) s = kchunks;
+    if (s < 1) s = 1;
+    KVB_CHECK((size_t)n_tiles * (size_t)s <= 0x7fffffffu, "%s: too many tiles", name);
+    CUtensorMap wmap, xmap;
+    {
+        const uint64_t dims[2] = {in_dim, w_rows};
+        const uint64_t strides[1] = {in_dim * 2};
+        const uint32_t box[2] = {(uint32_t)kLrK, (uint32_t)(glu ? 64 : kLrTile)};
+        const int st = encode_tmap(&wmap, w, 2, dims, strides, box, dtype);
+        if (st) return st;
+    }
+    {
+        const uint64_t dims[2] = {in_dim, rows};
+        const uint64_t strides[1] = {in_dim * 2};
+        const uint32_t box[2] = {(uint32_t)kLrK, (uint32_t)n};  // rows past `rows` read as 0
+        const int st = encode_tmap(&xmap, x, 2, dims, strides, box, dtype);
+        if (st) return st;
+    }
+    LinearRowsArgs a;
+    a.rows = (int)rows;
+    a.out = (int)out;
+    a.glu_up = glu ? (int)out : 0;
+    a.kchunks = kchunks;
+    a.splits = s;
+    a.y = y;
+    const uint32_t fmt = dtype == KVB_BF16 ? 1u : 0u;
+    cudaError_t e;
+    if (dtype == KVB_BF16)
+        e = glu ? launch_linear_rows_n<true, __nv_bfloat16>(n, stream, wmap, xmap, a, n_tiles, fmt)
+                : launch_linear_rows_n<false, __nv_bfloat16>(n, stream, wmap, xmap, a, n_tiles, fmt);
+    else
+        e = glu ? launch_linear_rows_n<true, __half>(n, stream, wmap, xmap, a, n_tiles, fmt)
+                : launch_linear_rows_n<false, __half>(n, stream, wmap, xmap, a, n_tiles, fmt);
+    if (e != cudaSuccess) return cuda_fail(e, name);
     return KVB_OK;
 }
 
@@ -693,15 +825,15 @@ int kvb_embedding_rmsnorm(kvb_stream_t stream, const int32_t* ids, size_t t, con
         return kvb_rmsnorm(stream, x, x_len, w, w_len, out, out_len, t, hidden, eps, dtype);
     }
     const float ih = 1.0f / (float)hidden;
-    if (dtype == KVB_BF16)
-        embedding_rmsnorm_row_kernel<__nv_bfloat16><<<(unsigned)t, (unsigned)chunks, 0, stream>>>(
-            ids, (const uint4*)table, (const uint4*)w, (uint4*)x, (uint4*)out, (int)chunks,
-            (int)vocab, ih, eps);
-    else
-        embedding_rmsnorm_row_kernel<__half><<<(unsigned)t, (unsigned)chunks, 0, stream>>>(
-            ids, (const uint4*)table, (const uint4*)w, (uint4*)x, (uint4*)out, (int)chunks,
-            (int)vocab, ih, eps);
-    KVB_CHECK_LAUNCH("embedding_rmsnorm launch");
+    const cudaError_t le =
+        dtype == KVB_BF16
+            ? launch_pdl(embedding_rmsnorm_row_kernel<__nv_bfloat16>, dim3((unsigned)t),
+                         dim3((unsigned)chunks), 0, stream, ids, (const uint4*)table,
+                         (const uint4*)w, (uint4*)x, (uint4*)out, (int)chunks, (int)vocab, ih, eps)
+            : launch_pdl(embedding_rmsnorm_row_kernel<__half>, dim3((unsigned)t),
+                         dim3((unsigned)chunks), 0, stream, ids, (const uint4*)table,
+                         (const uint4*)w, (uint4*)x, (uint4*)out, (int)chunks, (int)vocab, ih, eps);
+    if (le != cudaSuccess) return cuda_fail(le, "embedding_rmsnorm launch");
     return KVB_OK;
 }
 
@@ -1673,6 +1805,41 @@ int kvb_lm_head_argmax(kvb_stream_t stream, const void* x, size_t x_len, const v
                                                                     advance2);
     KVB_CHECK_LAUNCH("lm_head_argmax finish launch");
     return KVB_OK;
+}
+
+// ------------------------------------------------------------------ projections of few rows
+int kvb_linear_rows(kvb_stream_t stream, const void* x, size_t x_len, const void* w, size_t w_len,
+                    void* y, size_t y_len, size_t rows, size_t in_dim, size_t out_dim, int splits,
+                    int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(x_len == rows * in_dim, "linear_rows: x has %zu elems, want %zux%zu", x_len, rows,
+              in_dim);
+    KVB_CHECK(w_len == out_dim * in_dim, "linear_rows: w has %zu elems, want %zux%zu", w_len,
+              out_dim, in_dim);
+    KVB_CHECK(y_len == rows * out_dim, "linear_rows: y has %zu elems, want %zux%zu", y_len, rows,
+              out_dim);
+    KVB_CHECK(splits >= 0 && splits <= kLrMaxSplits, "linear_rows: splits %d outside [0, %d]",
+              splits, kLrMaxSplits);
+    if (rows == 0 || out_dim == 0) return KVB_OK;
+    return linear_rows_launch(stream, x, w, y, rows, in_dim, out_dim, false, splits, dtype,
+                              "linear_rows");
+}
+
+int kvb_linear_silu_mul(kvb_stream_t stream, const void* x, size_t x_len, const void* w_gu,
+                        size_t w_len, void* act, size_t act_len, size_t rows, size_t hidden,
+                        size_t inter, int splits, int dtype) {
+    KVB_CHECK_DTYPE(dtype);
+    KVB_CHECK(x_len == rows * hidden, "linear_silu_mul: x has %zu elems, want %zux%zu", x_len,
+              rows, hidden);
+    KVB_CHECK(w_len == 2 * inter * hidden, "linear_silu_mul: w_gu has %zu elems, want %zux%zu",
+              w_len, 2 * inter, hidden);
+    KVB_CHECK(act_len == rows * inter, "linear_silu_mul: act has %zu elems, want %zux%zu", act_len,
+              rows, inter);
+    KVB_CHECK(splits >= 0 && splits <= kLrMaxSplits, "linear_silu_mul: splits %d outside [0, %d]",
+              splits, kLrMaxSplits);
+    if (rows == 0 || inter == 0) return KVB_OK;
+    return linear_rows_launch(stream, x, w_gu, act, rows, hidden, inter, true, splits, dtype,
+                              "linear_silu_mul");
 }
 
 // ------------------------------------------------------------------ self test

@@ -79,6 +79,7 @@ struct kvb_decoder_s {
     float top_p = 1.f;
     uint64_t seed = 0;
     bool fused_lm_head = false;     // greedy steps: kvb_lm_head_argmax where it applies
+    bool row_projections = false;   // kvb_linear_rows / kvb_linear_silu_mul where they apply
     const void* final_norm = nullptr;
     std::vector<const void*> attn_norm, w_qkv, w_o, mlp_norm, w_gu, w_down;
     uint8_t* kc = nullptr;
@@ -130,10 +131,24 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
          false);
     if (!kvb::embedding_rmsnorm_fused(B, H, d->embed, d->attn_norm[0], d->at(L.x), d->at(L.h)))
         ++own;  // it ran as two launches
+    // one projection y[B, out] = x[B, in] w^T: this library's kernel for decode-sized
+    // batches where enabled and supported, else cuBLAS
+    const bool rows_proj = d->row_projections && B <= 128;
+    auto proj = [&](const void* x, size_t in, const void* w, void* y, size_t out) -> int {
+        if (rows_proj) {
+            const int r = kvb_linear_rows(s, x, B * in, w, out * in, y, B * out, B, in, out, 0, dt);
+            if (r != KVB_ERR_UNSUPPORTED) {
+                if (r == KVB_OK) ++own;
+                return r;
+            }
+        }
+        const int r = kvb_linear(d->blas, s, x, B * in, w, out * in, y, B * out, B, in, out, dt, 0);
+        if (r == KVB_OK) ++lib;
+        return r;
+    };
     for (int l = 0; l < c.n_layers; ++l) {
-        STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->w_qkv[l], qkvd * H, d->at(L.qkv), B * qkvd,
-                        B, H, qkvd, dt, 0),
-             true);
+        st = proj(d->at(L.h), H, d->w_qkv[l], d->at(L.qkv), qkvd);
+        if (st != KVB_OK) return st;
         if (!d->block_table) {
             uint8_t* kl = d->kc + (size_t)l * layer_elems * 2;
             uint8_t* vl = d->vc + (size_t)l * layer_elems * 2;
@@ -168,19 +183,26 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
                  false);
         }
         if (L.attn_ws_len > 0) ++own;  // the split-KV combine pass
-        STEP(kvb_linear(d->blas, s, d->at(L.attn), B * qd, d->w_o[l], H * qd, d->at(L.o), B * H, B,
-                        qd, H, dt, 0),
-             true);
+        st = proj(d->at(L.attn), qd, d->w_o[l], d->at(L.o), H);
+        if (st != KVB_OK) return st;
         STEP(kvb_add_rmsnorm(s, d->at(L.x), B * H, d->at(L.o), B * H, d->mlp_norm[l], H, d->at(L.h),
                              B * H, B, H, c.eps, dt),
              false);
-        STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->w_gu[l], 2 * I * H, d->at(L.gu), B * 2 * I,
-                        B, H, 2 * I, dt, 0),
-             true);
-        STEP(kvb_silu_mul(s, d->at(L.gu), B * 2 * I, d->at(L.act), B * I, B, I, dt), false);
-        STEP(kvb_linear(d->blas, s, d->at(L.act), B * I, d->w_down[l], H * I, d->at(L.o), B * H, B,
-                        I, H, dt, 0),
-             true);
+        int gst = KVB_ERR_UNSUPPORTED;
+        if (rows_proj) {  // gate/up projection and SiLU*mul in one pass
+            gst = kvb_linear_silu_mul(s, d->at(L.h), B * H, d->w_gu[l], 2 * I * H, d->at(L.act),
+                                      B * I, B, H, I, 0, dt);
+            if (gst != KVB_OK && gst != KVB_ERR_UNSUPPORTED) return gst;
+            if (gst == KVB_OK) ++own;
+        }
+        if (gst != KVB_OK) {
+            STEP(kvb_linear(d->blas, s, d->at(L.h), B * H, d->w_gu[l], 2 * I * H, d->at(L.gu),
+                            B * 2 * I, B, H, 2 * I, dt, 0),
+                 true);
+            STEP(kvb_silu_mul(s, d->at(L.gu), B * 2 * I, d->at(L.act), B * I, B, I, dt), false);
+        }
+        st = proj(d->at(L.act), I, d->w_down[l], d->at(L.o), H);
+        if (st != KVB_OK) return st;
         const void* next_norm = (l + 1 < c.n_layers) ? d->attn_norm[l + 1] : d->final_norm;
         STEP(kvb_add_rmsnorm(s, d->at(L.x), B * H, d->at(L.o), B * H, next_norm, H, d->at(L.h), B * H,
                              B, H, c.eps, dt),
@@ -338,6 +360,13 @@ int kvb_decoder_set_sampling(kvb_decoder_t d, float temperature, float top_p, ui
 int kvb_decoder_set_fused_lm_head(kvb_decoder_t d, int enable) {
     KVB_CHECK(d, "decoder_set_fused_lm_head: null decoder");
     d->fused_lm_head = enable != 0;
+    drop_graph(d);
+    return KVB_OK;
+}
+
+int kvb_decoder_set_row_projections(kvb_decoder_t d, int enable) {
+    KVB_CHECK(d, "decoder_set_row_projections: null decoder");
+    d->row_projections = enable != 0;
     drop_graph(d);
     return KVB_OK;
 }

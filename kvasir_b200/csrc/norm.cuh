@@ -166,6 +166,12 @@ __global__ void __launch_bounds__(1024) rmsnorm_row_kernel(uint4* __restrict__ x
                                                           uint4* __restrict__ out, int chunks,
                                                           float inv_hidden, float eps) {
     __shared__ float red[32];
+    // a projection launched as this grid's programmatic dependent may start streaming
+    // its weights now; it reads this kernel's output only after the grid completes.
+    // This kernel is itself launched that way: nothing is read before the preceding
+    // kernel has completed.
+    asm volatile("griddepcontrol.launch_dependents;");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const size_t row = blockIdx.x;
     const int c = threadIdx.x;
     const int lane = c & 31, warp = c >> 5;
@@ -210,6 +216,8 @@ __global__ void __launch_bounds__(1024) embedding_rmsnorm_row_kernel(
     uint4* __restrict__ x, uint4* __restrict__ out, int chunks, int vocab, float inv_hidden,
     float eps) {
     __shared__ float red[32];
+    asm volatile("griddepcontrol.launch_dependents;");  // as rmsnorm_row_kernel
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const size_t row = blockIdx.x;
     const int c = threadIdx.x;
     const int lane = c & 31, warp = c >> 5;

@@ -193,6 +193,11 @@ class Decoder:
         self.logits is then not written by those steps)."""
         check(self._lib.kvb_decoder_set_fused_lm_head(self._h, 1 if enable else 0))
 
+    def set_row_projections(self, enable: bool = True) -> None:
+        """Projections on kvb_linear_rows and the gate/up projection + SiLU*mul on
+        kvb_linear_silu_mul (decode-sized batches) instead of cuBLAS."""
+        check(self._lib.kvb_decoder_set_row_projections(self._h, 1 if enable else 0))
+
     def set_lengths(self, cur_len) -> None:
         """Tokens already in each sequence's cache; the next step writes there."""
         arr = np.ascontiguousarray(np.broadcast_to(np.asarray(cur_len, np.int32), (self.n_seq,)))

@@ -336,6 +336,18 @@ class Gpu:
                                            hidden, vocab, _ptr(workspace), ws_len, _ptr(ids),
                                            _ptr(advance), _ptr(advance2), dtype_tag(x)))
 
+    def linear_rows(self, x, w, y, rows, in_dim, out_dim, splits=0):
+        """kvb_linear_rows: y = x @ w^T on this library's tensor-core kernel
+        (rows <= 128; splits 0 = automatic)."""
+        check(self._lib.kvb_linear_rows(self._s, _ptr(x), x.numel(), _ptr(w), w.numel(), _ptr(y),
+                                        y.numel(), rows, in_dim, out_dim, splits, dtype_tag(x)))
+
+    def linear_silu_mul(self, x, w_gu, act, rows, hidden, inter, splits=0):
+        """kvb_linear_silu_mul: act = silu(G) * U with [G | U] = x @ w_gu^T."""
+        check(self._lib.kvb_linear_silu_mul(self._s, _ptr(x), x.numel(), _ptr(w_gu), w_gu.numel(),
+                                            _ptr(act), act.numel(), rows, hidden, inter, splits,
+                                            dtype_tag(x)))
+
     def argmax(self, logits, rows, vocab, ids, advance=None, advance2=None):
         if logits.dtype != torch.float32 or ids.dtype != torch.int32:
             raise ShapeError("argmax: f32 logits and int32 ids expected")

@@ -140,3 +140,31 @@ def test_lm_head_argmax_and_prefill_f32_check_shapes_before_launch():
     st, msg = _status(lib.kvb_attention_prefill_f32, None, fake, 2 * 768, fake, fake,
                       2 * 16 * 64 - 1, fake, 2 * 8 * 64, 1, 2, 0, 8, 2, 64, 16, L.KVB_BF16)
     assert st == L.KVB_ERR_SHAPE and "bad cache sizes" in msg
+
+
+def test_linear_rows_check_shapes_and_support_before_launch():
+    """kvb_linear_rows / kvb_linear_silu_mul: length checks are KVB_ERR_SHAPE, shapes
+    the kernel does not take are KVB_ERR_UNSUPPORTED, both before any CUDA call."""
+    lib = L.lib()
+    fake = C.c_void_p(0x1000)
+    st, msg = _status(lib.kvb_linear_rows, None, fake, 4 * 64 - 1, fake, 128 * 64, fake, 4 * 128,
+                      4, 64, 128, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "linear_rows: x has" in msg
+    st, msg = _status(lib.kvb_linear_rows, None, fake, 4 * 64, fake, 128 * 64, fake, 4 * 128,
+                      4, 64, 128, 9, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "splits" in msg
+    st, msg = _status(lib.kvb_linear_rows, None, fake, 129 * 64, fake, 128 * 64, fake,
+                      129 * 128, 129, 64, 128, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_UNSUPPORTED and "rows <= 128" in msg
+    st, msg = _status(lib.kvb_linear_rows, None, fake, 4 * 60, fake, 128 * 60, fake, 4 * 128,
+                      4, 60, 128, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_UNSUPPORTED
+    st, msg = _status(lib.kvb_linear_silu_mul, None, fake, 4 * 64, fake, 2 * 100 * 64 - 1, fake,
+                      4 * 100, 4, 64, 100, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_SHAPE and "w_gu has" in msg
+    st, msg = _status(lib.kvb_linear_silu_mul, None, fake, 4 * 64, fake, 2 * 102 * 64, fake,
+                      4 * 102, 4, 64, 102, 0, L.KVB_BF16)
+    assert st == L.KVB_ERR_UNSUPPORTED and "multiple of 4" in msg
+    # nothing to do: OK without touching the pointers
+    assert lib.kvb_linear_rows(None, fake, 0, fake, 128 * 64, fake, 0, 0, 64, 128, 0,
+                               L.KVB_BF16) == L.KVB_OK

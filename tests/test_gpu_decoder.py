@@ -43,7 +43,10 @@ def _to_torch(wb, cfg):
                 w_down=[t(b, h, i) for b in wb["w_down"]])
 
 
-def test_decoder_matches_oracle_steps():
+@pytest.mark.parametrize("row_proj", [False, True])
+def test_decoder_matches_oracle_steps(row_proj):
+    """row_proj: the projections on kvb_linear_rows / kvb_linear_silu_mul instead of
+    cuBLAS + kvb_silu_mul (same bars: both sum in f32)."""
     from kvasir_b200.decoder import Decoder
     from kvasir_b200.rope import cos_sin_table
     cfg = _tiny_cfg()
@@ -51,6 +54,7 @@ def test_decoder_matches_oracle_steps():
     n_seq, max_seq = 3, 96
     wb = _weights_bits(rng, cfg)
     dec = Decoder(cfg, n_seq, max_seq, weights=_to_torch(wb, cfg))
+    dec.set_row_projections(row_proj)
     L, nkv, hd = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim
     # prefilled context: random K/V at positions < cur_len
     cur = np.array([5, 40, 64], np.int32)
@@ -87,7 +91,8 @@ def test_decoder_matches_oracle_steps():
         ids = got_ids.astype(np.int32)  # continue from the GPU's choice (drivers diverge otherwise)
         pos = pos + 1
     own, lib = dec.launches_per_step()
-    assert own > 0 and lib == 4 * L + 1
+    # cuBLAS: qkv, o, gate/up, down per layer + the f32 LM head; rows: the LM head only
+    assert own > 0 and lib == (1 if row_proj else 4 * L + 1)
     dec.close()
 
 

@@ -25,8 +25,10 @@ by their own scale (rms 0.9), an order of magnitude above the bar.
 
 Also: the first layer's new K / V rows (embedding, RMSNorm, qkv projection,
 RoPE, no residual history yet) equal the oracle's bit for bit in >= 99% of
-elements, and the same sequences decoded one per decoder (other GEMM shapes
-and split-KV chunking) agree with the batched step within the same bar."""
+elements, the same sequences decoded one per decoder (other GEMM shapes and
+split-KV chunking) agree with the batched step within the same bar, and so
+does a decoder whose projections run on kvb_linear_rows / kvb_linear_silu_mul
+instead of cuBLAS, fed the same ids."""
 import os
 
 import numpy as np
@@ -61,6 +63,11 @@ def test_full_llama_1b_decode_step_matches_oracle():
     dec.set_lengths(lens)
     ids = np.random.default_rng(3).integers(0, cfg.vocab_size, n_seq).astype(np.int32)
     dec.ids_in.copy_(torch.from_numpy(ids).cuda())
+    rows = Decoder(cfg, n_seq, max_seq, weights=dec.w)  # projections off cuBLAS
+    rows.set_row_projections(True)
+    rows.kc.copy_(dec.kc)
+    rows.vc.copy_(dec.vc)
+    rows.set_lengths(lens)
     singles = []
     for b in range(n_seq):
         d1 = Decoder(cfg, 1, max_seq, weights=dec.w)
@@ -84,7 +91,9 @@ def test_full_llama_1b_decode_step_matches_oracle():
         for step in range(steps):
             for b, d1 in enumerate(singles):
                 d1.ids_in.copy_(torch.from_numpy(ids[b:b + 1]).cuda())
+            rows.ids_in.copy_(torch.from_numpy(ids).cuda())
             dec.step()
+            rows.step()
             for d1 in singles:
                 d1.step()
             torch.cuda.synchronize()
@@ -107,6 +116,11 @@ def test_full_llama_1b_decode_step_matches_oracle():
             assert (err.max(axis=1) <= tol).all(), msg
             assert (np.sqrt((err ** 2).mean(axis=1)) <= LOGIT_TOL_FACTOR * spread_rms).all(), msg
             assert (np.abs(one - got).max(axis=1) <= tol).all(), f"step {step}: batch vs single"
+            got_rows = rows.logits.cpu().numpy().astype(np.float64)
+            err_rows = np.abs(got_rows - want)
+            assert (err_rows.max(axis=1) <= tol).all(), (
+                f"step {step}: row projections max |err| {err_rows.max(axis=1)}, bar {tol}")
+            assert (np.sqrt((err_rows ** 2).mean(axis=1)) <= LOGIT_TOL_FACTOR * spread_rms).all()
             assert (spread <= LLAMA1B_LOGIT_SPREAD).all(), f"spread {spread}"
             # ids: the greedy pick of the GPU's own logits (first index of the max), equal
             # to the oracle's wherever the oracle's top-2 margin exceeds twice the row's
@@ -135,6 +149,6 @@ def test_full_llama_1b_decode_step_matches_oracle():
     finally:
         O.set_round_dither(0.0)
         O.set_threads(1)
-        for d in singles + [dec]:
+        for d in singles + [dec, rows]:
             d.close()
     print(f"ids compared exactly on {compared} of {steps * n_seq} (sequence, step) pairs")
