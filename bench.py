@@ -4,8 +4,10 @@ Default (the contract line): BASELINE config 5 -- sequence-sharded long-context
 greedy decode of a random-init Llama-3.2-1B (16 layers, bf16): 256 independent
 sequences with a 16384-token KV cache each, split evenly over the ranks (one
 process per GPU; `torchrun --nproc-per-node N bench.py --gpus N`).  A step is
-one decode step (one new token for every sequence) of the whole model: cuBLAS
-projections + the kvb kernels + greedy argmax, replayed as one CUDA graph.
+one decode step (one new token for every sequence) of the whole model: the
+projections (cuBLAS, or this library's kvb_linear_rows / kvb_linear_silu_mul at
+64 or fewer sequences per GPU) + the kvb kernels + greedy argmax, replayed as
+one CUDA graph.
 
   value     whole-job tokens/s with ids, weights and KV resident in HBM,
             CUDA-event timed over K steps, max over ranks;
@@ -27,7 +29,8 @@ projections + the kvb kernels + greedy argmax, replayed as one CUDA graph.
 `--workload cfg1|cfg2|cfg3|cfg4` print per-kernel lines for the other
 BASELINE configs instead; `--workload sample` times the device-side sampler;
 `--workload attn5` times the config-5 attention launch alone (`--seqs` sets
-its size).
+its size); `--workload lmhead` the fused LM head + argmax; `--workload proj`
+the decode-step projections at `--seqs` rows (kvb_linear_rows against cuBLAS).
 """
 from __future__ import annotations
 
@@ -284,7 +287,7 @@ def run_decode(args):
     dec = Decoder(cfg, n_local, max_seq, device=f"cuda:{local}", seed=0, paged_block_size=bs)
     # greedy steps end in kvb_lm_head_argmax where it applies (32 or fewer sequences per GPU)
     dec.set_fused_lm_head(not args.unfused_lm_head)
-    row_proj = args.projections == "rows" or (args.projections == "auto" and n_local <= 32)
+    row_proj = args.projections == "rows" or (args.projections == "auto" and n_local <= 64)
     dec.set_row_projections(row_proj)
     # every sequence's context is seeded by its global index: the same data at any N
     dec.fill_kv_normal(seed=1000, first_seq=first)
@@ -490,7 +493,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="kernel", choices=["kernel", "reference"])
     ap.add_argument("--workload", default="cfg5", choices=["cfg1", "cfg2", "cfg3", "cfg4", "cfg5", "sample", "attn5",
-                                                 "lmhead"])
+                                                 "lmhead", "proj"])
     ap.add_argument("--seqs", type=int, default=256, help="total sequences (cfg5)")
     ap.add_argument("--context", type=int, default=16384, help="KV tokens per sequence (cfg5)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -502,8 +505,8 @@ def main():
                     help="cfg5: keep the cuBLAS LM head + argmax even where the fused pass applies")
     ap.add_argument("--projections", default="auto", choices=["auto", "cublas", "rows"],
                     help="cfg5: qkv / o / gate-up / down projections on cuBLAS or on "
-                         "kvb_linear_rows + kvb_linear_silu_mul (auto: rows for <= 32 "
-                         "sequences per GPU)")
+                         "kvb_linear_rows + kvb_linear_silu_mul (auto: rows for <= 64 "
+                         "sequences per GPU, where they measure faster)")
     ap.add_argument("--ids-out", default="",
                     help="cfg5: write the gathered [steps, seqs] table of sampled ids (.npy, rank 0)")
     ap.add_argument("--paged", type=int, default=0,

@@ -472,30 +472,37 @@ def cfg4(args):
                "frac_of_roofline": tps / roof_tps, "peak": f"{peaks['hbm_gbs']} GB/s ({kind})",
                "lm_head": "cuBLAS f32 logits + kvb_argmax_f32",
                "launches_per_step": {"own": own, "cublas": lib}})
-        # the same greedy steps with the LM head and the argmax in one pass
-        dec.set_fused_lm_head(True)
-        dec.set_lengths(ctx)
-        for _ in range(3):
-            dec.step()
-        dec.set_lengths(ctx)
-        torch.cuda.synchronize()
-        a.record(s)
-        for _ in range(steps):
-            dec.step()
-        b.record(s)
-        b.synchronize()
-        ms_f = a.elapsed_time(b)
-        own, lib = dec.launches_per_step()
+        # the same greedy steps with the LM head and the argmax in one pass, then also
+        # with the projections on kvb_linear_rows / kvb_linear_silu_mul
         fused_bytes = step_bytes - B * cfg.vocab_size * 4
-        _emit({"workload": f"cfg4: 16-layer decode, batch {B}, context 1024, 256 greedy steps, "
-                           f"LM head + argmax fused",
-               "metric": "tokens/s", "value": B * steps / (ms_f * 1e-3), "unit": "tokens/s",
-               "ms_per_step": ms_f / steps, "bytes_per_step": fused_bytes,
-               "frac_of_roofline": (B * steps / (ms_f * 1e-3)) /
-                                   (B / (fused_bytes / (peaks["hbm_gbs"] * 1e9))),
-               "lm_head": "kvb_lm_head_argmax (f32 logits never stored)",
-               "launches_per_step": {"own": own, "cublas": lib}})
+        for rows_proj in (False, True):
+            dec.set_fused_lm_head(True)
+            dec.set_row_projections(rows_proj)
+            dec.set_lengths(ctx)
+            for _ in range(3):
+                dec.step()
+            dec.set_lengths(ctx)
+            torch.cuda.synchronize()
+            a.record(s)
+            for _ in range(steps):
+                dec.step()
+            b.record(s)
+            b.synchronize()
+            ms_f = a.elapsed_time(b)
+            own, lib = dec.launches_per_step()
+            _emit({"workload": f"cfg4: 16-layer decode, batch {B}, context 1024, 256 greedy steps, "
+                               f"LM head + argmax fused" +
+                               (", projections on kvb_linear_rows" if rows_proj else ""),
+                   "metric": "tokens/s", "value": B * steps / (ms_f * 1e-3), "unit": "tokens/s",
+                   "ms_per_step": ms_f / steps, "bytes_per_step": fused_bytes,
+                   "frac_of_roofline": (B * steps / (ms_f * 1e-3)) /
+                                       (B / (fused_bytes / (peaks["hbm_gbs"] * 1e9))),
+                   "lm_head": "kvb_lm_head_argmax (f32 logits never stored)",
+                   "projections": ("kvb_linear_rows + kvb_linear_silu_mul" if rows_proj
+                                   else "cuBLAS (autotuned) + kvb_silu_mul"),
+                   "launches_per_step": {"own": own, "cublas": lib}})
         dec.set_fused_lm_head(False)
+        dec.set_row_projections(False)
         # the same steps with device-side temperature / top-p sampling in place of argmax,
         # and the two sampling kernels alone on this step's logits
         dec.set_sampling(0.8, 0.95, seed=1)
@@ -648,6 +655,94 @@ def attn5(args):
            "l2": "K/V above L2" if n_seq * per * 4 > (1 << 30) else "flushed between launches"})
 
 
+# ----------------------------------------------------------------------------- projections
+def proj(args):
+    """The decode step's four projections of Llama-3.2-1B for `--seqs` rows (qkv
+    2048 -> 3072, o 2048 -> 2048, down 8192 -> 2048, gate/up 2048 -> 2 x 8192 +
+    SiLU*mul): kvb_linear_rows / kvb_linear_silu_mul against kvb_linear (cuBLAS,
+    autotuned) + kvb_silu_mul.  Each is timed as a chain of 24 calls on 24
+    different weight matrices (together above L2) captured in one CUDA graph, as
+    the decode step runs them, alone and with an RMSNorm launch in front of every
+    call (the step's order).  `--steps 0` runs each form once, uncaptured (a
+    profiler target)."""
+    from kvasir_b200 import _lib as L
+    import ctypes as C
+    peaks, kind = _peaks()
+    s = torch.cuda.Stream()
+    g = Gpu(0, stream=s)
+    lib = L.lib()
+    blas_ws = torch.empty(32 << 20, dtype=torch.uint8, device="cuda")
+    lib.kvb_blas_set_workspace(g._blas, C.c_void_p(blas_ws.data_ptr()), blas_ws.numel())
+    lib.kvb_blas_set_autotune(g._blas, 1)
+    rows, R = args.seqs, 24
+    gen = torch.Generator(device="cuda").manual_seed(3)
+
+    def graph_us(calls, reps=20):
+        with torch.cuda.stream(s):
+            for c in calls:
+                c()
+        s.synchronize()
+        if args.steps == 0:
+            return float("nan")
+        G = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(G, stream=s):
+            for c in calls:
+                c()
+        with torch.cuda.stream(s):
+            G.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(reps):
+                G.replay()
+            e1.record(s)
+        e1.synchronize()
+        return e0.elapsed_time(e1) / reps / len(calls) * 1e3
+
+    with torch.cuda.stream(s):
+        for name, k, out, glu in (("qkv", 2048, 3072, False), ("o", 2048, 2048, False),
+                                  ("down", 8192, 2048, False), ("gate/up + SiLU*mul", 2048, 8192, True)):
+            n_w = 2 * out if glu else out
+            ws = [torch.empty(n_w * k, dtype=torch.bfloat16, device="cuda").normal_(0, 0.02, generator=gen)
+                  for _ in range(R)]
+            x = torch.randn(rows * k, generator=gen, device="cuda").to(torch.bfloat16)
+            nw = torch.ones(k, dtype=torch.bfloat16, device="cuda")
+            h = torch.empty_like(x)
+            y = torch.empty(rows * out, dtype=torch.bfloat16, device="cuda")
+            gu = torch.empty(rows * 2 * out, dtype=torch.bfloat16, device="cuda") if glu else None
+
+            def call(i, pre, mine):
+                def f():
+                    src = x
+                    if pre:
+                        g.rmsnorm(x, nw, h, rows, k, 1e-5)
+                        src = h
+                    if mine:
+                        if glu:
+                            g.linear_silu_mul(src, ws[i], y, rows, k, out)
+                        else:
+                            g.linear_rows(src, ws[i], y, rows, k, out)
+                    elif glu:
+                        g.linear_f16(src, ws[i], gu, rows, k, 2 * out)
+                        g.silu_mul(gu, y, rows, out)
+                    else:
+                        g.linear_f16(src, ws[i], y, rows, k, out)
+                return f
+
+            res = {pre: {mine: graph_us([call(i, pre, mine) for i in range(R)]) for mine in (True, False)}
+                   for pre in (False, True)}
+            wb = n_w * k * 2
+            _emit({"workload": f"{name} projection, {rows} rows, Llama-3.2-1B", "metric": "us",
+                   "value": res[False][True], "unit": "us per call (graph chain)",
+                   "linear_rows_us": res[False][True], "cublas_us": res[False][False],
+                   "after_rmsnorm": {"linear_rows_us": res[True][True], "cublas_us": res[True][False]},
+                   "weight_bytes": wb,
+                   "weight_gbs": wb / (res[False][True] * 1e-6) / 1e9,
+                   "frac_of_peak": wb / (res[False][True] * 1e-6) / 1e9 / peaks["hbm_gbs"],
+                   "peak": f"{peaks['hbm_gbs']} GB/s ({kind})"})
+            del ws
+    assert g.device_error() == 0
+
+
 def run(name, args):
     {"cfg1": cfg1, "cfg2": cfg2, "cfg3": cfg3, "cfg4": cfg4, "sample": sample,
-     "attn5": attn5, "lmhead": lmhead}[name](args)
+     "attn5": attn5, "lmhead": lmhead, "proj": proj}[name](args)
