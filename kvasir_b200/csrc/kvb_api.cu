@@ -297,14 +297,18 @@ static int launch_rope(kvb_stream_t stream, const RopeArgs& a, int rows, int dty
 }
 
 // ---------------------------------------------------------------- decode attention launcher
-// Keys per CTA: aim for ~8 waves of 3 resident CTAs per SM over the worst-case
+// Keys per CTA: aim for ~5 waves of 3 resident CTAs per SM over the worst-case
 // work (every sequence at max_len), at least one 64-key tile per warp -- four
 // per warp once the (sequence, kv head) pairs alone fill every SM, where short
 // chunks only add combine work (measured: batch 32 at context 1088 and config 2
 // gain 1-3 %; one sequence, 8 pairs, needs the smaller chunks' parallelism).
+// Measured at context 16384 on 32 / 64 / 256 sequences: 5 waves 163.3 / 307.4 /
+// 1174.7 us per launch, 8 waves 167.5 / 310.6 / 1188.5, 3 and 4 waves in between,
+// 2 and 16 waves slower (fewer, longer chunks pay fewer CTA start-ups and less
+// combine work, until the last wave's shortfall outweighs that).
 static int decode_chunk_keys(size_t n_seq, size_t n_kv, size_t max_len) {
     const size_t tiles = (max_len + 63) / 64;
-    const size_t target = (size_t)num_sms() * 3 * 8;
+    const size_t target = (size_t)num_sms() * 3 * 5;
     size_t per_cta = (n_seq * n_kv * tiles + target - 1) / target;
     const size_t min_tiles = n_seq * n_kv >= (size_t)num_sms() ? 16 : 4;
     if (per_cta < min_tiles) per_cta = min_tiles;
