@@ -376,7 +376,10 @@ int kvb_argmax_f32(kvb_stream_t stream, const float* logits, size_t rows, size_t
  * multiple of 64 with rows <= 16 ? hidden <= 4096 : hidden <= 2048, 16-byte
  * aligned buffers, else KVB_ERR_UNSUPPORTED.  The workspace
  * (kvb_lm_head_argmax_workspace_bytes(rows)) holds per-CTA partials; its
- * contents need no initialisation.  Two launches. */
+ * contents need no initialisation.  Two launches, both programmatic dependents
+ * of the kernel before them: x is read after that kernel completes, w as soon
+ * as the pass runs (as for kvb_linear_rows, w must not be the output of one of
+ * this library's kernels still in flight). */
 size_t kvb_lm_head_argmax_workspace_bytes(size_t rows);
 int kvb_lm_head_argmax(kvb_stream_t stream, const void* x, size_t x_len, const void* w,
                        size_t w_len, size_t rows, size_t hidden, size_t vocab, void* workspace,

@@ -59,6 +59,10 @@ struct DecodeArgs {
     uint16_t* kc_w;
     uint16_t* vc_w;
     long long cache_seq_stride;  // elements between sequences' caches
+    // The cache rows before each sequence's new key are final (no kernel that can still
+    // be running writes them: the decode-step driver's launches).  The first K/V tiles
+    // are then requested before griddepcontrol.wait; otherwise nothing is read before it.
+    int kv_ready;
 };
 
 // First row (of 64 elements) of the 64-key tile starting at key kt0 (a multiple of
@@ -103,10 +107,12 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     // shortest pieces of work (longest first: a shorter tail).
     // the combine pass (a programmatic dependent) may launch once every CTA got here;
     // it still waits for this grid's completion before it reads any partial.  This
-    // kernel is launched the same way after the qkv projection: it touches no memory
-    // before that kernel has completed.
+    // kernel is launched the same way after the qkv projection: it reads memory that
+    // the preceding kernels write only after griddepcontrol.wait -- at once, or with
+    // a.kv_ready after requesting its first K/V tiles (those rows are final, and the
+    // lengths were written by an earlier step).
     asm volatile("griddepcontrol.launch_dependents;");
-    asm volatile("griddepcontrol.wait;" ::: "memory");
+    if (!a.kv_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
     const int kvh = blockIdx.x, b = blockIdx.y;
     const int from_end = (int)gridDim.z - 1 - (int)blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -117,6 +123,7 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     const int n_chunks = (len + a.chunk_keys - 1) / a.chunk_keys;
     T* outb = reinterpret_cast<T*>(a.out) + (size_t)b * a.out_row_stride + (size_t)kvh * G * 64;
     if (len == 0) {  // no keys: defined as a zero output row
+        if (a.kv_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
         if (from_end == 0)
             for (int i = threadIdx.x; i < G * 64; i += blockDim.x) outb[i] = Elem<T>::from_f(0.f);
         return;
@@ -161,6 +168,7 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     const int kt_first = key_begin + warp * kDecTileKeys;
     const bool early = kt_first < key_end && !(appends && rope_p < kt_first + kDecTileKeys);
     if (early && lane == 0) issue(kt_first);
+    if (a.kv_ready) asm volatile("griddepcontrol.wait;" ::: "memory");  // q, the new row
 
     if (appends) {
         const T* kin = reinterpret_cast<const T*>(a.q) + (size_t)b * a.q_row_stride +

@@ -363,6 +363,7 @@ struct DecodeLaunch {
     const float* rope_cos = nullptr;
     const float* rope_sin = nullptr;
     size_t rope_max_pos = 0;
+    bool kv_ready = false;  // DecodeArgs::kv_ready
 };
 
 static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
@@ -398,6 +399,7 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
     a.kc_w = static_cast<uint16_t*>(const_cast<void*>(L.kc));
     a.vc_w = static_cast<uint16_t*>(const_cast<void*>(L.vc));
     a.cache_seq_stride = (long long)L.seq_stride;
+    a.kv_ready = L.kv_ready ? 1 : 0;
     int ck = decode_chunk_keys(L.n_seq, L.n_kv, L.max_len);
     const size_t need = decode_ws_bytes(L.n_seq, L.max_len, L.n_q, L.n_kv);
     if (need == 0 || L.ws == nullptr || L.ws_len < need || !aligned(L.ws, 16)) {
@@ -1272,13 +1274,14 @@ int kvb_attention_decode(kvb_stream_t stream, const void* q, size_t q_row_stride
     return launch_generic_attn(stream, a, n_seq, dtype);
 }
 
-int kvb_rope_attention_decode(kvb_stream_t stream, const void* qkv, size_t qkv_len,
-                              const float* cos_t, const float* sin_t, size_t table_len, void* kc,
-                              void* vc, size_t seq_stride, size_t cache_len, const int32_t* lens,
-                              size_t n_seq, size_t max_len, size_t n_q, size_t n_kv,
-                              size_t head_dim, size_t max_seq, float scale, void* out,
-                              size_t out_row_stride, void* workspace, size_t workspace_len,
-                              int dtype) {
+static int rope_attention_decode_impl(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                      const float* cos_t, const float* sin_t, size_t table_len,
+                                      void* kc, void* vc, size_t seq_stride, size_t cache_len,
+                                      const int32_t* lens, size_t n_seq, size_t max_len,
+                                      size_t n_q, size_t n_kv, size_t head_dim, size_t max_seq,
+                                      float scale, void* out, size_t out_row_stride,
+                                      void* workspace, size_t workspace_len, int dtype,
+                                      bool kv_ready) {
     KVB_CHECK_DTYPE(dtype);
     const size_t stride = (n_q + 2 * n_kv) * head_dim;
     const size_t per_seq = n_kv * max_seq * head_dim;
@@ -1334,7 +1337,21 @@ int kvb_rope_attention_decode(kvb_stream_t stream, const void* qkv, size_t qkv_l
     L.rope_cos = cos_t;
     L.rope_sin = sin_t;
     L.rope_max_pos = table_len / (head_dim / 2);
+    L.kv_ready = kv_ready;
     return launch_decode_mma(stream, L);
+}
+
+int kvb_rope_attention_decode(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                              const float* cos_t, const float* sin_t, size_t table_len, void* kc,
+                              void* vc, size_t seq_stride, size_t cache_len, const int32_t* lens,
+                              size_t n_seq, size_t max_len, size_t n_q, size_t n_kv,
+                              size_t head_dim, size_t max_seq, float scale, void* out,
+                              size_t out_row_stride, void* workspace, size_t workspace_len,
+                              int dtype) {
+    return rope_attention_decode_impl(stream, qkv, qkv_len, cos_t, sin_t, table_len, kc, vc,
+                                      seq_stride, cache_len, lens, n_seq, max_len, n_q, n_kv,
+                                      head_dim, max_seq, scale, out, out_row_stride, workspace,
+                                      workspace_len, dtype, false);
 }
 
 int kvb_attention_prefill(kvb_stream_t stream, const void* qkv, size_t qkv_len, const void* kc,
@@ -1451,14 +1468,12 @@ int kvb_attention_prefill_paged(kvb_stream_t stream, const void* qkv, size_t qkv
 
 // kvb_rope_kv_append_paged (one row per sequence, at position lens[b] - 1) and
 // kvb_attention_decode_paged in one launch.
-int kvb_rope_attention_decode_paged(kvb_stream_t stream, const void* qkv, size_t qkv_len,
-                                    const float* cos_t, const float* sin_t, size_t table_len,
-                                    void* k_pool, void* v_pool, size_t pool_len,
-                                    const int32_t* block_table, size_t max_blocks,
-                                    size_t block_size, const int32_t* lens, size_t n_seq,
-                                    size_t max_len, size_t n_q, size_t n_kv, size_t head_dim,
-                                    float scale, void* out, size_t out_row_stride, void* workspace,
-                                    size_t workspace_len, int dtype) {
+static int rope_attention_decode_paged_impl(
+    kvb_stream_t stream, const void* qkv, size_t qkv_len, const float* cos_t, const float* sin_t,
+    size_t table_len, void* k_pool, void* v_pool, size_t pool_len, const int32_t* block_table,
+    size_t max_blocks, size_t block_size, const int32_t* lens, size_t n_seq, size_t max_len,
+    size_t n_q, size_t n_kv, size_t head_dim, float scale, void* out, size_t out_row_stride,
+    void* workspace, size_t workspace_len, int dtype, bool kv_ready) {
     KVB_CHECK_DTYPE(dtype);
     const size_t stride = (n_q + 2 * n_kv) * head_dim;
     KVB_CHECK(n_kv > 0 && n_q % n_kv == 0,
@@ -1518,7 +1533,22 @@ int kvb_rope_attention_decode_paged(kvb_stream_t stream, const void* qkv, size_t
     L.rope_cos = cos_t;
     L.rope_sin = sin_t;
     L.rope_max_pos = table_len / (head_dim / 2);
+    L.kv_ready = kv_ready;
     return launch_decode_mma(stream, L);
+}
+
+int kvb_rope_attention_decode_paged(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                    const float* cos_t, const float* sin_t, size_t table_len,
+                                    void* k_pool, void* v_pool, size_t pool_len,
+                                    const int32_t* block_table, size_t max_blocks,
+                                    size_t block_size, const int32_t* lens, size_t n_seq,
+                                    size_t max_len, size_t n_q, size_t n_kv, size_t head_dim,
+                                    float scale, void* out, size_t out_row_stride, void* workspace,
+                                    size_t workspace_len, int dtype) {
+    return rope_attention_decode_paged_impl(stream, qkv, qkv_len, cos_t, sin_t, table_len, k_pool,
+                                            v_pool, pool_len, block_table, max_blocks, block_size,
+                                            lens, n_seq, max_len, n_q, n_kv, head_dim, scale, out,
+                                            out_row_stride, workspace, workspace_len, dtype, false);
 }
 
 int kvb_attention_decode_paged(kvb_stream_t stream, const void* q, size_t q_row_stride,
@@ -1796,18 +1826,21 @@ int kvb_lm_head_argmax(kvb_stream_t stream, const void* x, size_t x_len, const v
     a.part_i = reinterpret_cast<int32_t*>(static_cast<float*>(workspace) + (size_t)kLmMaxCtas * rows);
     const uint32_t fmt = dtype == KVB_BF16 ? 1u : 0u;
     const int smem = lm_smem_bytes(n, (int)hidden);
+    cudaError_t e;
     if (n == 16) {
         set_max_smem(lm_head_argmax_kernel<16>, lm_smem_bytes(16, kLmMaxXBytes / 32));
-        lm_head_argmax_kernel<16><<<grid, kLmThreads, smem, stream>>>(wmap, xmap, a, fmt);
+        e = launch_pdl(lm_head_argmax_kernel<16>, dim3(grid), dim3(kLmThreads), smem, stream, wmap,
+                       xmap, a, fmt);
     } else {
         set_max_smem(lm_head_argmax_kernel<32>, lm_smem_bytes(32, kLmMaxXBytes / 64));
-        lm_head_argmax_kernel<32><<<grid, kLmThreads, smem, stream>>>(wmap, xmap, a, fmt);
+        e = launch_pdl(lm_head_argmax_kernel<32>, dim3(grid), dim3(kLmThreads), smem, stream, wmap,
+                       xmap, a, fmt);
     }
-    KVB_CHECK_LAUNCH("lm_head_argmax launch");
-    lm_head_argmax_finish_kernel<<<(unsigned)rows, 32, 0, stream>>>(a.part_v, a.part_i, grid,
-                                                                    (int)rows, ids, advance,
-                                                                    advance2);
-    KVB_CHECK_LAUNCH("lm_head_argmax finish launch");
+    if (e != cudaSuccess) return cuda_fail(e, "lm_head_argmax launch");
+    e = launch_pdl(lm_head_argmax_finish_kernel, dim3((unsigned)rows), dim3(32), 0, stream,
+                   (const float*)a.part_v, (const int32_t*)a.part_i, grid, (int)rows, ids, advance,
+                   advance2);
+    if (e != cudaSuccess) return cuda_fail(e, "lm_head_argmax finish launch");
     return KVB_OK;
 }
 
@@ -1863,3 +1896,35 @@ int kvb_selftest_wait_timeout(kvb_stream_t stream, uint32_t limit_ms) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ decode-step forms
+namespace kvb {
+
+int rope_attention_decode_in_step(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                  const float* cos_t, const float* sin_t, size_t table_len,
+                                  void* kc, void* vc, size_t seq_stride, size_t cache_len,
+                                  const int32_t* lens, size_t n_seq, size_t max_len, size_t n_q,
+                                  size_t n_kv, size_t head_dim, size_t max_seq, float scale,
+                                  void* out, size_t out_row_stride, void* workspace,
+                                  size_t workspace_len, int dtype) {
+    return rope_attention_decode_impl(stream, qkv, qkv_len, cos_t, sin_t, table_len, kc, vc,
+                                      seq_stride, cache_len, lens, n_seq, max_len, n_q, n_kv,
+                                      head_dim, max_seq, scale, out, out_row_stride, workspace,
+                                      workspace_len, dtype, true);
+}
+
+int rope_attention_decode_paged_in_step(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                        const float* cos_t, const float* sin_t, size_t table_len,
+                                        void* k_pool, void* v_pool, size_t pool_len,
+                                        const int32_t* block_table, size_t max_blocks,
+                                        size_t block_size, const int32_t* lens, size_t n_seq,
+                                        size_t max_len, size_t n_q, size_t n_kv, size_t head_dim,
+                                        float scale, void* out, size_t out_row_stride,
+                                        void* workspace, size_t workspace_len, int dtype) {
+    return rope_attention_decode_paged_impl(stream, qkv, qkv_len, cos_t, sin_t, table_len, k_pool,
+                                            v_pool, pool_len, block_table, max_blocks, block_size,
+                                            lens, n_seq, max_len, n_q, n_kv, head_dim, scale, out,
+                                            out_row_stride, workspace, workspace_len, dtype, true);
+}
+
+}  // namespace kvb

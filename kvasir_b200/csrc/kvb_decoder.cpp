@@ -8,7 +8,8 @@
 // projection -> SiLU*mul -> down projection -> residual add; then the final
 // norm, the tied LM head (f32 logits) and greedy argmax.  The residual add is
 // fused into the following rmsnorm (kvb_add_rmsnorm); RoPE, the KV append and
-// decode attention are one launch (kvb_rope_attention_decode) on contiguous
+// decode attention are one launch (kvb_rope_attention_decode, in the step form
+// that starts its K/V reads before the preceding kernel completes) on contiguous
 // caches at head_dim 64.  All device memory is caller-owned.
 #include <cuda_runtime.h>
 
@@ -153,11 +154,11 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
             uint8_t* kl = d->kc + (size_t)l * layer_elems * 2;
             uint8_t* vl = d->vc + (size_t)l * layer_elems * 2;
             if (hd == 64 && nq / nkv <= 16) {  // RoPE, KV append and attention: one launch
-                STEP(kvb_rope_attention_decode(s, d->at(L.qkv), B * qkvd, d->cos_t, d->sin_t,
-                                               table_len, kl, vl, seq_stride, layer_elems,
-                                               d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd,
-                                               max_seq, 1.0f / sqrtf((float)hd), d->at(L.attn), qd,
-                                               d->at(L.attn_ws), L.attn_ws_len, dt),
+                STEP(kvb::rope_attention_decode_in_step(
+                         s, d->at(L.qkv), B * qkvd, d->cos_t, d->sin_t, table_len, kl, vl,
+                         seq_stride, layer_elems, d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd,
+                         max_seq, 1.0f / sqrtf((float)hd), d->at(L.attn), qd, d->at(L.attn_ws),
+                         L.attn_ws_len, dt),
                      false);
             } else {
                 STEP(kvb_rope_kv_append_batched(s, d->at(L.qkv), B, d->at<int32_t>(L.pos), d->cos_t,
@@ -174,12 +175,11 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
             uint8_t* kl = d->kpool + (size_t)l * d->pool_len * 2;
             uint8_t* vl = d->vpool + (size_t)l * d->pool_len * 2;
             // paged mode requires head_dim 64 and 64-key blocks: always one launch
-            STEP(kvb_rope_attention_decode_paged(s, d->at(L.qkv), B * qkvd, d->cos_t, d->sin_t,
-                                                 table_len, kl, vl, d->pool_len, d->block_table,
-                                                 d->max_blocks, d->block_size,
-                                                 d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd,
-                                                 1.0f / sqrtf((float)hd), d->at(L.attn), qd,
-                                                 d->at(L.attn_ws), L.attn_ws_len, dt),
+            STEP(kvb::rope_attention_decode_paged_in_step(
+                     s, d->at(L.qkv), B * qkvd, d->cos_t, d->sin_t, table_len, kl, vl,
+                     d->pool_len, d->block_table, d->max_blocks, d->block_size,
+                     d->at<int32_t>(L.lens), B, max_seq, nq, nkv, hd, 1.0f / sqrtf((float)hd),
+                     d->at(L.attn), qd, d->at(L.attn_ws), L.attn_ws_len, dt),
                  false);
         }
         if (L.attn_ws_len > 0) ++own;  // the split-KV combine pass

@@ -42,6 +42,28 @@ int encode_tmap(CUtensorMap* map, const void* base, int rank, const uint64_t* di
 // attribute or occupancy call while a step is being recorded).
 void sample_prepare();
 
+// kvb_rope_attention_decode(_paged) for the decode-step driver.  Inside its step
+// the cache rows before each sequence's new key are final: no kernel that can
+// still be running when the launch starts writes them (each layer's cache is
+// written only by its own attention launch, and steps are separate graph
+// launches).  The decode kernel may then request its first K/V tiles before it
+// waits for the preceding kernel (griddepcontrol.wait).
+int rope_attention_decode_in_step(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                  const float* cos_t, const float* sin_t, size_t table_len,
+                                  void* kc, void* vc, size_t seq_stride, size_t cache_len,
+                                  const int32_t* lens, size_t n_seq, size_t max_len, size_t n_q,
+                                  size_t n_kv, size_t head_dim, size_t max_seq, float scale,
+                                  void* out, size_t out_row_stride, void* workspace,
+                                  size_t workspace_len, int dtype);
+int rope_attention_decode_paged_in_step(kvb_stream_t stream, const void* qkv, size_t qkv_len,
+                                        const float* cos_t, const float* sin_t, size_t table_len,
+                                        void* k_pool, void* v_pool, size_t pool_len,
+                                        const int32_t* block_table, size_t max_blocks,
+                                        size_t block_size, const int32_t* lens, size_t n_seq,
+                                        size_t max_len, size_t n_q, size_t n_kv, size_t head_dim,
+                                        float scale, void* out, size_t out_row_stride,
+                                        void* workspace, size_t workspace_len, int dtype);
+
 }  // namespace kvb
 
 #define KVB_CHECK(cond, ...)                                         \

@@ -68,6 +68,10 @@ __global__ void __launch_bounds__(kLmThreads, 1)
     uint8_t* sw = sx + (size_t)kchunks * N * 128;  // kLmStages x 16 KB
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+    // Launched as a programmatic dependent of the kernel before it: W (never the output
+    // of a kernel still running) is requested before griddepcontrol.wait, x after it.
+    // The merge kernel after this one may launch at once; it waits for this grid.
+    asm volatile("griddepcontrol.launch_dependents;");
     if (threadIdx.x == 0) {
         mbar_init(&x_full, 1);
         for (int s = 0; s < kLmStages; ++s) {
@@ -92,12 +96,19 @@ __global__ void __launch_bounds__(kLmThreads, 1)
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             tma_prefetch_desc(&wmap);
-            mbar_expect_tx(&x_full, (uint32_t)(kchunks * N * 128));
-            for (int c = 0; c < kchunks; ++c) tma_load_2d(sx + (size_t)c * N * 128, &xmap, &x_full, c * kLmK, 0);
+            tma_prefetch_desc(&xmap);
             int it = 0;
+            bool x_issued = false;
             for (int t = blockIdx.x; t < a.n_tiles && !s_err; t += gridDim.x) {
                 for (int c = 0; c < kchunks; ++c, ++it) {
                     const int s = it % kLmStages;
+                    if (it == kLmStages && !x_issued) {  // the ring is full: now x
+                        asm volatile("griddepcontrol.wait;" ::: "memory");
+                        mbar_expect_tx(&x_full, (uint32_t)(kchunks * N * 128));
+                        for (int k = 0; k < kchunks; ++k)
+                            tma_load_2d(sx + (size_t)k * N * 128, &xmap, &x_full, k * kLmK, 0);
+                        x_issued = true;
+                    }
                     if (it >= kLmStages && !mbar_wait(&empty[s], ((it - kLmStages) / kLmStages) & 1)) {
                         s_err = 1;
                         break;
@@ -105,6 +116,12 @@ __global__ void __launch_bounds__(kLmThreads, 1)
                     mbar_expect_tx(&full[s], kLmStageBytes);
                     tma_load_2d(sw + s * kLmStageBytes, &wmap, &full[s], c * kLmK, t * kLmRows);
                 }
+            }
+            if (!x_issued) {  // fewer W chunks than stages in this CTA
+                asm volatile("griddepcontrol.wait;" ::: "memory");
+                mbar_expect_tx(&x_full, (uint32_t)(kchunks * N * 128));
+                for (int k = 0; k < kchunks; ++k)
+                    tma_load_2d(sx + (size_t)k * N * 128, &xmap, &x_full, k * kLmK, 0);
             }
             if (s_err) {  // let every copy this CTA issued land before it exits (bounded)
                 for (int j = it - kLmStages < 0 ? 0 : it - kLmStages; j < it; ++j)
@@ -186,6 +203,8 @@ __global__ void __launch_bounds__(kLmThreads, 1)
             }
         }
         named_bar_sync(1, 128);
+        // the partials' buffer was last read by an earlier merge kernel
+        asm volatile("griddepcontrol.wait;" ::: "memory");
         if (threadIdx.x < a.rows) {
             const int r = threadIdx.x;
             float x = red_v[0][r];
@@ -210,6 +229,7 @@ __global__ void __launch_bounds__(32) lm_head_argmax_finish_kernel(const float* 
                                                                    int n_parts, int rows,
                                                                    int32_t* ids, int32_t* adv,
                                                                    int32_t* adv2) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");  // the partials of the pass before
     const int r = blockIdx.x, lane = threadIdx.x;
     float x = -INFINITY;
     int i = 0x7fffffff;
