@@ -103,7 +103,8 @@ __global__ void __launch_bounds__(kLrThreads, 1)
     const int tile = (int)blockIdx.x / n_split, split = (int)blockIdx.x % n_split;
     const int c0 = split * a.kchunks / n_split;
     const int nc = (split + 1) * a.kchunks / n_split - c0;  // >= 1: splits <= kchunks
-    const int u0 = split * kUnits / n_split, u1 = (split + 1) * kUnits / n_split;  // this CTA's
+    // the units of the output tile this CTA sums over the slices and writes
+    const int u0 = split * kUnits / n_split, u1 = (split + 1) * kUnits / n_split;
 
     // a kernel launched as this grid's programmatic dependent may start its prologue
     asm volatile("griddepcontrol.launch_dependents;");
@@ -191,7 +192,8 @@ __global__ void __launch_bounds__(kLrThreads, 1)
         // ------------------------------------------------------------ accumulator -> units
         // The tile in unit order over the ring: every MMA has read its stages when
         // d_full completes, and every copy into them has landed.  Thread m holds W
-        // row m of the tile for all N rows of X.
+        // row m of the tile for all N rows of X; a row of X takes 128 floats in both
+        // unit orders, at offset mo.
         const int m = warp * 32 + lane;
         const int mo = kGlu ? ((m & 63) >> 2) * 8 + (m >= 64 ? 4 : 0) + (m & 3) : m;
         const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
@@ -204,7 +206,7 @@ __global__ void __launch_bounds__(kLrThreads, 1)
                 else tmem_ld16(tmem + lane_off + (uint32_t)c, v);
                 tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < kLd; ++j) part[(c + j) * (kGlu ? 128 : kLrTile) + mo] = v[j];
+                for (int j = 0; j < kLd; ++j) part[(c + j) * kLrTile + mo] = v[j];
             }
         } else if (lane == 0) {
             s_err = 1;
