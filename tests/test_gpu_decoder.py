@@ -125,10 +125,12 @@ def test_decoder_step_host_equals_device_step():
     b.close()
 
 
-def test_decoder_paged_cache_equals_contiguous():
+@pytest.mark.parametrize("row_proj", [False, True])
+def test_decoder_paged_cache_equals_contiguous(row_proj):
     """kvb_decoder_use_paged_cache: the same step over a shuffled pool of 64-key
     blocks (one block table for all layers) gives the same logits and ids, bit for
-    bit, as the contiguous cache, step after step (the appended K/V included)."""
+    bit, as the contiguous cache, step after step (the appended K/V included);
+    with the cuBLAS projections and with kvb_linear_rows / kvb_linear_silu_mul."""
     from kvasir_b200.decoder import Decoder
     cfg = _tiny_cfg()
     rng = np.random.default_rng(23)
@@ -155,6 +157,7 @@ def test_decoder_paged_cache_equals_contiguous():
     decs = []
     for paged in (False, True):
         d = Decoder(cfg, n_seq, max_seq, weights=_to_torch(wb, cfg))
+        d.set_row_projections(row_proj)
         d.kc.copy_(kc)
         d.vc.copy_(vc)
         if paged:
