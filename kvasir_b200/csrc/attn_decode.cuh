@@ -28,7 +28,8 @@ namespace kvb {
 constexpr int kDecTileKeys = 64;
 constexpr int kDecWarps = 4;
 constexpr int kDecTileBytes = kDecTileKeys * 64 * 2;  // one K (or V) tile
-constexpr int kDecSmemBytes = kDecWarps * 2 * kDecTileBytes + 1024;  // + alignment slack
+// the tiles, a chunk's folded state (G <= 16 heads x 66 floats), alignment slack
+constexpr int kDecSmemBytes = kDecWarps * 2 * kDecTileBytes + 16 * 66 * 4 + 1024;
 
 struct DecodeArgs {
     const uint16_t* q;
@@ -59,6 +60,7 @@ struct DecodeArgs {
     uint16_t* kc_w;
     uint16_t* vc_w;
     long long cache_seq_stride;  // elements between sequences' caches
+    int fold;                    // chunks folded in-kernel through a cluster (see the kernel)
     // The cache rows before each sequence's new key are final (no kernel that can still
     // be running writes them: the decode-step driver's launches).  The first K/V tiles
     // are then requested before griddepcontrol.wait; otherwise nothing is read before it.
@@ -93,28 +95,14 @@ __device__ __forceinline__ int decode_len(const DecodeArgs& a, int b) {
     return len;
 }
 
+// One chunk of attn_decode_kernel: chunk slot `from_end` (counted from the end of
+// the sequence) of kv head kvh of sequence b.  Called by every thread of the CTA.
+// Its result goes to the output row (a one-chunk sequence), to `fold` (this CTA's
+// shared memory, for the cluster fold) or to the workspace.
 template <typename T, bool kRope>
-__global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                             const __grid_constant__ CUtensorMap vmap,
-                                                             DecodeArgs a) {
-    extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t bars[kDecWarps];
-    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                               ~uintptr_t(1023));
-    // Grid (kv head, sequence, chunk slot); the slot counts chunks from the END of the
-    // sequence, and the last slot holds every sequence's last, partial chunk.  CTAs are
-    // dispatched slot by slot, so full chunks go first and the final wave holds the
-    // shortest pieces of work (longest first: a shorter tail).
-    // the combine pass (a programmatic dependent) may launch once every CTA got here;
-    // it still waits for this grid's completion before it reads any partial.  This
-    // kernel is launched the same way after the qkv projection: it reads memory that
-    // the preceding kernels write only after griddepcontrol.wait -- at once, or with
-    // a.kv_ready after requesting its first K/V tiles (those rows are final, and the
-    // lengths were written by an earlier step).
-    asm volatile("griddepcontrol.launch_dependents;");
-    if (!a.kv_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
-    const int kvh = blockIdx.x, b = blockIdx.y;
-    const int from_end = (int)gridDim.z - 1 - (int)blockIdx.z;
+__device__ __forceinline__ void decode_chunk(const CUtensorMap& kmap, const CUtensorMap& vmap,
+                                             const DecodeArgs& a, uint8_t* smem, uint64_t* bars,
+                                             int kvh, int b, int from_end, float* fold) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, c = lane & 3;
     const int G = a.group;
@@ -370,7 +358,7 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
     __syncthreads();
     float* wsb = nullptr;
     if (n_chunks > 1)
-        wsb = a.ws + (((size_t)b * a.n_kv + kvh) * a.max_chunks + chunk) * (size_t)G * 66;
+        wsb = fold ? fold : a.ws + (((size_t)b * a.n_kv + kvh) * a.max_chunks + chunk) * (size_t)G * 66;
     for (int i = threadIdx.x; i < G * 64; i += blockDim.x) {
         const int r = i >> 6, d = i & 63;
         float M = -INFINITY;
@@ -396,6 +384,66 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
             }
         }
     }
+}
+
+// Grid (kv head, sequence, chunk slot), or with a.fold (chunk slot, kv head,
+// sequence) in clusters of max_chunks CTAs.  The slot counts chunks from the END
+// of the sequence, and the last slot holds every sequence's last, partial chunk.
+// CTAs are dispatched slot by slot, so full chunks go first and the final wave
+// holds the shortest pieces of work (longest first: a shorter tail).
+// The combine pass (a programmatic dependent) may launch once every CTA got here;
+// it still waits for this grid's completion before it reads any partial.  This
+// kernel is launched the same way after the qkv projection: it reads memory that
+// the preceding kernels write only after griddepcontrol.wait -- at once, or with
+// a.kv_ready after requesting its first K/V tiles (those rows are final, and the
+// lengths were written by an earlier step).
+// a.fold: the chunks of one (sequence, kv head) form a cluster, and the CTA of the
+// last chunk folds the others' partial states through distributed shared memory
+// with the arithmetic of attn_combine_kernel (so the rows are the same bits), in
+// place of the workspace and the combine pass.  For small grids, where every
+// cluster is resident at once.  Every CTA of a cluster with keys passes both
+// cluster barriers; a cluster of an empty sequence passes none.
+template <typename T, bool kRope>
+__global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                             const __grid_constant__ CUtensorMap vmap,
+                                                             DecodeArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t bars[kDecWarps];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~uintptr_t(1023));
+    asm volatile("griddepcontrol.launch_dependents;");
+    if (!a.kv_ready) asm volatile("griddepcontrol.wait;" ::: "memory");
+    const int slot = a.fold ? (int)blockIdx.x : (int)blockIdx.z;
+    const int kvh = a.fold ? (int)blockIdx.y : (int)blockIdx.x;
+    const int b = a.fold ? (int)blockIdx.z : (int)blockIdx.y;
+    const int from_end = a.max_chunks - 1 - slot;
+    float* st = reinterpret_cast<float*>(smem + kDecWarps * 2 * kDecTileBytes);  // [G][66]
+    decode_chunk<T, kRope>(kmap, vmap, a, smem, bars, kvh, b, from_end, a.fold ? st : nullptr);
+    if (!a.fold) return;
+    const int G = a.group;
+    const int len = decode_len(a, b);
+    if (len == 0) return;  // the whole cluster: its row was written as zeros
+    const int n_chunks = (len + a.chunk_keys - 1) / a.chunk_keys;
+    cluster_sync();  // every chunk's state is in its CTA's shared memory
+    if (n_chunks > 1 && slot == a.max_chunks - 1) {
+        // chunk c of the sequence is cluster rank max_chunks - n_chunks + c
+        const uint32_t r0 = (uint32_t)(a.max_chunks - n_chunks);
+        T* outb = reinterpret_cast<T*>(a.out) + (size_t)b * a.out_row_stride + (size_t)kvh * G * 64;
+        for (int i = threadIdx.x; i < G * 64; i += blockDim.x) {
+            const int r = i >> 6;
+            float Mn = -INFINITY;
+            for (int c = 0; c < n_chunks; ++c) Mn = fmaxf(Mn, dsmem_ld(st + G * 64 + r, r0 + c));
+            float Lu = 0.f, Ou = 0.f;
+            for (int c = 0; c < n_chunks; ++c) {
+                const float mc = dsmem_ld(st + G * 64 + r, r0 + c);
+                const float f = mc == -INFINITY ? 0.f : exp2f(mc - Mn);
+                Lu += dsmem_ld(st + G * 65 + r, r0 + c) * f;
+                Ou += dsmem_ld(st + i, r0 + c) * f;
+            }
+            outb[i] = Elem<T>::from_f(Ou / Lu);
+        }
+    }
+    cluster_sync();  // no CTA leaves while the fold may still read its state
 }
 
 // Folds the per-chunk partials of every (sequence, kv head) with more than one chunk.

@@ -415,12 +415,33 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
     a.max_chunks = (int)((L.max_len + ck - 1) / ck);
     if (a.max_chunks < 1) a.max_chunks = 1;
 
-    dim3 grid((unsigned)L.n_kv, (unsigned)L.n_seq, a.max_chunks);
+    // Small split grids (every CTA resident at once, at most 8 chunks per sequence):
+    // the chunks of a (sequence, kv head) form a cluster and fold in the kernel, with
+    // no combine pass.  Measured on the one-sequence decode step: the combine launch
+    // and its programmatic boundary cost ~3.6 us per layer.
+    const size_t n_ctas = L.n_kv * L.n_seq * (size_t)a.max_chunks;
+    a.fold = (a.ws != nullptr && a.max_chunks >= 2 && a.max_chunks <= 8 &&
+              n_ctas <= (size_t)num_sms() * 3) ? 1 : 0;
+    cudaLaunchConfig_t dcfg = {};
+    dcfg.gridDim = a.fold ? dim3((unsigned)a.max_chunks, (unsigned)L.n_kv, (unsigned)L.n_seq)
+                          : dim3((unsigned)L.n_kv, (unsigned)L.n_seq, (unsigned)a.max_chunks);
+    dcfg.blockDim = dim3(128);
+    dcfg.dynamicSmemBytes = kDecSmemBytes;
+    dcfg.stream = stream;
+    cudaLaunchAttribute dattr[2];
+    dattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    dattr[0].val.programmaticStreamSerializationAllowed = 1;
+    dattr[1].id = cudaLaunchAttributeClusterDimension;
+    dattr[1].val.clusterDim.x = (unsigned)a.max_chunks;
+    dattr[1].val.clusterDim.y = 1;
+    dattr[1].val.clusterDim.z = 1;
+    dcfg.attrs = dattr;
+    dcfg.numAttrs = a.fold ? 2 : 1;
 #define KVB_DECODE_LAUNCH(T, ROPE)                                                   \
     do {                                                                             \
         set_max_smem(attn_decode_kernel<T, ROPE>, kDecSmemBytes);                    \
-        const cudaError_t le = launch_pdl(attn_decode_kernel<T, ROPE>, grid, dim3(128),  \
-                                          kDecSmemBytes, stream, kmap, vmap, a);      \
+        const cudaError_t le = cudaLaunchKernelEx(&dcfg, attn_decode_kernel<T, ROPE>,  \
+                                                  kmap, vmap, a);                    \
         if (le != cudaSuccess) return cuda_fail(le, "attention decode launch");       \
     } while (0)
     if (L.dtype == KVB_BF16) {
@@ -432,7 +453,7 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
     }
 #undef KVB_DECODE_LAUNCH
     KVB_CHECK_LAUNCH("attention decode launch");
-    if (a.max_chunks > 1) {
+    if (a.max_chunks > 1 && !a.fold) {
         // programmatic dependent launch: set-up overlaps the decode kernel's tail
         const int per_bytes = a.group * 66 * 4;
         const int cap = kCombineSmemBytes / per_bytes;

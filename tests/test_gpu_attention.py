@@ -95,6 +95,29 @@ def _run_batched(g, q, kc, vc, lens, n_q, n_kv, hd, max_seq, per, use_ws=True, d
     return host_f32(out, dtype)
 
 
+def test_decode_cluster_fold_equals_combine_pass(g):
+    """Small split grids fold their chunks inside the decode kernel (a cluster per
+    (sequence, kv head), distributed shared memory) instead of the workspace and the
+    combine pass, with the combine's arithmetic: the rows are the same bits.  8
+    sequences of 2000 keys are 8 chunks each, 512 CTAs (above one wave: workspace +
+    combine); the first 5 of them, 320 CTAs, fold; both use 256-key chunks."""
+    rng = np.random.default_rng(77)
+    n_q, n_kv, hd = 32, 8, 64
+    lens = [2000] * 8
+    q, kc, vc, max_seq, per = _batched_case(rng, lens)
+    q = O.from_f32(O.to_f32(q) * np.float32(3.0))  # peaked rows: the fold's weights matter
+    split = _run_batched(g, q, kc, vc, lens, n_q, n_kv, hd, max_seq, per)
+    n5 = 5
+    fold = _run_batched(g, q[:n5 * n_q * hd], kc[:n5 * per], vc[:n5 * per], lens[:n5], n_q,
+                        n_kv, hd, max_seq, per)
+    assert g.device_error() == 0
+    np.testing.assert_array_equal(fold.view(np.uint32), split[:n5 * n_q * hd].view(np.uint32))
+    want = O.attention_decode(q[:n5 * n_q * hd], n_q * hd, kc[:n5 * per], vc[:n5 * per],
+                              np.array(lens[:n5], np.int32), n_q, n_kv, hd, max_seq, 1 / 8.0)
+    err = np.abs(fold.astype(np.float64) - want)
+    assert np.all(err <= 2e-3 + np.abs(want) * 2.0 ** -8), err.max()
+
+
 def test_batched_decode_config2(g):
     """64 sequences, lengths U[1, 4096], 32/8 heads, hd 64,
     N(0,1) Q/K/V, scale 1/8."""
@@ -110,12 +133,15 @@ def test_batched_decode_config2(g):
     assert g.device_error() == 0
 
 
-@pytest.mark.parametrize("length,q_std", [(16385, 1.0), (700, 4.0)])
+@pytest.mark.parametrize("length,q_std", [(16385, 1.0), (2000, 4.0)])
 def test_decode_error_before_output_rounding(g, length, q_std):
     """The split-KV decode kernel's own error, before its output is rounded: 8
     sequences, each split over several chunks -- at the config-5 length with
-    N(0,1) inputs (flat softmax, small outputs), and at 700 keys with q scaled
-    by 4 (peaked softmax: outputs of unit scale, where the bar bites).
+    N(0,1) inputs (flat softmax, small outputs), and at 2000 keys with q scaled
+    by 4 (peaked softmax: outputs of unit scale, where the bar bites).  Both
+    grids are above one wave (33 and 8 chunks of 64 (sequence, kv head) pairs),
+    so the chunks' partials go to the workspace rather than being folded in the
+    kernel.
     Every chunk leaves f32 partials in the workspace -- per query head the
     unnormalised O row, the running max m (log2 units) and the sum l -- which
     are folded here in f64 (O = sum_c 2^(m_c - M) O_c / sum_c 2^(m_c - M) l_c)
