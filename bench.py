@@ -440,8 +440,9 @@ def run_decode(args):
 
 
 def cfg5_config(n_total, ctx, n_local, world, bs, cfg, per):
-    return {"workload": "cfg5: sequence-sharded long-context decode, Llama-3.2-1B "
-                        "(16 layers, random init), 256 sequences x 16384-token KV",
+    name = "cfg5" if (n_total, ctx) == (256, 16384) else "decode step"
+    return {"workload": f"{name}: sequence-sharded long-context decode, Llama-3.2-1B "
+                        f"(16 layers, random init), {n_total} sequences x {ctx}-token KV",
             "n_seq_total": n_total, "context": ctx, "n_seq_per_gpu": n_local,
             "parallelism": f"independent sequences over {world} GPU(s)",
             "kv_cache": (f"paged, {bs}-token blocks scattered by a seeded table"
