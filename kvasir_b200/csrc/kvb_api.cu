@@ -340,6 +340,43 @@ static size_t decode_ws_bytes(size_t n_seq, size_t max_len, size_t n_q, size_t n
     return n_seq * n_kv * chunks * group * 66 * sizeof(float);
 }
 
+// How a split-KV decode call runs, from its shape and workspace:
+//   kSingle  one CTA per (sequence, kv head), no workspace (none given, or too small);
+//   kChunks  fixed-size chunks, partials in the workspace, a combine pass;
+//   kFold    the same chunks folded in the kernel through a cluster (small grids).
+enum DecodeMode { kSingle, kChunks, kFold };
+struct DecodePlan {
+    DecodeMode mode;
+    int chunk_keys, max_chunks;
+};
+static DecodePlan decode_plan(size_t n_seq, size_t max_len, size_t n_q, size_t n_kv,
+                              const void* ws, size_t ws_len) {
+    DecodePlan p;
+    int ck = decode_chunk_keys(n_seq, n_kv, max_len);
+    const size_t need = decode_ws_bytes(n_seq, max_len, n_q, n_kv);
+    const bool chunk_ws = need > 0 && ws != nullptr && ws_len >= need && aligned(ws, 16);
+    if (!chunk_ws) {
+        ck = (int)(((max_len + 255) / 256) * 256);  // one chunk: no workspace
+        if (ck == 0) ck = 256;
+    }
+    // chunks are the grid's z extent: at most 65535 (wider chunks need less workspace)
+    if ((max_len + ck - 1) / ck > 65535) ck = (int)(((max_len + 65534) / 65535 + 255) / 256 * 256);
+    p.chunk_keys = ck;
+    p.max_chunks = (int)((max_len + ck - 1) / ck);
+    if (p.max_chunks < 1) p.max_chunks = 1;
+    // Small split grids (every CTA resident at once, at most 8 chunks per sequence):
+    // the chunks of a (sequence, kv head) form a cluster and fold in the kernel, with
+    // no combine pass.  Measured on the one-sequence decode step: the combine launch
+    // and its programmatic boundary cost ~3.6 us per layer.
+    const size_t n_ctas = n_kv * n_seq * (size_t)p.max_chunks;
+    if (chunk_ws && p.max_chunks >= 2 && p.max_chunks <= 8 && n_ctas <= (size_t)num_sms() * 3) {
+        p.mode = kFold;
+        return p;
+    }
+    p.mode = chunk_ws && p.max_chunks > 1 ? kChunks : kSingle;
+    return p;
+}
+
 struct DecodeLaunch {
     const void* q;
     size_t q_row_stride;
@@ -400,28 +437,12 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
     a.vc_w = static_cast<uint16_t*>(const_cast<void*>(L.vc));
     a.cache_seq_stride = (long long)L.seq_stride;
     a.kv_ready = L.kv_ready ? 1 : 0;
-    int ck = decode_chunk_keys(L.n_seq, L.n_kv, L.max_len);
-    const size_t need = decode_ws_bytes(L.n_seq, L.max_len, L.n_q, L.n_kv);
-    if (need == 0 || L.ws == nullptr || L.ws_len < need || !aligned(L.ws, 16)) {
-        ck = (int)(((L.max_len + 255) / 256) * 256);  // one chunk: no workspace
-        if (ck == 0) ck = 256;
-        a.ws = nullptr;
-    } else {
-        a.ws = static_cast<float*>(L.ws);
-    }
-    // chunks are the grid's z extent: at most 65535 (wider chunks need less workspace)
-    if ((L.max_len + ck - 1) / ck > 65535) ck = (int)(((L.max_len + 65534) / 65535 + 255) / 256 * 256);
-    a.chunk_keys = ck;
-    a.max_chunks = (int)((L.max_len + ck - 1) / ck);
-    if (a.max_chunks < 1) a.max_chunks = 1;
+    const DecodePlan plan = decode_plan(L.n_seq, L.max_len, L.n_q, L.n_kv, L.ws, L.ws_len);
+    a.ws = plan.mode == kSingle ? nullptr : static_cast<float*>(L.ws);
+    a.chunk_keys = plan.chunk_keys;
+    a.max_chunks = plan.max_chunks;
+    a.fold = plan.mode == kFold ? 1 : 0;
 
-    // Small split grids (every CTA resident at once, at most 8 chunks per sequence):
-    // the chunks of a (sequence, kv head) form a cluster and fold in the kernel, with
-    // no combine pass.  Measured on the one-sequence decode step: the combine launch
-    // and its programmatic boundary cost ~3.6 us per layer.
-    const size_t n_ctas = L.n_kv * L.n_seq * (size_t)a.max_chunks;
-    a.fold = (a.ws != nullptr && a.max_chunks >= 2 && a.max_chunks <= 8 &&
-              n_ctas <= (size_t)num_sms() * 3) ? 1 : 0;
     cudaLaunchConfig_t dcfg = {};
     dcfg.gridDim = a.fold ? dim3((unsigned)a.max_chunks, (unsigned)L.n_kv, (unsigned)L.n_seq)
                           : dim3((unsigned)L.n_kv, (unsigned)L.n_seq, (unsigned)a.max_chunks);
@@ -453,7 +474,7 @@ static int launch_decode_mma(kvb_stream_t stream, const DecodeLaunch& L) {
     }
 #undef KVB_DECODE_LAUNCH
     KVB_CHECK_LAUNCH("attention decode launch");
-    if (a.max_chunks > 1 && !a.fold) {
+    if (plan.mode == kChunks) {
         // programmatic dependent launch: set-up overlaps the decode kernel's tail
         const int per_bytes = a.group * 66 * 4;
         const int cap = kCombineSmemBytes / per_bytes;
@@ -1946,6 +1967,12 @@ int rope_attention_decode_paged_in_step(kvb_stream_t stream, const void* qkv, si
                                             v_pool, pool_len, block_table, max_blocks, block_size,
                                             lens, n_seq, max_len, n_q, n_kv, head_dim, scale, out,
                                             out_row_stride, workspace, workspace_len, dtype, true);
+}
+
+int decode_combine_launches(size_t n_seq, size_t max_len, size_t n_q, size_t n_kv,
+                            size_t head_dim, const void* workspace, size_t workspace_len) {
+    if (head_dim != 64 || n_kv == 0 || n_q % n_kv != 0 || n_q / n_kv > 16 || n_seq == 0) return 0;
+    return decode_plan(n_seq, max_len, n_q, n_kv, workspace, workspace_len).mode == kChunks ? 1 : 0;
 }
 
 }  // namespace kvb

@@ -182,7 +182,8 @@ static int record_step(kvb_decoder_s* d, kvb_stream_t s) {
                      d->at(L.attn), qd, d->at(L.attn_ws), L.attn_ws_len, dt),
                  false);
         }
-        if (L.attn_ws_len > 0) ++own;  // the split-KV combine pass
+        own += kvb::decode_combine_launches(B, max_seq, nq, nkv, hd, d->at(L.attn_ws),
+                                            L.attn_ws_len);  // the split-KV combine pass
         st = proj(d->at(L.attn), qd, d->w_o[l], d->at(L.o), H);
         if (st != KVB_OK) return st;
         STEP(kvb_add_rmsnorm(s, d->at(L.x), B * H, d->at(L.o), B * H, d->mlp_norm[l], H, d->at(L.h),

@@ -64,6 +64,11 @@ int rope_attention_decode_paged_in_step(kvb_stream_t stream, const void* qkv, si
                                         float scale, void* out, size_t out_row_stride,
                                         void* workspace, size_t workspace_len, int dtype);
 
+// Launches of a split-KV combine pass (0 or 1) that a split-KV decode call of this
+// shape and workspace makes after its decode kernel (head_dim 64, aligned buffers).
+int decode_combine_launches(size_t n_seq, size_t max_len, size_t n_q, size_t n_kv,
+                            size_t head_dim, const void* workspace, size_t workspace_len);
+
 }  // namespace kvb
 
 #define KVB_CHECK(cond, ...)                                         \
