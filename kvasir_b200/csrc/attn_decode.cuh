@@ -8,7 +8,9 @@
 //
 // Data path per warp, per 64-key tile:
 //   TMA (cp.async.bulk.tensor, 128-byte swizzle, no multicast) brings the K
-//   and V tiles (8 KB each) into shared memory and completes an mbarrier;
+//   and V tiles (8 KB each) into shared memory, each completing its own
+//   mbarrier, so that the next K tile loads while this tile's softmax and
+//   P V run, and the next V tile once P V has read this one;
 //   S = Q K^T runs on the tensor cores as m16n8k16 MMAs with the group's
 //   query heads as the 16 rows (padded), K fragments via ldmatrix;
 //   an online softmax in f32 (exp2, running max / sum) turns S into P;
@@ -133,29 +135,41 @@ __device__ __forceinline__ void decode_chunk(const CUtensorMap& kmap, const CUte
     const bool appends = kRope && rope_p >= 0 && chunk == n_chunks - 1;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kDecWarps; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 2 * kDecWarps; ++i) mbar_init(&bars[i], 1);
         fence_mbar_init();
     }
     __syncthreads();
 
     uint8_t* ktile = smem + warp * 2 * kDecTileBytes;
     uint8_t* vtile = ktile + kDecTileBytes;
+    uint64_t* bar_k = &bars[warp];              // this warp's K tile
+    uint64_t* bar_v = &bars[kDecWarps + warp];  // and its V tile, completed separately
     const int row_base = (int)((long long)b * a.seq_rows + (long long)kvh * a.max_seq);
     // paged: lane 0 reads the block of its next tile while the current one loads
     int blk_next = lane == 0 ? decode_block_of(a, b, key_begin + warp * kDecTileKeys) : 0;
-    auto issue = [&](int kt0) {  // lane 0: the K and V tiles of keys kt0 .. kt0 + 63
+    auto tile_row = [&](int kt0) {  // lane 0: cache row of keys kt0 .. kt0 + 63
         const int row = decode_tile_row(a, b, kvh, row_base, kt0, blk_next);
-        mbar_expect_tx(&bars[warp], 2 * kDecTileBytes);
-        tma_load_2d(ktile, &kmap, &bars[warp], 0, row);
-        tma_load_2d(vtile, &vmap, &bars[warp], 0, row);
         const int kn = kt0 + kDecWarps * kDecTileKeys;
         if (kn < key_end) blk_next = decode_block_of(a, b, kn);
+        return row;
+    };
+    auto issue_k = [&](int row) {
+        mbar_expect_tx(bar_k, kDecTileBytes);
+        tma_load_2d(ktile, &kmap, bar_k, 0, row);
+    };
+    auto issue_v = [&](int row) {
+        mbar_expect_tx(bar_v, kDecTileBytes);
+        tma_load_2d(vtile, &vmap, bar_v, 0, row);
     };
     // The first tile's copy is in flight while q is loaded (and the new row written):
     // only the tile that holds the new key waits for that write.
     const int kt_first = key_begin + warp * kDecTileKeys;
     const bool early = kt_first < key_end && !(appends && rope_p < kt_first + kDecTileKeys);
-    if (early && lane == 0) issue(kt_first);
+    if (early && lane == 0) {
+        const int row = tile_row(kt_first);
+        issue_k(row);
+        issue_v(row);
+    }
     if (a.kv_ready) asm volatile("griddepcontrol.wait;" ::: "memory");  // q, the new row
 
     if (appends) {
@@ -227,20 +241,30 @@ __device__ __forceinline__ void decode_chunk(const CUtensorMap& kmap, const CUte
 #pragma unroll
     for (int j = 0; j < 8; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    uint32_t phase = 0;
+    // One K and one V copy per warp at a time, each on its own barrier: the next
+    // tile's K is requested as soon as S = Q K^T has read this one (its load runs
+    // under the softmax and P V), its V once P V has read this V.  k_out / v_out:
+    // a copy is outstanding (warp-uniform; lane 0 issues).
+    uint32_t phase_k = 0, phase_v = 0;
+    bool k_out = early, v_out = early;
+    int row_next = 0;  // lane 0: row of the tile whose V is requested after P V
     bool ok = true;
 
-    for (int kt0 = kt_first; kt0 < key_end && ok; kt0 += kDecWarps * kDecTileKeys) {
+    for (int kt0 = kt_first; kt0 < key_end; kt0 += kDecWarps * kDecTileKeys) {
         const int nk = min(kDecTileKeys, key_end - kt0);
-        if (lane == 0 && !(early && kt0 == kt_first)) issue(kt0);
-        ok = mbar_wait(&bars[warp], phase);
-        phase ^= 1;
-        if (!ok) break;
-        if (nk < kDecTileKeys) {  // rows past the sequence end: zero V so that 0 * garbage stays 0
-            uint4* vz = reinterpret_cast<uint4*>(vtile);
-            for (int i = nk * 8 + lane; i < kDecTileKeys * 8; i += 32) vz[i] = make_uint4(0, 0, 0, 0);
-            __syncwarp();
+        const int kt_next = kt0 + kDecWarps * kDecTileKeys;
+        if (!k_out) {  // the first tile, when it waited for the new key's row
+            if (lane == 0) {
+                const int row = tile_row(kt0);
+                issue_k(row);
+                issue_v(row);
+            }
+            k_out = v_out = true;
         }
+        ok = mbar_wait(bar_k, phase_k);
+        if (!ok) break;
+        phase_k ^= 1;
+        k_out = false;
 
         // ---- S = Q K^T : 16 x 64 per warp
         float s[8][4];
@@ -256,6 +280,15 @@ __device__ __forceinline__ void decode_chunk(const CUtensorMap& kmap, const CUte
                 mma_16816<T>(s[j], qa[2 * hf], b0, b1);
                 mma_16816<T>(s[j], qa[2 * hf + 1], b2, b3);
             }
+        }
+        __syncwarp();
+        fence_async_smem();  // generic-proxy reads of the K tile precede the next TMA write
+        if (kt_next < key_end) {
+            if (lane == 0) {
+                row_next = tile_row(kt_next);
+                issue_k(row_next);
+            }
+            k_out = true;
         }
         // ---- online softmax (log2 domain); rows g (e = 0,1) and g + 8 (e = 2,3)
         float mx0 = -INFINITY, mx1 = -INFINITY;
@@ -300,6 +333,15 @@ __device__ __forceinline__ void decode_chunk(const CUtensorMap& kmap, const CUte
             o[j][2] *= al1;
             o[j][3] *= al1;
         }
+        ok = mbar_wait(bar_v, phase_v);
+        if (!ok) break;
+        phase_v ^= 1;
+        v_out = false;
+        if (nk < kDecTileKeys) {  // rows past the sequence end: zero V so that 0 * garbage stays 0
+            uint4* vz = reinterpret_cast<uint4*>(vtile);
+            for (int i = nk * 8 + lane; i < kDecTileKeys * 8; i += 32) vz[i] = make_uint4(0, 0, 0, 0);
+            __syncwarp();
+        }
         // ---- O += P V : P from registers, V^T fragments via ldmatrix.trans.
         // P is split into a 16-bit head and a 16-bit remainder (P = hi + lo)
         // and both are multiplied: a single 16-bit P would carry a 2^-9
@@ -324,13 +366,18 @@ __device__ __forceinline__ void decode_chunk(const CUtensorMap& kmap, const CUte
             }
         }
         __syncwarp();
-        fence_async_smem();  // generic-proxy reads of this buffer precede the next TMA write
+        fence_async_smem();  // generic-proxy reads of the V tile precede the next TMA write
+        if (kt_next < key_end) {
+            if (lane == 0) issue_v(row_next);
+            v_out = true;
+        }
     }
     if (!ok) {
         // A copy did not complete in time (the error word is set): wait once
-        // more, bounded, so that no copy lands in shared memory after the CTA
-        // exits, and contribute an empty state to the merge.
-        mbar_wait(&bars[warp], phase ^ 1);
+        // more, bounded, for each copy still outstanding, so that none lands in
+        // shared memory after the CTA exits, and contribute an empty state.
+        if (k_out) mbar_wait(bar_k, phase_k);
+        if (v_out) mbar_wait(bar_v, phase_v);
         m0 = m1 = -INFINITY;
         l0 = l1 = 0.f;
 #pragma unroll
@@ -408,7 +455,7 @@ __global__ void __launch_bounds__(128, 3) attn_decode_kernel(const __grid_consta
                                                              const __grid_constant__ CUtensorMap vmap,
                                                              DecodeArgs a) {
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t bars[kDecWarps];
+    __shared__ uint64_t bars[2 * kDecWarps];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~uintptr_t(1023));
     asm volatile("griddepcontrol.launch_dependents;");
